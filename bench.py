@@ -1,0 +1,389 @@
+#!/usr/bin/env python
+"""Benchmark of the index-resident multi-adapter LoRA forward on B200.
+
+Workload ``flux_sweep_b14`` (the per-linear sweep of the benchmark spec, config 2): the four
+FLUX.1-dev linear shapes 3072->3072, 3072->12288, 12288->3072, 15360->3072 at rank 16; B=14
+samples of 4096 image + 512 text tokens (M=4608); every sample routed to its own adapter, 14
+distinct slots drawn from a resident 10,000-slot bank of seeded uniform 9-bit packed indices.
+One step = the fused decode+SGMV of all four linears, each accumulating its per-sample LoRA
+delta in place into that linear's bf16 base output (4 kernel launches).  Inputs are larger
+than L2 (>= 396 MB of activations per launch), so no flush is needed between launches.
+
+Metric: tokens/s = (4 linears x B x M tokens x N ranks) / max-over-ranks step time.  Multi-GPU
+is weak scaling: every rank runs its own B=14 batch against its own replica of the bank; the
+only collectives are the timing barrier and the max over ranks.
+
+``--impl reference`` times the reference's CPU path (the oracle's restatement of
+lithe/serve.py MultiAdapterLinear in torch CPU ops, all host threads) on a bounded sample of
+the same workload and prints the same JSON line with "impl": "reference".
+"""
+from __future__ import annotations
+
+import argparse
+import datetime
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+if str(ROOT) not in sys.path:
+    sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+SHAPES = [(3072, 3072), (3072, 12288), (12288, 3072), (15360, 3072)]
+BATCH, TOKENS, RANK, LEVELS = 14, 4096 + 512, 16, 3
+BANK_SLOTS = 10_000
+METRIC = "SGMV tokens/s at B=14 FLUX shapes"
+FALLBACK_HBM_GBS = 6650.0
+CPU_SAMPLE_TOKENS = 256
+
+
+def algorithmic_bytes(d_in: int, d_out: int, b: int = BATCH, m: int = TOKENS, distinct: int = BATCH,
+                      accumulate: bool = True) -> float:
+    """x read + out read and write (in-place accumulate) + the packed indices of the adapters used."""
+    ids = distinct * LEVELS * RANK * (d_in + d_out) / 64 * 8 / 7
+    return b * m * d_in * 2 + (2 if accumulate else 1) * b * m * d_out * 2 + ids
+
+
+def flops(d_in: int, d_out: int, b: int = BATCH, m: int = TOKENS) -> float:
+    return 2.0 * b * m * RANK * (d_in + d_out)
+
+
+def modules():
+    return [{"name": f"lin{i}_{a}x{b}", "shape_a": [RANK, a], "shape_b": [b, RANK]} for i, (a, b) in enumerate(SHAPES)]
+
+
+# --------------------------------------------------------------------------------------- ranks
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return world, rank, local
+
+
+def init_dist(world: int, local: int):
+    torch.cuda.set_device(local)
+    if world > 1:
+        import torch.distributed as dist
+        os.environ.setdefault("MASTER_ADDR", "127.0.0.1")
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=600),
+                                device_id=torch.device("cuda", local))
+
+
+def barrier(world: int):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(value: float, world: int) -> float:
+    if world == 1:
+        return value
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# --------------------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi samples of this GPU's clocks and throttle reasons during the timed region."""
+
+    FIELDS = ("clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,clocks_event_reasons.hw_slowdown,"
+              "clocks_event_reasons.hw_thermal_slowdown,clocks_event_reasons.sw_thermal_slowdown,"
+              "clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, device: int):
+        self.proc = None
+        self.path = None
+        try:
+            uuid = str(torch.cuda.get_device_properties(device).uuid)
+            self.gpu = uuid if uuid.startswith("GPU-") else f"GPU-{uuid}"
+        except Exception:  # pragma: no cover - depends on the torch build
+            self.gpu = str(device)
+
+    def __enter__(self):
+        fd, self.path = tempfile.mkstemp(suffix=".csv")
+        os.close(fd)
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", self.gpu, f"--query-gpu={self.FIELDS}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=open(self.path, "w"), stderr=subprocess.DEVNULL)
+        except OSError:
+            self.proc = None
+        time.sleep(0.3)
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self):
+        rows = []
+        if self.path and os.path.exists(self.path):
+            for line in open(self.path):
+                parts = [p.strip() for p in line.split(",")]
+                if len(parts) >= 8:
+                    rows.append(parts)
+            os.unlink(self.path)
+        if not rows:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unsampled"], "samples": 0}
+
+        def num(s):
+            try:
+                return float(s)
+            except ValueError:
+                return None
+        sm = [num(r[0]) for r in rows if num(r[0]) is not None]
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][1]),
+                "power_w_max": max((num(r[2]) or 0.0) for r in rows), "reasons": reasons, "samples": len(rows)}
+
+
+def measured_peaks():
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return float(d["hbm_gbs"]), "measured"
+    return FALLBACK_HBM_GBS, "fallback"
+
+
+def traffic_per_launch():
+    """dram bytes per launch per shape from the committed ncu summary (None if not captured)."""
+    p = ROOT / "profiles" / "sgmv_index_flux_b14_traffic.json"
+    if not p.exists():
+        return None
+    return json.loads(p.read_text()).get("dram_bytes_per_launch")
+
+
+# --------------------------------------------------------------------------------------- CPU arm
+def cpu_reference_rate(seconds: float, seed: int = 0):
+    """Tokens/s of the oracle port of serve.py's forward (LoRA path: decode + bmm + add) on the
+    host cores, over a bounded sample: 1 sample x CPU_SAMPLE_TOKENS tokens of every shape, fp32."""
+    from oracle import codebook_ref, sgmv_ref
+    threads = os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    pa, pb = codebook_ref.twin_pools()
+    rng = np.random.default_rng(seed)
+    cases = []
+    for d_in, d_out in SHAPES:
+        bank_a = rng.integers(0, 512, (1, LEVELS, RANK * d_in // 64))
+        bank_b = rng.integers(0, 512, (1, LEVELS, d_out * RANK // 64))
+        x = torch.randn(1, CPU_SAMPLE_TOKENS, d_in, generator=torch.Generator().manual_seed(seed))
+        base = torch.randn(1, CPU_SAMPLE_TOKENS, d_out, generator=torch.Generator().manual_seed(seed + 1))
+        cases.append((x, base, bank_a, bank_b, d_out))
+    ids, w = sgmv_ref.routes_to_tables([[(0, 1.0)]])
+
+    def one_pass():
+        for x, base, ba, bb, d_out in cases:
+            sgmv_ref.serve_forward(base, x, ba, bb, [1.0], ids, w, RANK, d_out, pa, pb)
+
+    one_pass()                                   # warm-up
+    passes, t0 = 0, time.perf_counter()
+    while True:
+        one_pass()
+        passes += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    tokens = passes * len(SHAPES) * CPU_SAMPLE_TOKENS
+    return tokens / el, threads, passes, el
+
+
+def run_reference(args):
+    world, rank, _ = dist_env()
+    if rank != 0:
+        return
+    seconds_per_step = max(0.5, min(10.0, 60.0 / max(1, args.steps + args.warmup)))
+    for _ in range(args.warmup):
+        cpu_reference_rate(seconds_per_step / 4)
+    rates = []
+    for _ in range(args.steps):
+        rate, threads, passes, el = cpu_reference_rate(seconds_per_step)
+        rates.append(rate)
+    value = statistics.median(rates)
+    sample = (f"1 sample x {CPU_SAMPLE_TOKENS} tokens of each of the 4 shapes per pass, fp32, "
+              f"~{seconds_per_step:.1f} s of passes per step")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * len(SHAPES) * CPU_SAMPLE_TOKENS / value,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic: seeded uniform 9-bit indices, x ~ N(0,1)",
+        "config": {"workload": "flux_sweep_b14", "shapes": SHAPES, "batch": BATCH, "tokens_per_sample": TOKENS,
+                   "rank": RANK, "path": "oracle port of lithe/serve.py MultiAdapterLinear (torch CPU)"},
+        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+        "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# --------------------------------------------------------------------------------------- GPU arm
+def run_lithe(args):
+    from lithe_b200 import device_errors
+    from lithe_b200.kernels import PackedBank, PackedLayout, packed_codebook_lora_delta_
+
+    world, rank, local = dist_env()
+    init_dist(world, local)
+    dev = torch.device("cuda", local)
+    layout = PackedLayout.from_modules(modules())
+    bank = PackedBank(layout, BANK_SLOTS, dev)
+    bank.fill_random(seed=1234)                                  # replicated: identical on every rank
+    slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100 + rank))[:BATCH]
+    ids = slots.to(torch.int32).to(dev)
+    g = torch.Generator(device=dev)
+    g.manual_seed(10 + rank)
+    xs = [torch.randn(BATCH, TOKENS, a, generator=g, device=dev, dtype=torch.bfloat16) for a, _ in SHAPES]
+    outs = [(torch.randn(BATCH, TOKENS, b, generator=g, device=dev, dtype=torch.bfloat16) * 0.05) for _, b in SHAPES]
+    names = layout.names
+    stream = torch.cuda.current_stream(dev)
+
+    def step(evs=None):
+        for i in range(len(SHAPES)):
+            if evs is not None:
+                evs[i][0].record(stream)
+            packed_codebook_lora_delta_(outs[i], xs[i], bank, names[i], ids, scaling=1.0)
+            if evs is not None:
+                evs[i][1].record(stream)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize(dev)
+    if device_errors(dev):
+        raise RuntimeError("kernel reported a device error during warm-up")
+
+    # ---- device-timed region: K steps, per-launch events on the launching stream
+    evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+            for _ in SHAPES] for _ in range(args.steps)]
+    t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        t_start.record(stream)
+        for k in range(args.steps):
+            step(evs[k])
+        t_end.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    total_ms = t_start.elapsed_time(t_end)
+    total_ms = max_over_ranks(total_ms, world)
+    ms_per_step = total_ms / args.steps
+    per_shape_ms = [statistics.mean(evs[k][i][0].elapsed_time(evs[k][i][1]) for k in range(args.steps))
+                    for i in range(len(SHAPES))]
+    launches = args.steps * len(SHAPES)
+    tokens_per_step = len(SHAPES) * BATCH * TOKENS * world
+    value = tokens_per_step / (ms_per_step / 1000.0)
+
+    # ---- end-to-end through the public API with host buffers (pinned), copies timed
+    max_in = max(a for a, _ in SHAPES)
+    max_out = max(b for _, b in SHAPES)
+    x_host = torch.empty(BATCH * TOKENS * max_in, dtype=torch.bfloat16, pin_memory=True)
+    o_host = torch.empty(BATCH * TOKENS * max_out, dtype=torch.bfloat16, pin_memory=True)
+    x_host.normal_()
+    o_host.normal_().mul_(0.05)
+    h2d = sum(BATCH * TOKENS * (a + b) * 2 for a, b in SHAPES)
+    d2h = sum(BATCH * TOKENS * b * 2 for _, b in SHAPES)
+
+    def e2e_step():
+        for i, (a, b) in enumerate(SHAPES):
+            xs[i].copy_(x_host[: BATCH * TOKENS * a].view(BATCH, TOKENS, a), non_blocking=True)
+            outs[i].copy_(o_host[: BATCH * TOKENS * b].view(BATCH, TOKENS, b), non_blocking=True)
+            packed_codebook_lora_delta_(outs[i], xs[i], bank, names[i], ids, scaling=1.0)
+            o_host[: BATCH * TOKENS * b].view(BATCH, TOKENS, b).copy_(outs[i], non_blocking=True)
+
+    e2e_steps = max(1, min(args.steps, 5))
+    e2e_step()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+    errors = device_errors(dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, threads, passes, el = cpu_reference_rate(args.cpu_seconds)
+        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
+               "sample": f"oracle port of serve.py forward, fp32, 1 sample x {CPU_SAMPLE_TOKENS} tokens of each "
+                         f"of the 4 shapes, {passes} passes in {el:.1f} s"}
+
+    peak, peak_kind = measured_peaks()
+    alg = [algorithmic_bytes(a, b) for a, b in SHAPES]
+    achieved = sum(alg) / (sum(per_shape_ms) / 1000.0) / 1e9
+    traffic = traffic_per_launch()
+    shapes_out = []
+    for i, (a, b) in enumerate(SHAPES):
+        key = f"{a}x{b}"
+        gbs = alg[i] / (per_shape_ms[i] / 1000.0) / 1e9
+        shapes_out.append({"shape": key, "ms": per_shape_ms[i], "tokens_per_s": BATCH * TOKENS / (per_shape_ms[i] / 1e3),
+                           "algorithmic_bytes": alg[i], "achieved_gbs": gbs, "frac_of_peak": gbs / peak,
+                           "tflops": flops(a, b) / (per_shape_ms[i] / 1e3) / 1e12,
+                           "dram_bytes": None if traffic is None else traffic.get(key)})
+    mean_traffic = None
+    if traffic is not None and all(s["dram_bytes"] is not None for s in shapes_out):
+        mean_traffic = sum(s["dram_bytes"] for s in shapes_out) / len(shapes_out)
+
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: seeded uniform 9-bit packed indices (10,000-slot bank), x ~ N(0,1) bf16",
+            "config": {"workload": "flux_sweep_b14", "shapes": [f"{a}->{b}" for a, b in SHAPES], "batch": BATCH,
+                       "tokens_per_sample": TOKENS, "rank": RANK, "bank_slots": BANK_SLOTS,
+                       "distinct_adapters": BATCH, "parallelism": f"sample-sharded dp{world}, bank replicated",
+                       "l2": "inputs larger than L2 (>= 396 MB of activations per launch), no flush"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"hbm_gbs of {peak_kind}", "traffic": mean_traffic,
+                         "algorithmic_bytes_per_launch": sum(alg) / len(alg),
+                         "kernel": "lithe::sgmv_index_kernel<16>"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": len(SHAPES) * BATCH * TOKENS * world / (e2e_ms / 1000.0), "unit": "tokens/s",
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                    "api": "lithe_b200.kernels.packed_codebook_lora_delta_ (C ABI lithe_sgmv_index), pinned host buffers"},
+            "clocks": clocks.summary(),
+            "gpu_launches": launches,
+            "per_shape": shapes_out,
+            "device_errors": errors,
+        }
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["lithe", "reference"], default="lithe")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "lithe":
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_lithe(args)
+
+
+if __name__ == "__main__":
+    main()

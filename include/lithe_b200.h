@@ -1,0 +1,141 @@
+/*
+ * lithe_b200.h -- C ABI of the B200 (sm_100a) index-resident multi-adapter LoRA path.
+ *
+ * Every pointer named "device" is a CUDA device pointer on the current device; every
+ * "stream" is a cudaStream_t passed as void*.  No entry point allocates device memory,
+ * synchronises the host or keeps a pointer after it returns: the caller owns all buffers
+ * and the work is ordered on the given stream only.  Return value: LITHE_OK (0) or a
+ * negative LITHE_ERR_* code; lithe_last_error() gives a message for the calling thread.
+ *
+ * Data formats (identical to the reference implementation, JianJiang1995/LITHE):
+ *   - codebook: 512 codewords of 64 values, c_k[t] = (2*popc((k ^ P(t)) & 511) - 9) / 3
+ *     with P(t) bit q = parity(t & q), q < 9 (lithe/codebook.py:35-69).  A level-l pool of
+ *     side A/B is sigma_l * c_k, so each pool level holds exactly 10 distinct fp32 values
+ *     lut[side][l][n] = pool[l][k][t] for n = popc((k ^ P(t)) & 511).  The entry points
+ *     take those 10 values per (side, level) instead of the (L,512,64) pools.
+ *   - packed index stream (lithe/kernels/packed.py:1-17,38-52): one adapter's indices in
+ *     (block, level)-major order, 7 nine-bit indices per little-endian uint64 word; index p
+ *     lives in word p/7, bits [9*(p%7), 9*(p%7)+9).  Per module the A blocks come first,
+ *     then the B blocks (packed.py:125-133).
+ *   - level-major integer banks (lithe/serve.py:58-67, lithe/kernels/layers.py:105-106):
+ *     (n_slots, L, n_blocks) int16 or int32.
+ */
+#ifndef LITHE_B200_H
+#define LITHE_B200_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define LITHE_API __attribute__((visibility("default")))
+#else
+#define LITHE_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define LITHE_OK 0
+#define LITHE_ERR_ARG (-1)          /* invalid argument (shape, pointer, alignment)      */
+#define LITHE_ERR_UNSUPPORTED (-2)  /* valid but not handled by this build (e.g. rank)   */
+#define LITHE_ERR_CUDA (-3)         /* a CUDA runtime / driver call failed               */
+
+/* bits of the device-side error word (int32) that kernels may OR in */
+#define LITHE_DEVERR_SLOT 1         /* a sample referenced a slot >= n_slots             */
+#define LITHE_DEVERR_INDEX 2        /* an int16/int32 bank held an index outside [0,512) */
+#define LITHE_DEVERR_TIMEOUT 4      /* a pipeline wait ran past its time limit           */
+
+#define LITHE_IDX_PACKED9 0         /* uint64 words, 7 x 9-bit, (block, level)-major     */
+#define LITHE_IDX_I16 1             /* int16, level-major (slot, level, block)           */
+#define LITHE_IDX_I32 2             /* int32, level-major (slot, level, block)           */
+
+#define LITHE_DTYPE_BF16 0
+#define LITHE_DTYPE_F32 1
+
+#define LITHE_MAX_LEVELS 4
+
+/* Where one side (A or B) of one module sits in a resident index bank.
+ *   format LITHE_IDX_PACKED9: base = uint64 words of slot 0; slot s starts at
+ *     base + s*slot_stride words; block j of this side has its level-l index at stream
+ *     position offset + num_levels*j + l  (offset = num_levels * block offset of the side,
+ *     i.e. 3*a_off / 3*b_off of PackedLayout, lithe/kernels/packed.py:100-117).
+ *   format LITHE_IDX_I16 / LITHE_IDX_I32: element (s, l, j) is at
+ *     base[s*slot_stride + offset + l*level_stride + j]. */
+typedef struct lithe_index_view {
+    const void* base;          /* device */
+    int32_t format;            /* LITHE_IDX_* */
+    int32_t num_levels;        /* L, 1..LITHE_MAX_LEVELS */
+    int64_t slot_stride;       /* elements (words for PACKED9) between consecutive slots */
+    int64_t offset;            /* see above */
+    int64_t level_stride;      /* level-major formats only */
+} lithe_index_view;
+
+/* ABI version of this header; lithe_abi_version() returns the library's. */
+#define LITHE_ABI_VERSION 1
+LITHE_API int32_t lithe_abi_version(void);
+
+/* Message for the last non-zero return on the calling thread ("" if none). */
+LITHE_API const char* lithe_last_error(void);
+
+/*
+ * Fused index-resident per-sample LoRA forward for one linear (replaces the two Triton
+ * launches of shared_codebook_lora_delta, lithe/kernels/shared.py:197-263, plus the
+ * caller's "out + delta" pass, lithe/kernels/layers.py:131 and lithe/serve.py:97).
+ *
+ * For every sample b in [0, batch) with slot j = ids[b] (0 <= j < n_slots):
+ *     A_j = decode(idx_a, j) reshaped (rank, d_in);  B_j = decode(idx_b, j) reshaped (d_out, rank)
+ *     h   = bf16( w_b * scaling * (x[b] @ A_j^T) )             (fp32 accumulation)
+ *     accumulate != 0:  out[b] = bf16( out[b] + h @ B_j^T )    (in place, fp32 add)
+ *     accumulate == 0:  out[b] = bf16( h @ B_j^T )
+ * where decode sums lut values over levels 0..L-1 in fp32 (lithe/quant.py:74-81) and
+ * rounds to bf16 (the reference casts the decoded factors to the activation dtype,
+ * lithe/serve.py:96).  w_b = weights[b] (weights may be NULL: w_b = 1).
+ * ids[b] < 0: no adapter (out[b] untouched when accumulating, zero otherwise).
+ * ids[b] >= n_slots: same as < 0 and LITHE_DEVERR_SLOT is OR-ed into *err_flag.
+ *
+ *   x    device bf16 (batch, m, d_in) contiguous;  out device bf16 (batch, m, d_out)
+ *   ids  device int32 (batch);  weights device fp32 (batch) or NULL
+ *   lut  HOST fp32 [2][num_levels][10]: side A levels then side B levels
+ *   err_flag device int32 (may be NULL)
+ * Requirements: rank in {1,2,4,8,16}; d_in % 64 == 0; d_out % 8 == 0; (d_out*rank) % 64 == 0;
+ * x, out 16-byte aligned; idx_a and idx_b with the same num_levels.
+ */
+LITHE_API int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate,
+                         const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                         int64_t n_slots, const int32_t* ids, const float* weights,
+                         int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank,
+                         const float* lut, float scaling, int32_t* err_flag, void* stream);
+
+/*
+ * Whole-adapter decode of a packed stream into dense 64-value blocks (replaces
+ * _decode_packed_kernel / decode_packed, lithe/kernels/packed.py:151-177,205-222).
+ *   words   device uint64, the packed (block, level)-major stream of one adapter
+ *   n_blocks number of 64-value blocks (PackedLayout.total_blocks)
+ *   sides   device int8 (n_blocks): 0 = A block, 1 = B block (NULL: all side A)
+ *   lut     HOST fp32 [2][num_levels][10]
+ *   out     device (n_blocks, 64) of out_dtype (LITHE_DTYPE_BF16 or LITHE_DTYPE_F32)
+ * The fp32 output equals lithe.quant.rvq_decode_blocks bit for bit; the bf16 output is
+ * that value rounded to nearest even.
+ */
+LITHE_API int32_t lithe_decode_packed(const uint64_t* words, int64_t n_blocks, int32_t num_levels,
+                            const int8_t* sides, const float* lut, void* out,
+                            int32_t out_dtype, void* stream);
+
+/*
+ * Batched decode of n_sel slots of a resident packed bank in one launch (the hot-swap /
+ * decode-throughput path, serving/_common.py:241-244 run once per slot in the reference).
+ *   bank      device uint64, slot s at bank + s*slot_stride words
+ *   slot_ids  device int32 (n_sel): slots to decode (ids outside [0, n_slots) set
+ *             LITHE_DEVERR_SLOT in *err_flag and leave their output rows untouched)
+ *   out       device (n_sel, n_blocks, 64) of out_dtype
+ */
+LITHE_API int32_t lithe_decode_packed_batch(const uint64_t* bank, int64_t slot_stride, int64_t n_slots,
+                                  const int32_t* slot_ids, int32_t n_sel, int64_t n_blocks,
+                                  int32_t num_levels, const int8_t* sides, const float* lut,
+                                  void* out, int32_t out_dtype, int32_t* err_flag, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* LITHE_B200_H */

@@ -1,0 +1,229 @@
+// Device helpers shared by the LITHE sm_100a kernels: inline-PTX wrappers for mbarrier,
+// TMA (cp.async.bulk.tensor) and warp MMA, plus the procedural twin-Hadamard decode.
+#pragma once
+
+#include <cstdint>
+#include <cuda_bf16.h>
+#include <cuda.h>
+
+#include "lithe_b200.h"
+
+namespace lithe {
+
+// ---------------------------------------------------------------------------------------
+// Codebook: c_k[t] = (2*popc((k ^ P(t)) & 511) - 9) / 3, P(t) bit q = parity(t & q), q < 9
+// (lithe/codebook.py:35-69).  q < 9 only touches bits 0..3 of t, so c_k has period 16 in t,
+// and P is linear over GF(2): P(8h + i) = P(8h) ^ P(i) with P(8) = 256.
+// ---------------------------------------------------------------------------------------
+__host__ __device__ constexpr uint32_t hadamard_pattern(uint32_t t) {
+    uint32_t p = 0;
+    for (uint32_t q = 0; q < 9; ++q) {
+        uint32_t v = t & q, par = 0;
+        while (v) { par ^= (v & 1u); v >>= 1; }
+        p |= par << q;
+    }
+    return p;
+}
+static_assert(hadamard_pattern(1) == 170 && hadamard_pattern(8) == 256 &&
+              hadamard_pattern(15) == 406 && hadamard_pattern(16) == 0,
+              "Sylvester-Hadamard row pattern");
+
+// Decoded values of one 64-value block at the 8 positions u = 8*half + i (i = 0..7)
+// (every t with t & 15 == u has the same value).  lut: [level][16] fp32 in shared memory,
+// k[l]: the block's 9-bit index at level l.  Levels are summed 0,1,..,L-1 in fp32, the
+// order of lithe/quant.py:77-80, so the result is bit-identical to the reference decode.
+template <int kMaxLevels>
+__device__ __forceinline__ void decode_eight(const float* __restrict__ lut, const uint32_t* k,
+                                             int levels, uint32_t half, float v[8]) {
+#pragma unroll
+    for (int l = 0; l < kMaxLevels; ++l) {
+        if (l < levels) {
+            const uint32_t kk = k[l] ^ (half << 8);
+            const float* row = lut + l * 16;
+#pragma unroll
+            for (int i = 0; i < 8; ++i) {
+                const float c = row[__popc(kk ^ hadamard_pattern(i))];
+                v[i] = (l == 0) ? c : v[i] + c;
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t*>(&h);
+}
+
+// fp32 views of the two bf16 halves of a 32-bit word (exact)
+__device__ __forceinline__ float bf16lo_to_f32(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float bf16hi_to_f32(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// ---------------------------------------------------------------------------------------
+// Index bank reads.  PACKED9: stream position p in word p/7 at bit 9*(p%7)
+// (lithe/kernels/packed.py:38-52,171-177).  I16 / I32: level-major (slot, level, block).
+// Out-of-range integers in the I16/I32 banks are masked to 9 bits and reported.
+// ---------------------------------------------------------------------------------------
+struct IndexView {
+    const void* base;
+    int32_t format;
+    int32_t levels;
+    int64_t slot_stride;
+    int64_t offset;
+    int64_t level_stride;
+};
+
+__device__ __forceinline__ uint64_t ldg_nc_u64(const uint64_t* p) {
+    uint64_t v;
+    asm volatile("ld.global.nc.u64 %0, [%1];" : "=l"(v) : "l"(p));
+    return v;
+}
+
+template <int kMaxLevels>
+__device__ __forceinline__ void fetch_indices(const IndexView& v, int64_t slot, int64_t blk,
+                                              uint32_t k[kMaxLevels], int32_t* err) {
+    if (v.format == LITHE_IDX_PACKED9) {
+        const uint64_t* w = static_cast<const uint64_t*>(v.base) + slot * v.slot_stride;
+        const uint64_t p0 = static_cast<uint64_t>(v.offset + static_cast<int64_t>(v.levels) * blk);
+#pragma unroll
+        for (int l = 0; l < kMaxLevels; ++l) {
+            if (l < v.levels) {
+                const uint64_t p = p0 + l;
+                const uint64_t wi = p / 7u;
+                const uint32_t sh = 9u * static_cast<uint32_t>(p - wi * 7u);
+                k[l] = static_cast<uint32_t>(ldg_nc_u64(w + wi) >> sh) & 511u;
+            } else {
+                k[l] = 0;
+            }
+        }
+    } else {
+        bool bad = false;
+#pragma unroll
+        for (int l = 0; l < kMaxLevels; ++l) {
+            if (l < v.levels) {
+                const int64_t e = slot * v.slot_stride + v.offset + l * v.level_stride + blk;
+                int32_t raw;
+                if (v.format == LITHE_IDX_I16) raw = __ldg(static_cast<const int16_t*>(v.base) + e);
+                else raw = __ldg(static_cast<const int32_t*>(v.base) + e);
+                bad |= (raw < 0) | (raw > 511);
+                k[l] = static_cast<uint32_t>(raw) & 511u;
+            } else {
+                k[l] = 0;
+            }
+        }
+        if (bad && err) atomicOr(err, LITHE_DEVERR_INDEX);
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Shared-memory, mbarrier and TMA wrappers (PTX ISA 8.x, sm_90+ forms valid on sm_100a)
+// ---------------------------------------------------------------------------------------
+__device__ __forceinline__ uint32_t smem_u32(const void* p) {
+    return static_cast<uint32_t>(__cvta_generic_to_shared(p));
+}
+
+__device__ __forceinline__ void mbar_init(uint64_t* bar, uint32_t count) {
+    asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t* bar, uint32_t bytes) {
+    asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)),
+                 "r"(bytes)
+                 : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+__device__ __forceinline__ uint64_t global_timer_ns() {
+    uint64_t t;
+    asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));
+    return t;
+}
+
+// Time limit of one pipeline wait.  A wait that runs out sets *abort (shared) and the
+// device error word, and every other wait of the block then returns false as well.
+constexpr uint64_t kWaitLimitNs = 4000000000ull;
+constexpr uint32_t kWaitSpinLimit = 1u << 28;   // second bound, independent of the timer
+
+static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                            int32_t* err) {
+    const uint64_t t0 = global_timer_ns();
+    for (uint32_t it = 0; it < kWaitSpinLimit; ++it) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        if ((it & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) break;
+    }
+    *abort = 1;
+    if (err) atomicOr(err, LITHE_DEVERR_TIMEOUT);
+    return false;
+}
+
+__device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity, volatile int* abort,
+                                          int32_t* err) {
+    if (mbar_try_wait(bar, parity)) return true;
+    return mbar_wait_slow(bar, parity, abort, err);
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, uint64_t* bar,
+                                            int32_t c0, int32_t c1, int32_t c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes"
+        " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+        : "memory");
+}
+
+__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int32_t c0,
+                                             int32_t c1, int32_t c2) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
+            reinterpret_cast<uint64_t>(map)),
+        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
+        : "memory");
+}
+
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+
+template <int N>
+__device__ __forceinline__ void bulk_wait_read() {
+    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
+}
+
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
+__device__ __forceinline__ void fence_proxy_async_smem() {
+    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+__device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {
+    asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(map)) : "memory");
+}
+
+// D = A(16x16 bf16, row) * B(16x8 bf16, col) + C, fp32 accumulate
+__device__ __forceinline__ void mma_bf16_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1,
+                                               const float c[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9},"
+        " {%10,%11,%12,%13};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
+          "f"(c[2]), "f"(c[3]));
+}
+
+}  // namespace lithe

@@ -1,0 +1,500 @@
+// Fused index-resident per-sample LoRA forward (shrink + expand, decode fused in).
+//
+// Replaces the two Triton launches of lithe/kernels/shared.py:36-157 (shrink decodes A
+// tiles and writes y_lo; expand decodes B tiles per M-tile and writes a fresh delta),
+// the separate "delta * scaling" pass (shared.py:261-262) and the caller's "out + delta"
+// pass (lithe/kernels/layers.py:131, lithe/serve.py:97).  One persistent launch per linear:
+//
+//   work unit  = (sample b, 64-token tile); CTA i owns a contiguous range of units.
+//   per unit   = d_in/64 "x chunks" (64x64 bf16 activation tiles, TMA, 128B swizzle)
+//              + d_out/64 "out chunks" (64x64 bf16 output tiles, TMA load + TMA store).
+//   warps      = 4 consumer warps (16 tokens each), 1 TMA producer warp, 2 decoder warps.
+//   pipeline   = kStages shared-memory stages; each stage holds one 8 KB tile and the
+//                512 B decoded factor chunk that goes with it; full barrier = TMA bytes +
+//                one decoder arrival, empty barrier = one arrival per consumer warp.
+//
+// Decoded factors.  The codeword c_k has period 16 (device_common.cuh), so
+//   A_j[r, 64c + t] = a_{r,c}[t & 15]     (16 values per (rank row, 64-column chunk))
+//   B_j[o, r]       = w_G[r_eff]          with 4 consecutive-in-pattern rows identical
+// and a decoded chunk is 16 rows x 16 values (512 B of bf16) for both sides.
+//
+// Shrink (per x chunk, per consumer warp): h[16 x 16] += x[16 x 64] . A_chunk^T with
+// 8 mma.m16n8k16.  The reduction index inside each 32-column window is permuted so that
+// every thread reads its activations as one 16-byte vector per row; the A fragment uses
+// the same permutation (both are a bijection of the window's 32 columns).
+// Expand (per out chunk): the 64 output columns of a chunk are 16 distinct "logical"
+// columns repeated 4 times, so delta = h . B^T is 2 mma.m16n8k16 (n = 16 logical
+// columns, k = 16 ranks) and each thread adds its 2 results to 8 output values per row.
+// The bf16 output tile is read-modified-written in shared memory and stored by TMA.
+#include "device_common.cuh"
+#include "host_common.h"
+
+namespace lithe {
+
+constexpr int kBM = 64;                 // tokens per work unit
+constexpr int kChunk = 64;              // columns per chunk
+constexpr int kConsumerWarps = 4;
+constexpr int kDecodeWarps = 2;
+constexpr int kProducerWarp = kConsumerWarps;
+constexpr int kFirstDecodeWarp = kConsumerWarps + 1;
+constexpr int kThreads = 32 * (kConsumerWarps + 1 + kDecodeWarps);
+constexpr int kStages = 16;
+constexpr int kTileBytes = kBM * kChunk * 2;      // 8192
+constexpr int kFactBytes = 16 * 16 * 2;           // 512
+constexpr int kLutFloats = 2 * LITHE_MAX_LEVELS * 16;
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * (kTileBytes + kFactBytes) +
+                              2 * kStages * sizeof(uint64_t) + kLutFloats * sizeof(float) + 16;
+
+struct SgmvParams {
+    IndexView ia, ib;
+    const int32_t* ids;
+    const float* weights;
+    int32_t* err;
+    int64_t n_slots;
+    int32_t m, d_in, d_out;
+    int32_t n_mtiles, n_xchunks, n_ochunks, total_units;
+    int32_t accumulate;
+    int32_t a_blocks_per_row;   // d_in / 64
+    int32_t b_blocks;           // d_out * rank / 64
+    float scaling;
+    float lut[2][LITHE_MAX_LEVELS][16];
+};
+
+struct Unit {
+    int b, mt;
+    int64_t slot;
+    bool active;
+    int nx, no;
+};
+
+__device__ __forceinline__ Unit unit_at(const SgmvParams& p, int u) {
+    Unit r;
+    r.b = u / p.n_mtiles;
+    r.mt = u - r.b * p.n_mtiles;
+    const int32_t sid = __ldg(p.ids + r.b);
+    r.slot = sid;
+    r.active = sid >= 0 && static_cast<int64_t>(sid) < p.n_slots;
+    r.nx = r.active ? p.n_xchunks : 0;
+    r.no = (r.active || !p.accumulate) ? p.n_ochunks : 0;
+    return r;
+}
+
+__device__ __forceinline__ uint4 lds128(const uint8_t* a) { return *reinterpret_cast<const uint4*>(a); }
+__device__ __forceinline__ void sts128(uint8_t* a, uint4 v) { *reinterpret_cast<uint4*>(a) = v; }
+
+// bf16x2 word + (dlo, dhi) in fp32, rounded to nearest even
+__device__ __forceinline__ uint32_t add_bf16x2(uint32_t w, float dlo, float dhi) {
+    return pack_bf16x2(bf16lo_to_f32(w) + dlo, bf16hi_to_f32(w) + dhi);
+}
+
+// ---------------------------------------------------------------------------------------
+// Decoder warps
+// ---------------------------------------------------------------------------------------
+// A chunk c: rows r = 0..15 (rows >= kRank are zero), values u = 0..15 in natural order.
+// Lane (r = lane/2, half = lane&1) writes bytes [r*32 + half*16, +16).
+template <int kRank>
+__device__ __forceinline__ void decode_a_chunk(const SgmvParams& p, const float* lut_a, int64_t slot, int c,
+                                               uint8_t* fact, int lane) {
+    const int r = lane >> 1;
+    const uint32_t half = lane & 1;
+    uint4 q = make_uint4(0, 0, 0, 0);
+    if (r < kRank) {
+        uint32_t k[LITHE_MAX_LEVELS];
+        fetch_indices<LITHE_MAX_LEVELS>(p.ia, slot, static_cast<int64_t>(r) * p.a_blocks_per_row + c, k, p.err);
+        float v[8];
+        decode_eight<LITHE_MAX_LEVELS>(lut_a, k, p.ia.levels, half, v);
+        q = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                       pack_bf16x2(v[6], v[7]));
+    }
+    sts128(fact + r * 32 + half * 16, q);
+}
+
+// B chunk j: 16 logical columns n, each a 16-rank vector stored with the rank order
+// [0,1,8,9, 2,3,10,11, 4,5,12,13, 6,7,14,15] so that an mma B fragment is one 8-byte read.
+// Logical column N = 16j + n covers the output columns of block G = N / per, pattern
+// offset e = N % per (per = 16/kRank): B[o, r] = w_G[kRank*e + r].
+template <int kRank>
+__device__ __forceinline__ void decode_b_chunk(const SgmvParams& p, const float* lut_b, int64_t slot, int j,
+                                               uint8_t* fact, int lane) {
+    constexpr int kPer = 16 / kRank;
+    const int n = lane >> 1;
+    const int half = lane & 1;      // ranks 8*half .. 8*half+7
+    const int N = 16 * j + n;
+    const int G = N / kPer;
+    const int e = N - G * kPer;
+    float val[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) val[i] = 0.f;
+    const bool live = (G < p.b_blocks) && (8 * half < kRank);
+    if (live) {
+        uint32_t k[LITHE_MAX_LEVELS];
+        fetch_indices<LITHE_MAX_LEVELS>(p.ib, slot, G, k, p.err);
+        const int u0 = kRank * e + 8 * half;    // first pattern position needed
+        float v[8];
+        decode_eight<LITHE_MAX_LEVELS>(lut_b, k, p.ib.levels, static_cast<uint32_t>(u0 >> 3), v);
+        const int off = u0 & 7;
+#pragma unroll
+        for (int i = 0; i < 8; ++i)
+            if (8 * half + i < kRank) val[i] = v[(off + i) & 7];
+    }
+    uint32_t* dst = reinterpret_cast<uint32_t*>(fact + n * 32);
+#pragma unroll
+    for (int i = 0; i < 8; i += 2) dst[(i >> 1) * 2 + half] = pack_bf16x2(val[i], val[i + 1]);
+}
+
+template <int kRank>
+__device__ void run_decoder(int d, int lane, const SgmvParams& p, uint8_t* facts, const float* lut_s,
+                            uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin, int u_end) {
+    uint32_t pos = 0;
+    for (int u = u_begin; u < u_end; ++u) {
+        const Unit un = unit_at(p, u);
+        const int n = un.nx + un.no;
+        for (int c = 0; c < n; ++c, ++pos) {
+            if (static_cast<int>(pos % kDecodeWarps) != d) continue;
+            const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return;
+            if (un.active) {
+                uint8_t* fact = facts + s * kFactBytes;
+                if (c < un.nx) decode_a_chunk<kRank>(p, lut_s, un.slot, c, fact, lane);
+                else decode_b_chunk<kRank>(p, lut_s + LITHE_MAX_LEVELS * 16, un.slot, c - un.nx, fact, lane);
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[s]);
+        }
+    }
+}
+
+// ---------------------------------------------------------------------------------------
+// Producer (one lane)
+// ---------------------------------------------------------------------------------------
+__device__ uint32_t run_producer(const SgmvParams& p, const CUtensorMap* tmx, const CUtensorMap* tmo,
+                                 uint8_t* tiles, uint64_t* full, uint64_t* empty, volatile int* abort,
+                                 int u_begin, int u_end) {
+    uint32_t pos = 0;
+    for (int u = u_begin; u < u_end; ++u) {
+        const Unit un = unit_at(p, u);
+        if (!un.active && un.slot >= p.n_slots && p.err) atomicOr(p.err, LITHE_DEVERR_SLOT);
+        const int n = un.nx + un.no;
+        for (int c = 0; c < n; ++c, ++pos) {
+            const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
+            if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return pos;
+            uint8_t* dst = tiles + s * kTileBytes;
+            if (c < un.nx) {
+                mbar_arrive_expect_tx(&full[s], kTileBytes);
+                tma_load_3d(dst, tmx, &full[s], c * kChunk, un.mt * kBM, un.b);
+            } else if (p.accumulate) {
+                mbar_arrive_expect_tx(&full[s], kTileBytes);
+                tma_load_3d(dst, tmo, &full[s], (c - un.nx) * kChunk, un.mt * kBM, un.b);
+            } else {
+                mbar_arrive(&full[s]);
+            }
+        }
+    }
+    return pos;
+}
+
+// ---------------------------------------------------------------------------------------
+// Consumer warps
+// ---------------------------------------------------------------------------------------
+// Apply the two expand results (c0 -> logical column 2t, c1 -> 2t+1 of n8 tile q) to the
+// thread's output values of one row, in the swizzled smem tile.
+template <int kRank>
+__device__ __forceinline__ void rmw_row(uint8_t* row, int g, int q, int t4, float c0, float c1, bool acc) {
+    if constexpr (kRank >= 8) {
+        uint8_t* a = row + ((((q << 2) + t4) ^ g) << 4);
+        uint4 v = acc ? lds128(a) : make_uint4(0, 0, 0, 0);
+        if constexpr (kRank == 16) {   // columns: c0 c0 c0 c0 c1 c1 c1 c1
+            v.x = add_bf16x2(v.x, c0, c0);
+            v.y = add_bf16x2(v.y, c0, c0);
+            v.z = add_bf16x2(v.z, c1, c1);
+            v.w = add_bf16x2(v.w, c1, c1);
+        } else {                       // columns: c0 c1 c0 c1 ...
+            v.x = add_bf16x2(v.x, c0, c1);
+            v.y = add_bf16x2(v.y, c0, c1);
+            v.z = add_bf16x2(v.z, c0, c1);
+            v.w = add_bf16x2(v.w, c0, c1);
+        }
+        sts128(a, v);
+    } else {
+        constexpr int kPer = 16 / kRank;            // logical columns per block
+        const int nl = 8 * q + 2 * t4;              // local logical column of c0
+        const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
+#pragma unroll
+        for (int pp = 0; pp < 4; ++pp) {
+            const int col = base + pp * kPer;       // even: c0 at col, c1 at col + 1
+            uint32_t* a = reinterpret_cast<uint32_t*>(row + ((((col >> 3) ^ g)) << 4) + (col & 7) * 2);
+            const uint32_t w = acc ? *a : 0u;
+            *a = add_bf16x2(w, c0, c1);
+        }
+    }
+}
+
+template <int kRank>
+__device__ void run_consumer(int w, int lane, const SgmvParams& p, const CUtensorMap* tmo_st, uint8_t* tiles,
+                             const uint8_t* facts, uint64_t* full, uint64_t* empty, volatile int* abort,
+                             int u_begin, int u_end) {
+    const int g = lane >> 2, t4 = lane & 3;
+    const int r0 = 16 * w + g;           // rows r0 and r0 + 8 of the 64-token tile
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    uint32_t pos = 0;
+    int pending = -1;                    // stage whose TMA store may still be reading smem
+    for (int u = u_begin; u < u_end; ++u) {
+        const Unit un = unit_at(p, u);
+        if (un.nx + un.no == 0) continue;
+        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+        for (int c = 0; c < un.nx; ++c, ++pos) {
+            const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
+            if (!mbar_wait(&full[s], ph, abort, p.err)) goto done;
+            {
+                const uint8_t* tile = tiles + s * kTileBytes;
+                const uint8_t* fa = facts + s * kFactBytes;
+                const uint8_t* ra = tile + r0 * 128;
+                const uint8_t* rb = ra + 8 * 128;
+                const uint4 xa0 = lds128(ra + ((t4 ^ g) << 4));
+                const uint4 xa1 = lds128(ra + (((4 + t4) ^ g) << 4));
+                const uint4 xb0 = lds128(rb + ((t4 ^ g) << 4));
+                const uint4 xb1 = lds128(rb + (((4 + t4) ^ g) << 4));
+                const uint4 f0 = lds128(fa + g * 32 + (t4 & 1) * 16);
+                const uint4 f1 = lds128(fa + (g + 8) * 32 + (t4 & 1) * 16);
+                {
+                    const uint32_t a[4] = {xa0.x, xb0.x, xa0.y, xb0.y};
+                    mma_bf16_16816(acc0, a, f0.x, f0.y, acc0);
+                    mma_bf16_16816(acc1, a, f1.x, f1.y, acc1);
+                }
+                {
+                    const uint32_t a[4] = {xa0.z, xb0.z, xa0.w, xb0.w};
+                    mma_bf16_16816(acc0, a, f0.z, f0.w, acc0);
+                    mma_bf16_16816(acc1, a, f1.z, f1.w, acc1);
+                }
+                {
+                    const uint32_t a[4] = {xa1.x, xb1.x, xa1.y, xb1.y};
+                    mma_bf16_16816(acc0, a, f0.x, f0.y, acc0);
+                    mma_bf16_16816(acc1, a, f1.x, f1.y, acc1);
+                }
+                {
+                    const uint32_t a[4] = {xa1.z, xb1.z, xa1.w, xb1.w};
+                    mma_bf16_16816(acc0, a, f0.z, f0.w, acc0);
+                    mma_bf16_16816(acc1, a, f1.z, f1.w, acc1);
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&empty[s]);
+        }
+        {
+            const float sc = p.scaling * (p.weights ? __ldg(p.weights + un.b) : 1.0f);
+            const uint32_t ha[4] = {pack_bf16x2(acc0[0] * sc, acc0[1] * sc), pack_bf16x2(acc0[2] * sc, acc0[3] * sc),
+                                    pack_bf16x2(acc1[0] * sc, acc1[1] * sc), pack_bf16x2(acc1[2] * sc, acc1[3] * sc)};
+            const int row_tile0 = un.mt * kBM + 16 * w;
+            const bool rows_live = row_tile0 < p.m;
+            for (int j = 0; j < un.no; ++j, ++pos) {
+                const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
+                if (!mbar_wait(&full[s], ph, abort, p.err)) goto done;
+                uint8_t* tile = tiles + s * kTileBytes;
+                float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
+                if (un.active) {
+                    const uint8_t* fb = facts + s * kFactBytes;
+                    const uint2 b0 = *reinterpret_cast<const uint2*>(fb + g * 32 + t4 * 8);
+                    const uint2 b1 = *reinterpret_cast<const uint2*>(fb + (g + 8) * 32 + t4 * 8);
+                    mma_bf16_16816(d0, ha, b0.x, b0.y, zero);
+                    mma_bf16_16816(d1, ha, b1.x, b1.y, zero);
+                }
+                uint8_t* ra = tile + r0 * 128;
+                uint8_t* rb = ra + 8 * 128;
+                const bool acc = p.accumulate != 0;
+                rmw_row<kRank>(ra, g, 0, t4, d0[0], d0[1], acc);
+                rmw_row<kRank>(rb, g, 0, t4, d0[2], d0[3], acc);
+                rmw_row<kRank>(ra, g, 1, t4, d1[0], d1[1], acc);
+                rmw_row<kRank>(rb, g, 1, t4, d1[2], d1[3], acc);
+                fence_proxy_async_smem();
+                __syncwarp();
+                if (lane == 0) {
+                    if (rows_live) tma_store_3d(tmo_st, tile + w * (16 * 128), j * kChunk, row_tile0, un.b);
+                    bulk_commit();
+                    bulk_wait_read<1>();
+                    if (pending >= 0) mbar_arrive(&empty[pending]);
+                    pending = static_cast<int>(s);
+                }
+                __syncwarp();
+            }
+            if (lane == 0 && pending >= 0) {
+                bulk_wait_read<0>();
+                mbar_arrive(&empty[pending]);
+                pending = -1;
+            }
+            __syncwarp();
+        }
+    }
+done:
+    if (lane == 0) bulk_wait_all();
+    __syncwarp();
+}
+
+template <int kRank>
+__global__ void __launch_bounds__(kThreads, 1)
+    sgmv_index_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmo_ld,
+                      const __grid_constant__ CUtensorMap tmo_st, const __grid_constant__ SgmvParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    uint8_t* tiles = base;
+    uint8_t* facts = tiles + kStages * kTileBytes;
+    uint64_t* full = reinterpret_cast<uint64_t*>(facts + kStages * kFactBytes);
+    uint64_t* empty = full + kStages;
+    float* lut_s = reinterpret_cast<float*>(empty + kStages);
+    volatile int* abort = reinterpret_cast<volatile int*>(lut_s + kLutFloats);
+
+    const int tid = threadIdx.x;
+    if (tid == 0) {
+        for (int s = 0; s < kStages; ++s) {
+            mbar_init(&full[s], 2);                 // producer + one decoder warp
+            mbar_init(&empty[s], kConsumerWarps);   // one arrival per consumer warp
+        }
+        *abort = 0;
+        fence_mbar_init();
+    }
+    for (int i = tid; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
+    __syncthreads();
+
+    const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_units / gridDim.x);
+    const int u_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.total_units / gridDim.x);
+    const int warp = tid >> 5, lane = tid & 31;
+
+    uint32_t issued = 0;
+    if (warp < kConsumerWarps) {
+        run_consumer<kRank>(warp, lane, p, &tmo_st, tiles, facts, full, empty, abort, u_begin, u_end);
+    } else if (warp == kProducerWarp) {
+        if (lane == 0) {
+            prefetch_tmap(&tmx);
+            prefetch_tmap(&tmo_ld);
+            prefetch_tmap(&tmo_st);
+            issued = run_producer(p, &tmx, &tmo_ld, tiles, full, empty, abort, u_begin, u_end);
+        }
+    } else {
+        run_decoder<kRank>(warp - kFirstDecodeWarp, lane, p, facts, lut_s, full, empty, abort, u_begin, u_end);
+    }
+    __syncthreads();
+    // After an aborted pipeline, let the producer's last TMA loads land before the block's
+    // shared memory is released (bounded: loads complete in microseconds).
+    if (*abort && warp == kProducerWarp && lane == 0) {
+        const uint64_t t0 = global_timer_ns();
+        const uint32_t first = issued > static_cast<uint32_t>(kStages) ? issued - kStages : 0u;
+        for (uint32_t q = first; q < issued; ++q) {
+            const uint32_t s = q % kStages, ph = (q / kStages) & 1u;
+            while (!mbar_try_wait(&full[s], ph) && global_timer_ns() - t0 < 20000000ull) {
+            }
+        }
+    }
+}
+
+template <int kRank>
+static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, const CUtensorMap& tmo_st,
+                           const SgmvParams& p, int grid, int device, cudaStream_t stream) {
+    static bool configured[64] = {false};
+    auto kern = sgmv_index_kernel<kRank>;
+    if (!configured[device]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(kSmemBytes));
+        if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(sgmv_index_kernel)");
+        configured[device] = true;
+    }
+    kern<<<grid, kThreads, kSmemBytes, stream>>>(tmx, tmo_ld, tmo_st, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "sgmv_index_kernel launch");
+    return LITHE_OK;
+}
+
+static int32_t check_view(const lithe_index_view* v, const char* name) {
+    if (!v) return fail_arg("%s is NULL", name);
+    if (!v->base) return fail_arg("%s.base is NULL", name);
+    if (v->format != LITHE_IDX_PACKED9 && v->format != LITHE_IDX_I16 && v->format != LITHE_IDX_I32)
+        return fail_arg("%s.format %d is not a LITHE_IDX_* value", name, v->format);
+    if (v->num_levels < 1 || v->num_levels > LITHE_MAX_LEVELS)
+        return fail_unsupported("%s.num_levels must be in [1, %d], got %d", name, LITHE_MAX_LEVELS, v->num_levels);
+    const int align = v->format == LITHE_IDX_PACKED9 ? 8 : (v->format == LITHE_IDX_I32 ? 4 : 2);
+    if (reinterpret_cast<uintptr_t>(v->base) % align) return fail_arg("%s.base is misaligned", name);
+    if (v->slot_stride < 0 || v->offset < 0 || v->level_stride < 0)
+        return fail_arg("%s has a negative stride or offset", name);
+    return LITHE_OK;
+}
+
+static IndexView to_view(const lithe_index_view* v) {
+    IndexView r;
+    r.base = v->base;
+    r.format = v->format;
+    r.levels = v->num_levels;
+    r.slot_stride = v->slot_stride;
+    r.offset = v->offset;
+    r.level_stride = v->level_stride;
+    return r;
+}
+
+}  // namespace lithe
+
+extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate, const lithe_index_view* idx_a,
+                                    const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids,
+                                    const float* weights, int32_t batch, int32_t m, int32_t d_in, int32_t d_out,
+                                    int32_t rank, const float* lut, float scaling, int32_t* err_flag, void* stream) {
+    using namespace lithe;
+    clear_error();
+    if (batch < 0 || m < 0) return fail_arg("batch (%d) and m (%d) must be >= 0", batch, m);
+    if (rank != 1 && rank != 2 && rank != 4 && rank != 8 && rank != 16)
+        return fail_unsupported("rank must be one of 1, 2, 4, 8, 16; got %d", rank);
+    if (d_in <= 0 || d_in % 64) return fail_arg("d_in must be a positive multiple of 64, got %d", d_in);
+    if (d_out <= 0 || d_out % 8) return fail_arg("d_out must be a positive multiple of 8, got %d", d_out);
+    if ((static_cast<int64_t>(d_out) * rank) % 64)
+        return fail_arg("d_out * rank must be a multiple of 64 (d_out=%d, rank=%d)", d_out, rank);
+    int32_t rc = check_view(idx_a, "idx_a");
+    if (rc != LITHE_OK) return rc;
+    rc = check_view(idx_b, "idx_b");
+    if (rc != LITHE_OK) return rc;
+    if (idx_a->num_levels != idx_b->num_levels) return fail_arg("idx_a and idx_b have different num_levels");
+    if (!lut) return fail_arg("lut is NULL");
+    if (n_slots < 0) return fail_arg("n_slots must be >= 0");
+    if (batch == 0 || m == 0) return LITHE_OK;
+    if (!x || !out || !ids) return fail_arg("x, out and ids must be non-NULL");
+    if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
+        return fail_arg("x and out must be 16-byte aligned");
+    const int64_t n_mtiles = (static_cast<int64_t>(m) + kBM - 1) / kBM;
+    if (n_mtiles * batch > 0x7fffffffLL) return fail_arg("batch * ceil(m/64) exceeds 2^31");
+
+    int device = 0, sms = 0;
+    rc = current_device_sms(&device, &sms);
+    if (rc != LITHE_OK) return rc;
+
+    CUtensorMap tmx, tmo_ld, tmo_st;
+    rc = encode_bf16_3d(&tmx, x, d_in, m, batch, kChunk, kBM);
+    if (rc != LITHE_OK) return rc;
+    rc = encode_bf16_3d(&tmo_ld, out, d_out, m, batch, kChunk, kBM);
+    if (rc != LITHE_OK) return rc;
+    rc = encode_bf16_3d(&tmo_st, out, d_out, m, batch, kChunk, 16);
+    if (rc != LITHE_OK) return rc;
+
+    SgmvParams p{};
+    p.ia = to_view(idx_a);
+    p.ib = to_view(idx_b);
+    p.ids = ids;
+    p.weights = weights;
+    p.err = err_flag;
+    p.n_slots = n_slots;
+    p.m = m;
+    p.d_in = d_in;
+    p.d_out = d_out;
+    p.n_mtiles = static_cast<int32_t>(n_mtiles);
+    p.n_xchunks = d_in / kChunk;
+    p.n_ochunks = (d_out + kChunk - 1) / kChunk;
+    p.total_units = static_cast<int32_t>(n_mtiles * batch);
+    p.accumulate = accumulate ? 1 : 0;
+    p.a_blocks_per_row = d_in / 64;
+    p.b_blocks = static_cast<int32_t>(static_cast<int64_t>(d_out) * rank / 64);
+    p.scaling = scaling;
+    expand_lut(lut, idx_a->num_levels, p.lut);
+
+    const int grid = static_cast<int>(p.total_units < sms ? p.total_units : sms);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    switch (rank) {
+        case 16: return launch_rank<16>(tmx, tmo_ld, tmo_st, p, grid, device, s);
+        case 8: return launch_rank<8>(tmx, tmo_ld, tmo_st, p, grid, device, s);
+        case 4: return launch_rank<4>(tmx, tmo_ld, tmo_st, p, grid, device, s);
+        case 2: return launch_rank<2>(tmx, tmo_ld, tmo_st, p, grid, device, s);
+        default: return launch_rank<1>(tmx, tmo_ld, tmo_st, p, grid, device, s);
+    }
+}

@@ -1,0 +1,153 @@
+"""The ``.lithe`` adapter file (format of lithe/fileio.py in the reference implementation).
+
+Byte layout::
+
+    b"LITHE001" | uint32 LE n | xz(UTF-8 JSON header) (n bytes) | xz(index stream)
+
+The index stream is little-endian uint16: the A-side indices of every module in header
+order, then the B-side indices of every module, each module's (L, n_blocks) matrix in
+row-major order (lithe/fileio.py:55-58).  Both parts are LZMA with preset 9 | EXTREME.
+The header carries the codebook description and its SHA-256, the payload SHA-256 and the
+module list; ``load_lithe`` checks both digests and the stream length (fileio.py:119-138).
+Decompression stays on the host: this is the cold path that fills a resident bank.
+"""
+from __future__ import annotations
+
+import hashlib
+import json
+import lzma
+import struct
+from dataclasses import dataclass, field
+from pathlib import Path
+from typing import Any, Dict, List
+
+import numpy as np
+
+from . import codebook as cb
+from .quant import num_blocks
+
+MAGIC = b"LITHE001"
+LZMA_PRESET = 9 | lzma.PRESET_EXTREME
+
+
+@dataclass
+class LitheAdapter:
+    """Index streams of one adapter plus everything needed to decode them."""
+
+    modules: List[Dict[str, Any]]                  # [{"name", "shape_a", "shape_b"}] in stream order
+    indices: Dict[str, Dict[str, np.ndarray]]      # name -> {"A": (L, nA) uint16, "B": (L, nB) uint16}
+    rank: int
+    alpha: float
+    key_format: str = "diffusers"
+    base_model: str = "black-forest-labs/FLUX.1-dev"
+    block_size: int = cb.BLOCK_SIZE
+    n_bits: int = cb.N_BITS
+    num_levels: int = cb.NUM_LEVELS
+    sigma_a: List[float] = field(default_factory=lambda: list(cb.SIGMA_A))
+    sigma_b: List[float] = field(default_factory=lambda: list(cb.SIGMA_B))
+    metadata: Dict[str, Any] = field(default_factory=dict)
+
+    @property
+    def num_indices(self) -> int:
+        return sum(int(v["A"].size) + int(v["B"].size) for v in self.indices.values())
+
+    @property
+    def scaling(self) -> float:
+        return float(self.alpha) / self.rank
+
+    def raw_stream(self) -> bytes:
+        names = [m["name"] for m in self.modules]
+        sides = [self.indices[n]["A"] for n in names] + [self.indices[n]["B"] for n in names]
+        return b"".join(np.ascontiguousarray(a, dtype="<u2").tobytes() for a in sides)
+
+
+def _header(ad: LitheAdapter, raw: bytes) -> Dict[str, Any]:
+    return {
+        "format": "lithe",
+        "version": 1,
+        "codebook": {
+            "name": "hadamard9-twin",
+            "block_size": ad.block_size,
+            "n_bits": ad.n_bits,
+            "num_levels": ad.num_levels,
+            "sigma_a": [float(s) for s in ad.sigma_a],
+            "sigma_b": [float(s) for s in ad.sigma_b],
+            "sha256": cb.codebook_sha256(ad.block_size, ad.n_bits),
+        },
+        "rank": ad.rank,
+        "alpha": ad.alpha,
+        "key_format": ad.key_format,
+        "base_model": ad.base_model,
+        "index_dtype": "uint16-le",
+        "num_indices": ad.num_indices,
+        "payload_sha256": hashlib.sha256(raw).hexdigest(),
+        "modules": ad.modules,
+        "metadata": ad.metadata,
+    }
+
+
+def save_lithe(path, ad: LitheAdapter) -> int:
+    """Write ``ad`` to ``path``; returns the file size in bytes."""
+    if ad.n_bits > 16:
+        raise ValueError("uint16 streams need n_bits <= 16")
+    raw = ad.raw_stream()
+    head = lzma.compress(json.dumps(_header(ad, raw), separators=(",", ":")).encode("utf-8"), preset=LZMA_PRESET)
+    body = lzma.compress(raw, preset=LZMA_PRESET)
+    path = Path(path)
+    path.parent.mkdir(parents=True, exist_ok=True)
+    path.write_bytes(MAGIC + struct.pack("<I", len(head)) + head + body)
+    return path.stat().st_size
+
+
+def _split_file(path):
+    data = Path(path).read_bytes()
+    if len(data) < len(MAGIC) + 4 or data[: len(MAGIC)] != MAGIC:
+        raise ValueError(f"{path}: not a .lithe file")
+    (n,) = struct.unpack_from("<I", data, len(MAGIC))
+    start = len(MAGIC) + 4
+    if start + n > len(data):
+        raise ValueError(f"{path}: truncated header")
+    try:
+        header = json.loads(lzma.decompress(data[start:start + n]).decode("utf-8"))
+    except (lzma.LZMAError, UnicodeDecodeError, json.JSONDecodeError) as e:
+        raise ValueError(f"{path}: corrupt header ({e})") from e
+    return header, data[start + n:]
+
+
+def read_header(path) -> Dict[str, Any]:
+    return _split_file(path)[0]
+
+
+def load_lithe(path, verify: bool = True) -> LitheAdapter:
+    header, body = _split_file(path)
+    try:
+        raw = lzma.decompress(body)
+    except lzma.LZMAError as e:
+        raise ValueError(f"{path}: corrupt index stream ({e})") from e
+    cbh = header["codebook"]
+    if verify:
+        if hashlib.sha256(raw).hexdigest() != header["payload_sha256"]:
+            raise ValueError(f"{path}: payload checksum mismatch")
+        if cbh["sha256"] != cb.codebook_sha256(cbh["block_size"], cbh["n_bits"]):
+            raise ValueError(f"{path}: codebook hash mismatch")
+    if len(raw) % 2:
+        raise ValueError(f"{path}: odd-length uint16 stream")
+    stream = np.frombuffer(raw, dtype="<u2")
+    levels, bs = int(cbh["num_levels"]), int(cbh["block_size"])
+    modules = header["modules"]
+    count_a = [levels * num_blocks(m["shape_a"], bs) for m in modules]
+    count_b = [levels * num_blocks(m["shape_b"], bs) for m in modules]
+    if sum(count_a) + sum(count_b) != stream.size:
+        raise ValueError(f"{path}: stream length {stream.size} does not match header")
+    indices: Dict[str, Dict[str, np.ndarray]] = {}
+    pos = 0
+    for m, c in zip(modules, count_a):
+        indices[m["name"]] = {"A": stream[pos:pos + c].reshape(levels, -1).copy()}
+        pos += c
+    for m, c in zip(modules, count_b):
+        indices[m["name"]]["B"] = stream[pos:pos + c].reshape(levels, -1).copy()
+        pos += c
+    return LitheAdapter(modules=modules, indices=indices, rank=header["rank"], alpha=header["alpha"],
+                        key_format=header["key_format"], base_model=header.get("base_model", ""),
+                        block_size=bs, n_bits=cbh["n_bits"], num_levels=levels,
+                        sigma_a=cbh["sigma_a"], sigma_b=cbh["sigma_b"], metadata=header.get("metadata", {}))

@@ -1,0 +1,153 @@
+"""Tensor-level wrappers over the C ABI (one function per entry point of include/lithe_b200.h).
+
+They check devices, dtypes and layouts, pass raw device pointers and the current torch
+stream to liblithe_b200, and raise on a non-zero return.  No host synchronisation: the
+kernels' device-side error word is read only by ``device_errors``.
+"""
+from __future__ import annotations
+
+import ctypes
+import threading
+from typing import Optional
+
+import numpy as np
+import torch
+
+from .. import _lib
+
+_err_words: dict = {}
+_err_lock = threading.Lock()
+
+
+def error_word(device: torch.device) -> torch.Tensor:
+    """The int32 device error word the kernels of ``device`` OR their LITHE_DEVERR_* bits into."""
+    device = torch.device(device)
+    if device.index is None:
+        device = torch.device("cuda", torch.cuda.current_device())
+    with _err_lock:
+        t = _err_words.get(device.index)
+        if t is None:
+            t = torch.zeros(1, dtype=torch.int32, device=device)
+            _err_words[device.index] = t
+    return t
+
+
+def device_errors(device=None, clear: bool = True) -> int:
+    """Synchronise with ``device``'s error word and return its LITHE_DEVERR_* bits."""
+    device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
+    w = error_word(device)
+    val = int(w.item())
+    if clear and val:
+        w.zero_()
+    return val
+
+
+def raise_device_errors(device=None) -> None:
+    bits = device_errors(device)
+    if bits:
+        names = [n for b, n in ((_lib.DEVERR_SLOT, "adapter slot out of range"),
+                                (_lib.DEVERR_INDEX, "index outside [0, 512) in an integer bank"),
+                                (_lib.DEVERR_TIMEOUT, "pipeline wait timed out")) if bits & b]
+        raise ValueError("lithe_b200 kernel reported: " + "; ".join(names))
+
+
+def _require_cuda(t: torch.Tensor, what: str) -> None:
+    if not t.is_cuda:
+        raise ValueError(f"{what} must be a CUDA tensor (lithe_b200 has no CPU path), got {t.device}")
+
+
+def stream_handle(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+def lut_array(lut: np.ndarray) -> ctypes.Array:
+    return _lib.float_array(np.asarray(lut, dtype=np.float32).reshape(-1))
+
+
+def index_view(base: torch.Tensor, fmt: int, levels: int, slot_stride: int, offset: int,
+               level_stride: int = 0) -> _lib.IndexView:
+    return _lib.IndexView(base.data_ptr(), fmt, levels, slot_stride, offset, level_stride)
+
+
+def level_major_view(idx: torch.Tensor) -> _lib.IndexView:
+    """View of an (n_slots, L, n_blocks) int16/int32 contiguous bank."""
+    fmt = {torch.int16: _lib.IDX_I16, torch.int32: _lib.IDX_I32}.get(idx.dtype)
+    if fmt is None or idx.dim() != 3 or not idx.is_contiguous():
+        raise ValueError("integer index banks must be contiguous (n_slots, L, n_blocks) int16/int32")
+    return index_view(idx, fmt, idx.shape[1], idx.shape[1] * idx.shape[2], 0, idx.shape[2])
+
+
+def sgmv_index_(x: torch.Tensor, out: torch.Tensor, *, accumulate: bool, view_a: _lib.IndexView,
+                view_b: _lib.IndexView, n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor],
+                rank: int, lut: np.ndarray, scaling: float, err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """lithe_sgmv_index on torch tensors; ``out`` (B, M, d_out) bf16 is written in place."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
+        raise TypeError(f"x and out must be bfloat16 (got {x.dtype}, {out.dtype})")
+    if x.dim() != 3 or out.dim() != 3 or x.shape[:2] != out.shape[:2]:
+        raise ValueError(f"x (B, M, d_in) and out (B, M, d_out) disagree: {tuple(x.shape)} vs {tuple(out.shape)}")
+    if not (x.is_contiguous() and out.is_contiguous()):
+        raise ValueError("x and out must be contiguous")
+    if out.device != x.device or ids.device != x.device:
+        raise ValueError("x, out and ids must be on the same device")
+    if ids.dtype != torch.int32 or ids.dim() != 1 or ids.numel() != x.shape[0] or not ids.is_contiguous():
+        raise ValueError("ids must be a contiguous (B,) int32 tensor")
+    if weights is not None and (weights.dtype != torch.float32 or weights.device != x.device
+                                or weights.numel() != x.shape[0] or not weights.is_contiguous()):
+        raise ValueError("weights must be a contiguous (B,) float32 tensor on x's device")
+    if err is None:
+        err = error_word(x.device)
+    bsz, m, d_in = x.shape
+    with torch.cuda.device(x.device):
+        rc = _lib.lib().lithe_sgmv_index(
+            x.data_ptr(), out.data_ptr(), 1 if accumulate else 0, ctypes.byref(view_a), ctypes.byref(view_b),
+            int(n_slots), ids.data_ptr(), weights.data_ptr() if weights is not None else None,
+            bsz, m, d_in, out.shape[2], int(rank), lut_array(lut), float(scaling), err.data_ptr(),
+            stream_handle(x.device))
+    _lib.check(rc, "lithe_sgmv_index")
+    return out
+
+
+def decode_packed_(words: torch.Tensor, n_blocks: int, levels: int, sides: Optional[torch.Tensor],
+                   lut: np.ndarray, out: torch.Tensor) -> torch.Tensor:
+    _require_cuda(words, "words")
+    if words.dtype not in (torch.int64, torch.uint64) or not words.is_contiguous():
+        raise ValueError("words must be a contiguous 64-bit tensor")
+    if out.dtype not in (torch.bfloat16, torch.float32) or not out.is_contiguous():
+        raise ValueError("out must be a contiguous bfloat16/float32 tensor")
+    if out.numel() != n_blocks * 64:
+        raise ValueError("out must hold n_blocks * 64 values")
+    if words.numel() * 7 < n_blocks * levels:
+        raise ValueError(f"words ({words.numel()}) too short for {n_blocks} blocks x {levels} levels")
+    if sides is not None and (sides.dtype != torch.int8 or sides.numel() != n_blocks or sides.device != words.device):
+        raise ValueError("sides must be an int8 tensor with one entry per block on the words' device")
+    with torch.cuda.device(words.device):
+        rc = _lib.lib().lithe_decode_packed(
+            words.data_ptr(), int(n_blocks), int(levels), sides.data_ptr() if sides is not None else None,
+            lut_array(lut), out.data_ptr(), _lib.DTYPE_F32 if out.dtype == torch.float32 else _lib.DTYPE_BF16,
+            stream_handle(words.device))
+    _lib.check(rc, "lithe_decode_packed")
+    return out
+
+
+def decode_packed_batch_(bank: torch.Tensor, slot_ids: torch.Tensor, n_blocks: int, levels: int,
+                         sides: Optional[torch.Tensor], lut: np.ndarray, out: torch.Tensor,
+                         err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    _require_cuda(bank, "bank")
+    if bank.dim() != 2 or bank.dtype not in (torch.int64, torch.uint64) or not bank.is_contiguous():
+        raise ValueError("bank must be a contiguous (n_slots, slot_stride) 64-bit tensor")
+    if slot_ids.dtype != torch.int32 or slot_ids.device != bank.device or not slot_ids.is_contiguous():
+        raise ValueError("slot_ids must be a contiguous int32 tensor on the bank's device")
+    if out.dtype not in (torch.bfloat16, torch.float32) or not out.is_contiguous() \
+            or out.numel() != slot_ids.numel() * n_blocks * 64:
+        raise ValueError("out must be a contiguous (n_sel, n_blocks, 64) bfloat16/float32 tensor")
+    if err is None:
+        err = error_word(bank.device)
+    with torch.cuda.device(bank.device):
+        rc = _lib.lib().lithe_decode_packed_batch(
+            bank.data_ptr(), bank.shape[1], bank.shape[0], slot_ids.data_ptr(), slot_ids.numel(), int(n_blocks),
+            int(levels), sides.data_ptr() if sides is not None else None, lut_array(lut), out.data_ptr(),
+            _lib.DTYPE_F32 if out.dtype == torch.float32 else _lib.DTYPE_BF16, err.data_ptr(),
+            stream_handle(bank.device))
+    _lib.check(rc, "lithe_decode_packed_batch")
+    return out

@@ -1,0 +1,123 @@
+"""Linear wrappers that route every sample of a batch to its own adapter
+(API of lithe/kernels/layers.py).
+
+``IndexLoRALinear``  index-resident slots; out = base(x) and the fused kernel adds each
+                     sample's delta into that output in place (one launch per forward, no
+                     delta tensor, no second pass over the output).
+``PackedLoRALinear`` the same over a shared ``PackedBank`` (9-bit packed residency): many
+                     modules and thousands of slots in one device tensor.
+Routing: with ``assign`` unset every sample uses slot 0 (lithe/kernels/layers.py:263-265);
+otherwise ``assign`` (B,) gives the slot of every sample, -1 for none.
+"""
+from __future__ import annotations
+
+from typing import Callable, Dict, Iterable, Optional
+
+import torch
+from torch import nn
+
+from .. import codebook as cb
+from . import _launch
+from .packed import PackedBank
+from .shared import packed_codebook_lora_delta_, shared_codebook_lora_delta_
+
+
+def _inference_only(out: torch.Tensor) -> None:
+    if out.requires_grad and torch.is_grad_enabled():
+        raise RuntimeError("lithe_b200 layers are inference-only: run them under torch.no_grad()")
+
+
+def _as3d(x: torch.Tensor, out: torch.Tensor):
+    if x.dim() == 2:
+        return x.unsqueeze(1), out.unsqueeze(1)
+    if x.dim() == 3:
+        return x, out
+    raise ValueError(f"unsupported input rank {x.dim()}")
+
+
+class IndexLoRALinear(nn.Module):
+    """y = W x + per-sample delta decoded on the fly from resident index slots."""
+
+    def __init__(self, base: nn.Linear, idx_a: torch.Tensor, idx_b: torch.Tensor,
+                 pool_a: torch.Tensor, pool_b: torch.Tensor, rank: int, scaling: float):
+        super().__init__()
+        self.base = base
+        for p in self.base.parameters():
+            p.requires_grad_(False)
+        dev = base.weight.device
+        self.register_buffer("idx_a", idx_a.to(device=dev, dtype=torch.int32).contiguous(), persistent=False)
+        self.register_buffer("idx_b", idx_b.to(device=dev, dtype=torch.int32).contiguous(), persistent=False)
+        self.register_buffer("pool_a", pool_a.to(dev), persistent=False)
+        self.register_buffer("pool_b", pool_b.to(dev), persistent=False)
+        self.rank = int(rank)
+        self.d_out = base.out_features
+        self.scaling = float(scaling)
+        self.assign: Optional[torch.Tensor] = None
+
+    @property
+    def num_slots(self) -> int:
+        return int(self.idx_a.shape[0])
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        out = self.base(x)
+        _inference_only(out)
+        x3, out3 = _as3d(x, out)
+        assign = self.assign
+        if assign is None:
+            assign = torch.zeros(x3.shape[0], dtype=torch.int32, device=x.device)
+        shared_codebook_lora_delta_(out3, x3, self.idx_a, self.pool_a, self.idx_b, self.pool_b, assign,
+                                    self.rank, self.d_out, self.scaling, accumulate=True)
+        return out
+
+
+class PackedLoRALinear(nn.Module):
+    """y = W x + per-sample delta from module ``name`` of a shared packed bank."""
+
+    def __init__(self, base: nn.Linear, bank: PackedBank, name: str, rank: int, scaling: float):
+        super().__init__()
+        self.base = base
+        for p in self.base.parameters():
+            p.requires_grad_(False)
+        i = bank.layout.index(name)
+        if bank.layout.shapes_a[i] != (rank, base.in_features) or bank.layout.shapes_b[i] != (base.out_features, rank):
+            raise ValueError(f"{name}: bank shapes {bank.layout.shapes_a[i]}, {bank.layout.shapes_b[i]} do not "
+                             f"match the linear ({base.in_features} -> {base.out_features}, r={rank})")
+        self.bank = bank
+        self.name = name
+        self.rank = int(rank)
+        self.scaling = float(scaling)
+        self.assign: Optional[torch.Tensor] = None
+        self.weights: Optional[torch.Tensor] = None
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        out = self.base(x)
+        _inference_only(out)
+        x3, out3 = _as3d(x, out)
+        assign = self.assign
+        if assign is None:
+            assign = torch.zeros(x3.shape[0], dtype=torch.int32, device=x.device)
+        packed_codebook_lora_delta_(out3, x3, self.bank, self.name, assign, scaling=self.scaling,
+                                    weights=self.weights)
+        return out
+
+
+def wrap_linears(model: nn.Module, paths: Iterable[str],
+                 factory: Callable[[str, nn.Linear], nn.Module]) -> Dict[str, nn.Module]:
+    """Replace ``model.<path>`` (an ``nn.Linear``) by ``factory(path, linear)`` for every path."""
+    wrapped = {}
+    for path in paths:
+        base = model.get_submodule(path)
+        if not isinstance(base, nn.Linear):
+            raise TypeError(f"{path} is not nn.Linear")
+        parent_name, _, child = path.rpartition(".")
+        parent = model.get_submodule(parent_name) if parent_name else model
+        module = factory(path, base)
+        setattr(parent, child, module)
+        wrapped[path] = module
+    return wrapped
+
+
+def pools_on(device, dtype=torch.float32):
+    """The twin pools on ``device`` (fp32 by default; any dtype decodes bit-exactly through it)."""
+    pa, pb = cb.twin_pools()
+    return pa.to(device=device, dtype=dtype), pb.to(device=device, dtype=dtype)

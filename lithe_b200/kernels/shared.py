@@ -1,0 +1,109 @@
+"""Index-resident per-sample LoRA delta, decode fused (API of lithe/kernels/shared.py).
+
+Each wrapped linear keeps, for every resident adapter, only its index tensors
+idx_A (n_slots, L, n_blocks_A) and idx_B (n_slots, L, n_blocks_B) plus one pair of codebook
+pools shared by all adapters; ``assign`` (B,) routes sample b to slot j = assign[b]:
+
+    A_j[r, d] = sum_l pool_A[l, idx_A[j, l, blk(r, d)], pos(r, d)]
+    B_j[o, r] = sum_l pool_B[l, idx_B[j, l, blk(o, r)], pos(o, r)]
+    delta[b]  = scaling * (x_b @ A_j^T) @ B_j^T
+
+One launch of the sm_100a kernel ``lithe_sgmv_index`` computes the whole batch, reading the
+int16/int32 banks in place (no per-call index copies) and decoding through the pools' ten
+distinct values per level, so the decoded factors equal a decode through the given pools bit
+for bit.  ``shared_codebook_lora_delta_`` accumulates into an existing output instead of
+allocating a delta (the path the layer wrappers use).
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from .. import codebook as cb
+from . import _launch
+
+
+def _check(x, idx_A, pools_A, idx_B, pools_B, assign, R, D_out):
+    """Argument checks of lithe/kernels/shared.py:160-174."""
+    if x.dim() != 3:
+        raise ValueError(f"x must be (B, M, D_in), got {tuple(x.shape)}")
+    bsz, _, d_in = x.shape
+    L, _, bs = pools_A.shape
+    if pools_B.shape != pools_A.shape:
+        raise ValueError("pools_A and pools_B must have the same (L, K, B) shape")
+    if idx_A.dim() != 3 or idx_B.dim() != 3 or idx_A.shape[1] != L or idx_B.shape[1] != L:
+        raise ValueError("index pools must be (n_slots, L, n_blocks)")
+    if R * d_in != idx_A.shape[2] * bs or D_out * R != idx_B.shape[2] * bs:
+        raise ValueError("index pools do not match (R, D_in, D_out)")
+    if d_in % bs or (D_out * R) % bs:
+        raise ValueError("d_in and d_out * r must be multiples of the block size")
+    if tuple(assign.shape) != (bsz,):
+        raise ValueError(f"assign must be ({bsz},)")
+    if idx_A.shape[0] != idx_B.shape[0]:
+        raise ValueError("idx_A and idx_B must hold the same number of slots")
+
+
+def _bank(idx: torch.Tensor, device) -> torch.Tensor:
+    if idx.dtype not in (torch.int16, torch.int32):
+        idx = idx.to(torch.int32)
+    return idx.to(device).contiguous()
+
+
+def shared_codebook_lora_delta_(out: torch.Tensor, x: torch.Tensor, idx_A: torch.Tensor, pools_A: torch.Tensor,
+                                idx_B: torch.Tensor, pools_B: torch.Tensor, assign: torch.Tensor, R: int,
+                                D_out: int, scaling: float, accumulate: bool = True,
+                                weights: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """out (B, M, D_out) bf16 += (or =, accumulate=False) the per-sample delta, in place.
+
+    ``weights`` (B,) fp32 multiplies each sample's delta (mixture gains); assign[b] < 0
+    leaves sample b without a delta.  Out-of-range slots are reported in the device error
+    word (``lithe_b200.device_errors``).
+    """
+    _check(x, idx_A, pools_A, idx_B, pools_B, assign, R, D_out)
+    if out.shape != (x.shape[0], x.shape[1], D_out):
+        raise ValueError(f"out must be {(x.shape[0], x.shape[1], D_out)}, got {tuple(out.shape)}")
+    ia, ib = _bank(idx_A, x.device), _bank(idx_B, x.device)
+    ids = assign.to(device=x.device, dtype=torch.int32).contiguous()
+    w = None if weights is None else weights.to(device=x.device, dtype=torch.float32).contiguous()
+    return _launch.sgmv_index_(x.contiguous(), out, accumulate=accumulate, view_a=_launch.level_major_view(ia),
+                               view_b=_launch.level_major_view(ib), n_slots=ia.shape[0], ids=ids, weights=w,
+                               rank=R, lut=cb.kernel_lut(pools_A, pools_B), scaling=scaling)
+
+
+def shared_codebook_lora_delta(x: torch.Tensor, idx_A: torch.Tensor, pools_A: torch.Tensor, idx_B: torch.Tensor,
+                               pools_B: torch.Tensor, assign: torch.Tensor, R: int, D_out: int, scaling: float,
+                               out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
+    """Per-sample LoRA delta (B, M, D_out) decoded on the fly from index pools.
+
+    x (B, M, D_in) bfloat16 on a CUDA device; idx_A (n_slots, L, n_blocks_A) and idx_B
+    (n_slots, L, n_blocks_B) integer; pools (L, K, 64) float (any dtype, Hadamard
+    structure checked); assign (B,) slot per sample.  Returns a bfloat16 tensor.
+    """
+    _check(x, idx_A, pools_A, idx_B, pools_B, assign, R, D_out)
+    if out_dtype not in (None, torch.bfloat16):
+        raise NotImplementedError("the sm_100a kernel produces bfloat16 deltas")
+    out = torch.empty((x.shape[0], x.shape[1], D_out), dtype=torch.bfloat16, device=x.device)
+    return shared_codebook_lora_delta_(out, x, idx_A, pools_A, idx_B, pools_B, assign, R, D_out, scaling,
+                                       accumulate=False)
+
+
+def packed_codebook_lora_delta_(out: torch.Tensor, x: torch.Tensor, bank, name: str, assign: torch.Tensor,
+                                scaling: Optional[float] = None, weights: Optional[torch.Tensor] = None,
+                                accumulate: bool = True) -> torch.Tensor:
+    """out (B, M, d_out) bf16 += per-sample delta of module ``name`` of a ``PackedBank``, in place.
+
+    The packed counterpart of ``shared_codebook_lora_delta_``: the kernel reads the bank's
+    9-bit packed words directly.  ``scaling`` defaults to the layout's alpha / rank.
+    """
+    i = bank.layout.index(name)
+    rank, d_in = bank.layout.shapes_a[i]
+    d_out = bank.layout.shapes_b[i][0]
+    if x.dim() != 3 or x.shape[-1] != d_in or out.shape != (x.shape[0], x.shape[1], d_out):
+        raise ValueError(f"{name}: x must be (B, M, {d_in}) and out (B, M, {d_out})")
+    va, vb = bank.views(name)
+    ids = assign.to(device=x.device, dtype=torch.int32).contiguous()
+    w = None if weights is None else weights.to(device=x.device, dtype=torch.float32).contiguous()
+    return _launch.sgmv_index_(x.contiguous(), out, accumulate=accumulate, view_a=va, view_b=vb,
+                               n_slots=bank.n_slots, ids=ids, weights=w, rank=rank, lut=bank.lut,
+                               scaling=bank.layout.scaling if scaling is None else scaling)

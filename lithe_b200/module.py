@@ -1,0 +1,180 @@
+"""LITHE LoRA linear wrapper and its injection into a model (API of lithe/module.py).
+
+Inference form of ``LitheLinear`` (lithe/module.py:63-156): after ``load_indices`` the layer
+computes  y = W x + (B_hat A_hat x) * alpha / r  with A_hat, B_hat decoded from its index
+streams.  The indices stay resident on the GPU in packed form and the fused sm_100a kernel
+decodes them inside the shrink/expand tiles, accumulating into the base output; shapes the
+fused kernel does not take (d_in not a multiple of 64, other ranks) use factors decoded once
+by the decode kernel and two cuBLAS products.  Training (straight-through re-quantisation of
+fp32 proxies) is not part of this package.
+"""
+from __future__ import annotations
+
+import math
+from typing import Dict, Iterable, List, Optional, Sequence
+
+import numpy as np
+import torch
+from torch import nn
+
+from . import codebook as cb
+from . import quant
+from .kernels import _launch
+from .kernels.layers import _inference_only
+from .kernels.packed import pack_indices
+
+# FLUX.1-dev attention + FFN linears; suffix match gives 19 x 12 + 38 x 3 = 342 linears.
+FLUX_TARGET_MODULES: List[str] = [
+    "attn.to_q",
+    "attn.to_k",
+    "attn.to_v",
+    "attn.to_out.0",
+    "attn.add_q_proj",
+    "attn.add_k_proj",
+    "attn.add_v_proj",
+    "attn.to_add_out",
+    "ff.net.0.proj",
+    "ff.net.2",
+    "ff_context.net.0.proj",
+    "ff_context.net.2",
+]
+
+_FUSED_RANKS = (1, 2, 4, 8, 16)
+
+
+class TwinCodebook(nn.Module):
+    """Holds the deterministic pools as non-persistent buffers (never saved)."""
+
+    def __init__(self, block_size: int = cb.BLOCK_SIZE, n_bits: int = cb.N_BITS,
+                 sigma_a: Sequence[float] = cb.SIGMA_A, sigma_b: Sequence[float] = cb.SIGMA_B):
+        super().__init__()
+        pool_a, pool_b = cb.twin_pools(block_size, n_bits, sigma_a, sigma_b)
+        self.block_size = block_size
+        self.n_bits = n_bits
+        self.sigma_a = tuple(float(s) for s in sigma_a)
+        self.sigma_b = tuple(float(s) for s in sigma_b)
+        self.register_buffer("pool_a", pool_a, persistent=False)
+        self.register_buffer("pool_b", pool_b, persistent=False)
+        self.register_buffer("proj", cb.projection_matrix(block_size, n_bits), persistent=False)
+        self.lut = cb.kernel_lut(pool_a, pool_b)
+
+    def decode(self, indices: torch.Tensor, shape, side: str, device=None) -> torch.Tensor:
+        """fp32 factor decoded on a CUDA device (bit-identical to the reference decode)."""
+        pool = self.pool_a if side == "A" else self.pool_b
+        return quant.decode(indices, shape, pool, device=device)
+
+
+class LitheLinear(nn.Module):
+    """y = W x + (B_hat A_hat x) * alpha / r with A_hat, B_hat on the Hadamard lattice."""
+
+    def __init__(self, base: nn.Linear, codebook: TwinCodebook, rank: int = 16, alpha: Optional[float] = None,
+                 requantize_every: int = 10, drift_tau: Optional[float] = None):
+        super().__init__()
+        self.base = base
+        for p in self.base.parameters():
+            p.requires_grad_(False)
+        self.in_features = base.in_features
+        self.out_features = base.out_features
+        self.rank = rank
+        self.alpha = float(rank if alpha is None else alpha)
+        self.scaling = self.alpha / rank
+        self.requantize_every = max(1, int(requantize_every))
+        self.drift_tau = drift_tau
+        self.__dict__["codebook"] = codebook
+        device = base.weight.device
+        self.lora_A = nn.Parameter(torch.empty(rank, self.in_features, device=device, dtype=torch.float32),
+                                   requires_grad=False)
+        self.lora_B = nn.Parameter(torch.zeros(self.out_features, rank, device=device, dtype=torch.float32),
+                                   requires_grad=False)
+        nn.init.kaiming_uniform_(self.lora_A, a=math.sqrt(5))
+        self._frozen = False
+        self._words: Optional[torch.Tensor] = None
+        self._ids: Optional[torch.Tensor] = None
+        self._cache: Optional[tuple] = None
+        self._idx = None
+
+    @property
+    def fused(self) -> bool:
+        """True when the forward runs the fused decode+SGMV kernel for this shape."""
+        return (self.rank in _FUSED_RANKS and self.in_features % 64 == 0 and self.out_features % 8 == 0
+                and (self.out_features * self.rank) % 64 == 0)
+
+    @torch.no_grad()
+    def load_indices(self, idx_a: torch.Tensor, idx_b: torch.Tensor) -> None:
+        """Freeze the module to the factors named by the index streams (L, nA) / (L, nB)."""
+        ia, ib = quant.as_index_array(idx_a), quant.as_index_array(idx_b)
+        na, nb = quant.num_blocks(self.lora_A.shape), quant.num_blocks(self.lora_B.shape)
+        if ia.ndim != 2 or ib.ndim != 2 or ia.shape[1] != na or ib.shape[1] != nb or ia.shape[0] != ib.shape[0]:
+            raise ValueError(f"index streams must be (L, {na}) and (L, {nb})")
+        dev = self.base.weight.device
+        stream = np.concatenate([ia.T.reshape(-1), ib.T.reshape(-1)])
+        words = pack_indices(stream).view(torch.int64)
+        if words.numel() % 2:
+            words = torch.cat([words, words.new_zeros(1)])
+        self._words = words.to(dev)
+        self._levels = ia.shape[0]
+        self._na = na
+        self._ids = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._idx = (ia, ib)
+        self._cache = None
+        self._frozen = True
+
+    def decoded_factors(self):
+        """(A_hat, B_hat) float32 as used by the forward pass, decoded on the GPU."""
+        if not self._frozen:
+            raise RuntimeError("no indices loaded: call load_indices() (training is not part of lithe_b200)")
+        if self._cache is None:
+            dev = self.base.weight.device
+            a = self.codebook.decode(torch.from_numpy(self._idx[0]), self.lora_A.shape, "A", device=dev)
+            b = self.codebook.decode(torch.from_numpy(self._idx[1]), self.lora_B.shape, "B", device=dev)
+            self._cache = (a, b)
+        return self._cache
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if not self._frozen:
+            raise RuntimeError("LitheLinear has no indices loaded (training is not part of lithe_b200)")
+        out = self.base(x)
+        _inference_only(out)
+        if self.fused and x.dtype == torch.bfloat16 and x.is_cuda:
+            x3 = x.reshape(1, -1, self.in_features).contiguous()
+            out3 = out.view(1, -1, self.out_features)
+            L = self._levels
+            va = _launch.index_view(self._words, 0, L, 0, 0)
+            vb = _launch.index_view(self._words, 0, L, 0, L * self._na)
+            _launch.sgmv_index_(x3, out3, accumulate=True, view_a=va, view_b=vb, n_slots=1, ids=self._ids,
+                                weights=None, rank=self.rank, lut=self.codebook.lut, scaling=self.scaling)
+            return out
+        a_hat, b_hat = self.decoded_factors()
+        delta = nn.functional.linear(nn.functional.linear(x, a_hat.to(x.dtype)), b_hat.to(x.dtype))
+        return out + delta * self.scaling
+
+
+def _match(path: str, targets: Iterable[str]) -> bool:
+    return any(path == t or path.endswith("." + t) for t in targets)
+
+
+def inject_lithe(model: nn.Module, target_modules: Sequence[str] = FLUX_TARGET_MODULES, rank: int = 16,
+                 alpha: Optional[float] = None, requantize_every: int = 10, drift_tau: Optional[float] = None,
+                 codebook: Optional[TwinCodebook] = None) -> Dict[str, LitheLinear]:
+    """Replace every nn.Linear whose path ends with a target suffix by a LitheLinear.
+
+    Returns an ordered {module_path: LitheLinear}; this order defines the index-stream layout.
+    """
+    codebook = codebook if codebook is not None else TwinCodebook()
+    targets = [(name, mod) for name, mod in model.named_modules()
+               if isinstance(mod, nn.Linear) and _match(name, target_modules)]
+    if not targets:
+        raise ValueError("no target linear found; check target_modules")
+    wrapped: Dict[str, LitheLinear] = {}
+    for name, mod in targets:
+        parent_name, _, child = name.rpartition(".")
+        parent = model.get_submodule(parent_name) if parent_name else model
+        layer = LitheLinear(mod, codebook, rank=rank, alpha=alpha, requantize_every=requantize_every,
+                            drift_tau=drift_tau)
+        setattr(parent, child, layer)
+        wrapped[name] = layer
+    return wrapped
+
+
+def lithe_layers(model: nn.Module) -> Dict[str, LitheLinear]:
+    return {n: m for n, m in model.named_modules() if isinstance(m, LitheLinear)}

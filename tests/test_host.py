@@ -1,0 +1,169 @@
+"""Host-side logic of the product package against the oracle (no GPU needed)."""
+import numpy as np
+import pytest
+import torch
+
+from lithe_b200 import codebook as cb
+from lithe_b200 import fileio, quant, serve
+from lithe_b200.kernels import packed
+from lithe_b200.module import FLUX_TARGET_MODULES, _match
+from oracle import codebook_ref, decode_ref
+from tests.helpers import GOLDEN, SMALL, golden_modules, load_golden, random_adapter
+
+
+def test_product_codebook_equals_oracle():
+    assert np.array_equal(cb.integer_codewords(), codebook_ref.integer_table())
+    assert cb.codebook_sha256() == codebook_ref.TABLE_SHA256
+    pa, pb = cb.twin_pools()
+    oa, ob = codebook_ref.twin_pools()
+    assert np.array_equal(pa.numpy().view(np.uint32), oa.view(np.uint32))
+    assert np.array_equal(pb.numpy().view(np.uint32), ob.view(np.uint32))
+    assert np.array_equal(cb.sylvester_hadamard(64), codebook_ref.hadamard(64))
+    assert np.array_equal(cb.sign_table(), codebook_ref.signs())
+    c = cb.codewords().double()
+    ref = torch.from_numpy(codebook_ref.signs().astype(np.float64)) @ \
+        torch.from_numpy(codebook_ref.generator().astype(np.float64)).T / 3.0
+    assert torch.equal(c, ref.float().double())
+
+
+def test_level_lut_matches_golden_and_sigmas():
+    z = load_golden("codebook.npz")
+    pa, pb = cb.twin_pools()
+    assert np.array_equal(cb.level_lut(pa), z["lut_a"]) and np.array_equal(cb.level_lut(pb), z["lut_b"])
+    assert np.array_equal(cb.lut_from_sigmas(cb.SIGMA_A), z["lut_a"])
+    assert np.array_equal(cb.lut_from_sigmas(cb.SIGMA_B), z["lut_b"])
+    lut = cb.kernel_lut(pa, pb)
+    assert lut.shape == (2, 3, 10) and lut.dtype == np.float32
+
+
+def test_level_lut_bf16_pools_reproduce_pool_values():
+    pa, _ = cb.twin_pools()
+    p16 = pa.to(torch.bfloat16)
+    lut = cb.level_lut(p16)
+    pc = cb.popcount_table()
+    for level in range(3):
+        assert torch.equal(torch.from_numpy(lut[level][pc]), p16[level].float())
+
+
+def test_level_lut_rejects_non_hadamard_pools():
+    pa, _ = cb.twin_pools()
+    bad = pa.clone()
+    bad[1, 7, 3] *= 1.5
+    with pytest.raises(ValueError):
+        cb.level_lut(bad)
+    with pytest.raises(ValueError):
+        cb.level_lut(torch.zeros(3, 512, 32))
+
+
+def test_pack_unpack_product_vs_oracle():
+    rng = np.random.default_rng(7)
+    for n in (1, 6, 7, 8, 700, 1001):
+        v = rng.integers(0, 512, n)
+        w = packed.pack_indices(v)
+        assert w.dtype == torch.uint64 and w.numel() == -(-n // 7)
+        assert np.array_equal(w.view(torch.int64).numpy().view(np.uint64), decode_ref.pack9(v))
+        assert np.array_equal(packed.unpack_indices(w, n).numpy(), v)
+    with pytest.raises(ValueError):
+        packed.pack_indices([512])
+
+
+def test_layout_and_stream_vs_oracle():
+    ad = random_adapter(SMALL, rank=16, seed=5)
+    words, lay = packed.pack_adapter(ad)
+    olay = decode_ref.layout(ad.modules)
+    assert lay.a_off == olay.a_off and lay.b_off == olay.b_off
+    assert np.array_equal(lay.sides.numpy(), olay.sides) and lay.num_words == olay.num_words
+    assert np.array_equal(packed.flat_indices(ad, lay), decode_ref.stream(ad.indices, olay))
+    shapes = ([(3072, 9216)] * 76 + [(3072, 18432)] * 38 + [(3072, 3072)] * 38 + [(3072, 12288)] * 38
+              + [(12288, 3072)] * 38 + [(3072, 21504)] * 38 + [(15360, 3072)] * 38)
+    mods = [{"name": f"m{i}", "shape_a": [16, a], "shape_b": [b, 16]} for i, (a, b) in enumerate(shapes)]
+    k304 = packed.PackedLayout.from_modules(mods)
+    assert k304.num_indices == 3_589_632 and k304.num_words * 8 == 4_102_440
+
+
+def test_blockify_roundtrip():
+    w = torch.randn(5, 13)
+    b = quant.blockify(w)
+    assert b.shape == (2, 64) and quant.num_blocks(w.shape) == 2
+    assert torch.equal(quant.unblockify(b, w.shape), w)
+    with pytest.raises(ValueError):
+        quant.as_index_array(np.array([[0, 512]]))
+
+
+def test_lithe_file_from_reference_loads():
+    z = load_golden("small_lithe.npz")
+    ad = fileio.load_lithe(GOLDEN / "small.lithe")
+    assert ad.modules == golden_modules(z) and ad.rank == int(z["rank"]) and ad.alpha == float(z["alpha"])
+    for m in ad.modules:
+        for s in ("A", "B"):
+            assert np.array_equal(ad.indices[m["name"]][s], z[f"idx/{m['name']}/{s}"])
+    assert fileio.read_header(GOLDEN / "small.lithe")["payload_sha256"] == \
+        __import__("json").loads(str(z["header"]))["payload_sha256"]
+
+
+def test_lithe_file_roundtrip_and_corruption(tmp_path):
+    ad = random_adapter(SMALL, rank=8, seed=2, alpha=4.0)
+    p = tmp_path / "a.lithe"
+    size = fileio.save_lithe(p, ad)
+    assert size == p.stat().st_size
+    back = fileio.load_lithe(p)
+    assert back.rank == 8 and back.alpha == 4.0 and back.modules == ad.modules
+    for name in ad.indices:
+        for s in ("A", "B"):
+            assert np.array_equal(back.indices[name][s], ad.indices[name][s])
+    data = bytearray(p.read_bytes())
+    bad = tmp_path / "bad_magic.lithe"
+    bad.write_bytes(b"NOTLITHE" + bytes(data[8:]))
+    with pytest.raises(ValueError):
+        fileio.load_lithe(bad)
+    trunc = tmp_path / "trunc.lithe"
+    trunc.write_bytes(bytes(data[:-20]))
+    with pytest.raises(ValueError):
+        fileio.load_lithe(trunc)
+    # same indices under a different payload digest -> checksum error
+    hdr = fileio.read_header(p)
+    other = random_adapter(SMALL, rank=8, seed=3, alpha=4.0)
+    q = tmp_path / "other.lithe"
+    fileio.save_lithe(q, other)
+    qd = q.read_bytes()
+    n_q = int.from_bytes(qd[8:12], "little")
+    n_p = int.from_bytes(bytes(data[8:12]), "little")
+    spliced = tmp_path / "spliced.lithe"
+    spliced.write_bytes(bytes(data[: 12 + n_p]) + qd[12 + n_q:])
+    with pytest.raises(ValueError):
+        fileio.load_lithe(spliced)
+    assert hdr["num_indices"] == ad.num_indices
+
+
+def test_router_and_parse_route():
+    r = serve.Router()
+    r.set([[(0, 1.0)], [(2, 1.0)], [], [(1, 0.6), (2, 0.4)]])
+    assert r.ids.tolist() == [[0, -1], [2, -1], [-1, -1], [1, 2]]
+    assert r.weights[3].tolist() == pytest.approx([0.6, 0.4])
+    with pytest.raises(ValueError):
+        r.set([[(0, -0.5)]])
+    assert serve.parse_route("1") == [(1, 1.0)]
+    assert serve.parse_route("0:0.6,2:0.4") == [(0, 0.6), (2, 0.4)]
+    assert serve.parse_route("none") == []
+
+
+def test_router_columns_fold_weights_and_scales():
+    r = serve.Router()
+    r.set([[(0, 1.0)], [], [(1, 0.6), (2, 0.4)]])
+    cols = r.columns(torch.device("cpu"), (2.0, 0.5, 1.0))
+    assert len(cols) == 2
+    assert cols[0][0].tolist() == [0, -1, 1] and cols[0][1].tolist() == pytest.approx([2.0, 0.0, 0.3])
+    assert cols[1][0].tolist() == [-1, -1, 2] and cols[1][1].tolist() == pytest.approx([0.0, 0.0, 0.4])
+    r.set([[(3, 1.0)]])
+    with pytest.raises(ValueError):
+        r.columns(torch.device("cpu"), (1.0, 1.0))
+
+
+def test_flux_target_count():
+    names = []
+    for i in range(19):
+        names += [f"transformer_blocks.{i}.{t}" for t in FLUX_TARGET_MODULES]
+    for i in range(38):
+        names += [f"single_transformer_blocks.{i}.attn.{t}" for t in ("to_q", "to_k", "to_v")]
+        names += [f"single_transformer_blocks.{i}.{t}" for t in ("proj_mlp", "proj_out", "norm.linear")]
+    assert sum(_match(n, FLUX_TARGET_MODULES) for n in names) == 342
