@@ -288,10 +288,11 @@ def run_lithe(args):
     # ---- end-to-end through the public API with host buffers (pinned), copies timed
     max_in = max(a for a, _ in SHAPES)
     max_out = max(b for _, b in SHAPES)
-    x_host = torch.empty(BATCH * TOKENS * max_in, dtype=torch.bfloat16, pin_memory=True)
-    o_host = torch.empty(BATCH * TOKENS * max_out, dtype=torch.bfloat16, pin_memory=True)
-    x_host.normal_()
-    o_host.normal_().mul_(0.05)
+    if not args.no_e2e:
+        x_host = torch.empty(BATCH * TOKENS * max_in, dtype=torch.bfloat16, pin_memory=True)
+        o_host = torch.empty(BATCH * TOKENS * max_out, dtype=torch.bfloat16, pin_memory=True)
+        x_host.normal_()
+        o_host.normal_().mul_(0.05)
     h2d = sum(BATCH * TOKENS * (a + b) * 2 for a, b in SHAPES)
     d2h = sum(BATCH * TOKENS * b * 2 for _, b in SHAPES)
 
@@ -302,18 +303,20 @@ def run_lithe(args):
             packed_codebook_lora_delta_(outs[i], xs[i], bank, names[i], ids, scaling=1.0)
             o_host[: BATCH * TOKENS * b].view(BATCH, TOKENS, b).copy_(outs[i], non_blocking=True)
 
-    e2e_steps = max(1, min(args.steps, 5))
-    e2e_step()
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    e0.record(stream)
-    for _ in range(e2e_steps):
+    e2e_ms = None
+    if not args.no_e2e:
+        e2e_steps = max(1, min(args.steps, 5))
         e2e_step()
-    e1.record(stream)
-    torch.cuda.synchronize(dev)
-    barrier(world)
-    e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(e2e_steps):
+            e2e_step()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+        barrier(world)
+        e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
     errors = device_errors(dev)
 
     cpu = None
@@ -354,9 +357,10 @@ def run_lithe(args):
                          "algorithmic_bytes_per_launch": sum(alg) / len(alg),
                          "kernel": "lithe::sgmv_index_kernel<16>"},
             "cpu_baseline": cpu,
-            "e2e": {"value": len(SHAPES) * BATCH * TOKENS * world / (e2e_ms / 1000.0), "unit": "tokens/s",
-                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                    "api": "lithe_b200.kernels.packed_codebook_lora_delta_ (C ABI lithe_sgmv_index), pinned host buffers"},
+            "e2e": None if e2e_ms is None else {
+                "value": len(SHAPES) * BATCH * TOKENS * world / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
+                "api": "lithe_b200.kernels.packed_codebook_lora_delta_ (C ABI lithe_sgmv_index), pinned host buffers"},
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "per_shape": shapes_out,
@@ -376,7 +380,16 @@ def main():
     ap.add_argument("--impl", choices=["lithe", "reference"], default="lithe")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--shapes", default="", help="comma list of d_inxd_out to run (default: all four), "
+                    "e.g. 3072x3072 for a single-shape profiling run")
     args = ap.parse_args()
+    if args.shapes:
+        global SHAPES
+        want = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
+        SHAPES = [sh for sh in SHAPES if sh in want]
+        if len(SHAPES) != len(want):
+            raise SystemExit(f"--shapes must be a subset of the FLUX shapes, got {args.shapes}")
     if args.warmup < 3 and args.impl == "lithe":
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":
