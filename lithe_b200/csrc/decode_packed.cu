@@ -28,8 +28,10 @@ struct DecodeParams {
 template <bool kF32>
 __global__ void __launch_bounds__(256) decode_packed_kernel(const __grid_constant__ DecodeParams p) {
     __shared__ float lut_s[2][LITHE_MAX_LEVELS][16];
+    __shared__ DecodeTables tab;
     for (int i = threadIdx.x; i < 2 * LITHE_MAX_LEVELS * 16; i += blockDim.x)
         (&lut_s[0][0][0])[i] = (&p.lut[0][0][0])[i];
+    build_decode_tables(&tab, &p.lut[0][0][0], p.levels, threadIdx.x, blockDim.x);
     __syncthreads();
 
     const int64_t sel = blockIdx.y;
@@ -61,7 +63,8 @@ __global__ void __launch_bounds__(256) decode_packed_kernel(const __grid_constan
         uint32_t k[LITHE_MAX_LEVELS];
         fetch_indices<LITHE_MAX_LEVELS>(view, slot, blk, k, nullptr);
         float v[8];
-        decode_eight<LITHE_MAX_LEVELS>(&lut_s[side][0][0], k, p.levels, half, v);
+        if (p.levels <= 3) decode_eight_fast(&tab, side, k, half, v);
+        else decode_eight<LITHE_MAX_LEVELS>(&lut_s[side][0][0], k, p.levels, half, v);
         char* dst = out + blk * kBlockBytes;
         if constexpr (kF32) {
             const float4 lo = make_float4(v[0], v[1], v[2], v[3]);
@@ -125,6 +128,8 @@ int32_t lithe_decode_packed(const uint64_t* words, int64_t n_blocks, int32_t num
     int32_t rc = check_common(n_blocks, num_levels, lut, out, out_dtype);
     if (rc != LITHE_OK) return rc;
     if (n_blocks > 0 && !words) return fail_arg("words is NULL");
+    if (static_cast<int64_t>(num_levels) * n_blocks > 0xffffffffLL)
+        return fail_unsupported("packed stream positions must fit in 32 bits");
     DecodeParams p{};
     p.bank = words;
     p.slot_stride = 0;
@@ -150,6 +155,8 @@ int32_t lithe_decode_packed_batch(const uint64_t* bank, int64_t slot_stride, int
     if (n_sel < 0 || n_sel > 65535) return fail_arg("n_sel must be in [0, 65535], got %d", n_sel);
     if (n_sel > 0 && (!bank || !slot_ids)) return fail_arg("bank and slot_ids must be non-NULL");
     const int64_t words_needed = (static_cast<int64_t>(num_levels) * n_blocks + 6) / 7;
+    if (static_cast<int64_t>(num_levels) * n_blocks > 0xffffffffLL)
+        return fail_unsupported("packed stream positions must fit in 32 bits");
     if (slot_stride < words_needed)
         return fail_arg("slot_stride %lld is smaller than the stream (%lld words)",
                         (long long)slot_stride, (long long)words_needed);

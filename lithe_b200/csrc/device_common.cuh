@@ -32,9 +32,12 @@ static_assert(hadamard_pattern(1) == 170 && hadamard_pattern(8) == 256 &&
 // (every t with t & 15 == u has the same value).  lut: [level][16] fp32 in shared memory,
 // k[l]: the block's 9-bit index at level l.  Levels are summed 0,1,..,L-1 in fp32, the
 // order of lithe/quant.py:77-80, so the result is bit-identical to the reference decode.
+// This is the general form (any number of levels); decode_eight_fast below is the form the
+// kernels use for L <= 3.
 template <int kMaxLevels>
 __device__ __forceinline__ void decode_eight(const float* __restrict__ lut, const uint32_t* k,
                                              int levels, uint32_t half, float v[8]) {
+    constexpr uint32_t kP[8] = {0u, 170u, 204u, 102u, 240u, 90u, 60u, 150u};   // hadamard_pattern(0..7)
 #pragma unroll
     for (int l = 0; l < kMaxLevels; ++l) {
         if (l < levels) {
@@ -42,10 +45,76 @@ __device__ __forceinline__ void decode_eight(const float* __restrict__ lut, cons
             const float* row = lut + l * 16;
 #pragma unroll
             for (int i = 0; i < 8; ++i) {
-                const float c = row[__popc(kk ^ hadamard_pattern(i))];
+                const float c = row[__popc(kk ^ kP[i])];
                 v[i] = (l == 0) ? c : v[i] + c;
             }
         }
+    }
+}
+static_assert(hadamard_pattern(0) == 0 && hadamard_pattern(1) == 170 && hadamard_pattern(2) == 204 &&
+              hadamard_pattern(3) == 102 && hadamard_pattern(4) == 240 && hadamard_pattern(5) == 90 &&
+              hadamard_pattern(6) == 60 && hadamard_pattern(7) == 150, "decode_eight pattern table");
+
+// Shared-memory tables of the fast decode (built once per CTA by build_decode_tables).
+//
+// With u = 8h + i, bit 0 of P(u) is 0, bit 8 is h and bits 1..7 are Q(i) = P(i) >> 1, so
+//   n(k, u) = popc((k ^ P(u)) & 511) = (k & 1) + (((k >> 8) & 1) ^ h) + popc(((k >> 1) & 127) ^ Q(i)).
+// pc[l][m] packs, for m = (k >> 1) & 127, the eight terms popc(m ^ Q(i)) as 16-bit fields
+// already scaled by 4 * {100, 10, 1}[l]; adding the three levels' words gives, field by
+// field, the byte offset of entry n0*100 + n1*10 + n2 of lut3, which holds the fp32 sum
+// (lut[0][n0] + lut[1][n1]) + lut[2][n2] -- the reference's summation order.
+struct DecodeTables {
+    uint4 pc[3][128];
+    float lut3[2][1000];
+};
+
+__device__ __forceinline__ void build_decode_tables(DecodeTables* t, const float* lut /*[2][4][16]*/,
+                                                    int levels, int tid, int nthreads) {
+    constexpr uint32_t kQ[8] = {0u, 85u, 102u, 51u, 120u, 45u, 30u, 75u};
+    for (int e = tid; e < 3 * 128; e += nthreads) {
+        const int l = e >> 7;
+        const uint32_t m = static_cast<uint32_t>(e & 127);
+        const uint32_t scale = l == 0 ? 400u : (l == 1 ? 40u : 4u);
+        uint32_t f[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) f[i] = scale * static_cast<uint32_t>(__popc(m ^ kQ[i]));
+        t->pc[l][m] = make_uint4(f[0] | (f[1] << 16), f[2] | (f[3] << 16), f[4] | (f[5] << 16), f[6] | (f[7] << 16));
+    }
+    for (int e = tid; e < 2000; e += nthreads) {
+        const int side = e >= 1000;
+        const int r = e - side * 1000;
+        const float* L = lut + side * 64;
+        float v = L[r / 100];
+        if (levels > 1) v = __fadd_rn(v, L[16 + (r / 10) % 10]);
+        if (levels > 2) v = __fadd_rn(v, L[32 + r % 10]);
+        t->lut3[side][r] = v;
+    }
+}
+static_assert((hadamard_pattern(1) >> 1) == 85 && (hadamard_pattern(2) >> 1) == 102 &&
+              (hadamard_pattern(3) >> 1) == 51 && (hadamard_pattern(4) >> 1) == 120 &&
+              (hadamard_pattern(5) >> 1) == 45 && (hadamard_pattern(6) >> 1) == 30 &&
+              (hadamard_pattern(7) >> 1) == 75, "pc table patterns");
+
+// Fast decode for L <= 3 (indices of absent levels must be 0): the 8 values of one half
+// block, bit-identical to decode_eight.
+__device__ __forceinline__ void decode_eight_fast(const DecodeTables* __restrict__ t, int side, const uint32_t* k,
+                                                  uint32_t half, float v[8]) {
+    uint32_t base = 0;
+    uint4 f[3];
+#pragma unroll
+    for (int l = 0; l < 3; ++l) {
+        const uint32_t scale = l == 0 ? 400u : (l == 1 ? 40u : 4u);
+        base += scale * ((k[l] & 1u) + (((k[l] >> 8) & 1u) ^ half));
+        f[l] = t->pc[l][(k[l] >> 1) & 127u];
+    }
+    const uint32_t bb = base | (base << 16);
+    const char* lut = reinterpret_cast<const char*>(t->lut3[side]);
+    const uint32_t w[4] = {f[0].x + f[1].x + f[2].x + bb, f[0].y + f[1].y + f[2].y + bb,
+                           f[0].z + f[1].z + f[2].z + bb, f[0].w + f[1].w + f[2].w + bb};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        v[2 * j] = *reinterpret_cast<const float*>(lut + (w[j] & 0xffffu));
+        v[2 * j + 1] = *reinterpret_cast<const float*>(lut + (w[j] >> 16));
     }
 }
 
@@ -82,15 +151,19 @@ template <int kMaxLevels>
 __device__ __forceinline__ void fetch_indices(const IndexView& v, int64_t slot, int64_t blk,
                                               uint32_t k[kMaxLevels], int32_t* err) {
     if (v.format == LITHE_IDX_PACKED9) {
+        // positions inside one slot fit in 32 bits (checked on the host)
         const uint64_t* w = static_cast<const uint64_t*>(v.base) + slot * v.slot_stride;
-        const uint64_t p0 = static_cast<uint64_t>(v.offset + static_cast<int64_t>(v.levels) * blk);
+        const uint32_t p0 = static_cast<uint32_t>(v.offset) + static_cast<uint32_t>(v.levels) * static_cast<uint32_t>(blk);
+        const uint32_t w0 = p0 / 7u;
+        const uint32_t r0 = p0 - 7u * w0;
+        const uint64_t a = ldg_nc_u64(w + w0);
+        // the block's last index may sit in the next word; read it only then (never past the stream)
+        const uint64_t b = (r0 + static_cast<uint32_t>(v.levels) > 7u) ? ldg_nc_u64(w + w0 + 1) : 0ull;
 #pragma unroll
         for (int l = 0; l < kMaxLevels; ++l) {
             if (l < v.levels) {
-                const uint64_t p = p0 + l;
-                const uint64_t wi = p / 7u;
-                const uint32_t sh = 9u * static_cast<uint32_t>(p - wi * 7u);
-                k[l] = static_cast<uint32_t>(ldg_nc_u64(w + wi) >> sh) & 511u;
+                const uint32_t r = r0 + l;
+                k[l] = static_cast<uint32_t>((r < 7u ? (a >> (9u * r)) : (b >> (9u * (r - 7u))))) & 511u;
             } else {
                 k[l] = 0;
             }
@@ -187,28 +260,6 @@ __device__ __forceinline__ void tma_load_3d(void* dst, const CUtensorMap* map, u
         " [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(smem_u32(dst)),
         "l"(reinterpret_cast<uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
         : "memory");
-}
-
-__device__ __forceinline__ void tma_store_3d(const CUtensorMap* map, const void* src, int32_t c0,
-                                             int32_t c1, int32_t c2) {
-    asm volatile(
-        "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%2, %3, %4}], [%1];" ::"l"(
-            reinterpret_cast<uint64_t>(map)),
-        "r"(smem_u32(src)), "r"(c0), "r"(c1), "r"(c2)
-        : "memory");
-}
-
-__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
-
-template <int N>
-__device__ __forceinline__ void bulk_wait_read() {
-    asm volatile("cp.async.bulk.wait_group.read %0;" ::"n"(N) : "memory");
-}
-
-__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
-
-__device__ __forceinline__ void fence_proxy_async_smem() {
-    asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* map) {

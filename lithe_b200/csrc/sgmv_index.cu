@@ -7,8 +7,9 @@
 //
 //   work unit  = (sample b, 64-token tile); CTA i owns a contiguous range of units.
 //   per unit   = d_in/64 "x chunks" (64x64 bf16 activation tiles, TMA, 128B swizzle)
-//              + d_out/64 "out chunks" (64x64 bf16 output tiles, TMA load + TMA store).
-//   warps      = 4 consumer warps (16 tokens each), 1 TMA producer warp, 2 decoder warps.
+//              + d_out/64 "out chunks" (64x64 bf16 base-output tiles, TMA load; the updated
+//                values go back with coalesced 16-byte stores straight from registers).
+//   warps      = 4 consumer warps (16 tokens each), 1 TMA producer warp, 4 decoder warps.
 //   pipeline   = kStages shared-memory stages; each stage holds one 8 KB tile and the
 //                512 B decoded factor chunk that goes with it; full barrier = TMA bytes +
 //                one decoder arrival, empty barrier = one arrival per consumer warp.
@@ -25,7 +26,7 @@
 // Expand (per out chunk): the 64 output columns of a chunk are 16 distinct "logical"
 // columns repeated 4 times, so delta = h . B^T is 2 mma.m16n8k16 (n = 16 logical
 // columns, k = 16 ranks) and each thread adds its 2 results to 8 output values per row.
-// The bf16 output tile is read-modified-written in shared memory and stored by TMA.
+// The stage is released as soon as the tile is in registers; the stores need no proxy fence.
 #include "device_common.cuh"
 #include "host_common.h"
 
@@ -34,7 +35,7 @@ namespace lithe {
 constexpr int kBM = 64;                 // tokens per work unit
 constexpr int kChunk = 64;              // columns per chunk
 constexpr int kConsumerWarps = 4;
-constexpr int kDecodeWarps = 2;
+constexpr int kDecodeWarps = 4;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kFirstDecodeWarp = kConsumerWarps + 1;
 constexpr int kThreads = 32 * (kConsumerWarps + 1 + kDecodeWarps);
@@ -42,7 +43,7 @@ constexpr int kStages = 16;
 constexpr int kTileBytes = kBM * kChunk * 2;      // 8192
 constexpr int kFactBytes = 16 * 16 * 2;           // 512
 constexpr int kLutFloats = 2 * LITHE_MAX_LEVELS * 16;
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * (kTileBytes + kFactBytes) +
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * (kTileBytes + kFactBytes) + sizeof(DecodeTables) +
                               2 * kStages * sizeof(uint64_t) + kLutFloats * sizeof(float) + 16;
 
 struct SgmvParams {
@@ -57,6 +58,7 @@ struct SgmvParams {
     int32_t a_blocks_per_row;   // d_in / 64
     int32_t b_blocks;           // d_out * rank / 64
     float scaling;
+    __nv_bfloat16* out;
     float lut[2][LITHE_MAX_LEVELS][16];
 };
 
@@ -90,77 +92,132 @@ __device__ __forceinline__ uint32_t add_bf16x2(uint32_t w, float dlo, float dhi)
 // ---------------------------------------------------------------------------------------
 // Decoder warps
 // ---------------------------------------------------------------------------------------
-// A chunk c: rows r = 0..15 (rows >= kRank are zero), values u = 0..15 in natural order.
-// Lane (r = lane/2, half = lane&1) writes bytes [r*32 + half*16, +16).
+// Indices of the block this lane decodes in chunk c of a unit (A chunk c < nx, else B
+// chunk c - nx).  Returns false when the lane's values are structurally zero (rank rows
+// >= kRank, or past the last B block).
 template <int kRank>
-__device__ __forceinline__ void decode_a_chunk(const SgmvParams& p, const float* lut_a, int64_t slot, int c,
-                                               uint8_t* fact, int lane) {
-    const int r = lane >> 1;
-    const uint32_t half = lane & 1;
-    uint4 q = make_uint4(0, 0, 0, 0);
-    if (r < kRank) {
-        uint32_t k[LITHE_MAX_LEVELS];
-        fetch_indices<LITHE_MAX_LEVELS>(p.ia, slot, static_cast<int64_t>(r) * p.a_blocks_per_row + c, k, p.err);
-        float v[8];
-        decode_eight<LITHE_MAX_LEVELS>(lut_a, k, p.ia.levels, half, v);
-        q = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                       pack_bf16x2(v[6], v[7]));
+__device__ __forceinline__ bool chunk_indices(const SgmvParams& p, const Unit& un, int c, int lane,
+                                              uint32_t k[LITHE_MAX_LEVELS]) {
+    const int row = lane >> 1;          // A: rank row r; B: logical column n
+    const int half = lane & 1;
+    if (c < un.nx) {
+        if (row >= kRank) return false;
+        fetch_indices<LITHE_MAX_LEVELS>(p.ia, un.slot, static_cast<int64_t>(row) * p.a_blocks_per_row + c, k, p.err);
+        return true;
     }
-    sts128(fact + r * 32 + half * 16, q);
+    constexpr int kPer = 16 / kRank;
+    const int G = (16 * (c - un.nx) + row) / kPer;
+    if (G >= p.b_blocks || 8 * half >= kRank) return false;
+    fetch_indices<LITHE_MAX_LEVELS>(p.ib, un.slot, G, k, p.err);
+    return true;
 }
 
-// B chunk j: 16 logical columns n, each a 16-rank vector stored with the rank order
+__device__ __forceinline__ void decode_values(const SgmvParams& p, const DecodeTables* tab, const float* lut_s,
+                                              int side, const uint32_t* k, uint32_t half, float v[8]) {
+    if (p.ia.levels <= 3) decode_eight_fast(tab, side, k, half, v);
+    else decode_eight<LITHE_MAX_LEVELS>(lut_s + side * LITHE_MAX_LEVELS * 16, k, p.ia.levels, half, v);
+}
+
+// A chunk: rows r = 0..15 (rows >= kRank are zero), values u = 0..15 in natural order.
+// Lane (r = lane/2, half = lane&1) writes bytes [r*32 + half*16, +16).
+// B chunk: 16 logical columns n, each a 16-rank vector stored with the rank order
 // [0,1,8,9, 2,3,10,11, 4,5,12,13, 6,7,14,15] so that an mma B fragment is one 8-byte read.
 // Logical column N = 16j + n covers the output columns of block G = N / per, pattern
 // offset e = N % per (per = 16/kRank): B[o, r] = w_G[kRank*e + r].
 template <int kRank>
-__device__ __forceinline__ void decode_b_chunk(const SgmvParams& p, const float* lut_b, int64_t slot, int j,
-                                               uint8_t* fact, int lane) {
+__device__ __forceinline__ void decode_chunk(const SgmvParams& p, const DecodeTables* tab, const float* lut_s,
+                                             const Unit& un, int c, bool live, const uint32_t* k, uint8_t* fact,
+                                             int lane) {
+    const int row = lane >> 1;
+    const uint32_t half = lane & 1;
+    if (c < un.nx) {
+        uint4 q = make_uint4(0, 0, 0, 0);
+        if (live) {
+            float v[8];
+            decode_values(p, tab, lut_s, 0, k, half, v);
+            q = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                           pack_bf16x2(v[6], v[7]));
+        }
+        sts128(fact + row * 32 + half * 16, q);
+        return;
+    }
     constexpr int kPer = 16 / kRank;
-    const int n = lane >> 1;
-    const int half = lane & 1;      // ranks 8*half .. 8*half+7
-    const int N = 16 * j + n;
-    const int G = N / kPer;
-    const int e = N - G * kPer;
     float val[8];
 #pragma unroll
     for (int i = 0; i < 8; ++i) val[i] = 0.f;
-    const bool live = (G < p.b_blocks) && (8 * half < kRank);
     if (live) {
-        uint32_t k[LITHE_MAX_LEVELS];
-        fetch_indices<LITHE_MAX_LEVELS>(p.ib, slot, G, k, p.err);
-        const int u0 = kRank * e + 8 * half;    // first pattern position needed
+        const int e = (16 * (c - un.nx) + row) % kPer;
+        const int u0 = kRank * e + 8 * static_cast<int>(half);   // first pattern position needed
         float v[8];
-        decode_eight<LITHE_MAX_LEVELS>(lut_b, k, p.ib.levels, static_cast<uint32_t>(u0 >> 3), v);
-        const int off = u0 & 7;
+        decode_values(p, tab, lut_s, 1, k, static_cast<uint32_t>(u0 >> 3), v);
+        if constexpr (kRank == 16) {
 #pragma unroll
-        for (int i = 0; i < 8; ++i)
-            if (8 * half + i < kRank) val[i] = v[(off + i) & 7];
+            for (int i = 0; i < 8; ++i) val[i] = v[i];
+        } else {
+            const int off = u0 & 7;
+#pragma unroll
+            for (int i = 0; i < 8; ++i)
+                if (8 * static_cast<int>(half) + i < kRank) val[i] = v[(off + i) & 7];
+        }
     }
-    uint32_t* dst = reinterpret_cast<uint32_t*>(fact + n * 32);
+    uint32_t* dst = reinterpret_cast<uint32_t*>(fact + row * 32);
 #pragma unroll
     for (int i = 0; i < 8; i += 2) dst[(i >> 1) * 2 + half] = pack_bf16x2(val[i], val[i + 1]);
 }
 
+// Decoder warp d fills the factor chunk of every pipeline position pos with
+// pos % kDecodeWarps == d.  The indices of its next chunk are fetched before it waits for
+// and decodes the current one, so the index-load latency overlaps the decode.
 template <int kRank>
-__device__ void run_decoder(int d, int lane, const SgmvParams& p, uint8_t* facts, const float* lut_s,
-                            uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin, int u_end) {
-    uint32_t pos = 0;
-    for (int u = u_begin; u < u_end; ++u) {
-        const Unit un = unit_at(p, u);
-        const int n = un.nx + un.no;
-        for (int c = 0; c < n; ++c, ++pos) {
-            if (static_cast<int>(pos % kDecodeWarps) != d) continue;
-            const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
-            if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return;
-            if (un.active) {
-                uint8_t* fact = facts + s * kFactBytes;
-                if (c < un.nx) decode_a_chunk<kRank>(p, lut_s, un.slot, c, fact, lane);
-                else decode_b_chunk<kRank>(p, lut_s + LITHE_MAX_LEVELS * 16, un.slot, c - un.nx, fact, lane);
-            }
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&full[s]);
+__device__ void run_decoder(int d, int lane, const SgmvParams& p, uint8_t* facts, const DecodeTables* tab,
+                            const float* lut_s, uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin,
+                            int u_end) {
+    int u = u_begin, c = 0;          // cursor: unit, chunk within the unit
+    uint32_t pos = 0;                // pipeline position of (u, c)
+    Unit un;
+    // Move to the next position owned by this warp (the current one when first == true).
+    auto seek = [&](bool first) {
+        if (!first) {
+            ++c;
+            ++pos;
         }
+        while (u < u_end) {
+            if (first || c == 0) un = unit_at(p, u);
+            first = false;
+            const int n = un.nx + un.no;
+            if (c < n) {
+                const int skip = (d - static_cast<int>(pos % kDecodeWarps) + kDecodeWarps) % kDecodeWarps;
+                if (c + skip < n) {
+                    c += skip;
+                    pos += skip;
+                    return true;
+                }
+                pos += n - c;
+            }
+            ++u;
+            c = 0;
+        }
+        return false;
+    };
+    bool have = seek(true);
+    uint32_t k_next[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
+    bool live_next = have && un.active && chunk_indices<kRank>(p, un, c, lane, k_next);
+    while (have) {
+        const Unit cur = un;
+        const int cc = c;
+        const uint32_t cpos = pos;
+        uint32_t k[LITHE_MAX_LEVELS];
+#pragma unroll
+        for (int l = 0; l < LITHE_MAX_LEVELS; ++l) k[l] = k_next[l];
+        const bool live = live_next;
+        have = seek(false);
+        live_next = have && un.active && chunk_indices<kRank>(p, un, c, lane, k_next);
+
+        const uint32_t s = cpos % kStages, ph = (cpos / kStages) & 1u;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return;
+        if (cur.active) decode_chunk<kRank>(p, tab, lut_s, cur, cc, live, k, facts + s * kFactBytes, lane);
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&full[s]);
     }
 }
 
@@ -196,148 +253,164 @@ __device__ uint32_t run_producer(const SgmvParams& p, const CUtensorMap* tmx, co
 // ---------------------------------------------------------------------------------------
 // Consumer warps
 // ---------------------------------------------------------------------------------------
-// Apply the two expand results (c0 -> logical column 2t, c1 -> 2t+1 of n8 tile q) to the
-// thread's output values of one row, in the swizzled smem tile.
+// Add the two expand results (c0 -> logical column 2t, c1 -> 2t+1 of n8 tile q) to the 8
+// contiguous output values a thread owns per row (ranks 16 and 8).
 template <int kRank>
-__device__ __forceinline__ void rmw_row(uint8_t* row, int g, int q, int t4, float c0, float c1, bool acc) {
-    if constexpr (kRank >= 8) {
-        uint8_t* a = row + ((((q << 2) + t4) ^ g) << 4);
-        uint4 v = acc ? lds128(a) : make_uint4(0, 0, 0, 0);
-        if constexpr (kRank == 16) {   // columns: c0 c0 c0 c0 c1 c1 c1 c1
-            v.x = add_bf16x2(v.x, c0, c0);
-            v.y = add_bf16x2(v.y, c0, c0);
-            v.z = add_bf16x2(v.z, c1, c1);
-            v.w = add_bf16x2(v.w, c1, c1);
-        } else {                       // columns: c0 c1 c0 c1 ...
-            v.x = add_bf16x2(v.x, c0, c1);
-            v.y = add_bf16x2(v.y, c0, c1);
-            v.z = add_bf16x2(v.z, c0, c1);
-            v.w = add_bf16x2(v.w, c0, c1);
-        }
-        sts128(a, v);
-    } else {
-        constexpr int kPer = 16 / kRank;            // logical columns per block
-        const int nl = 8 * q + 2 * t4;              // local logical column of c0
-        const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
-#pragma unroll
-        for (int pp = 0; pp < 4; ++pp) {
-            const int col = base + pp * kPer;       // even: c0 at col, c1 at col + 1
-            uint32_t* a = reinterpret_cast<uint32_t*>(row + ((((col >> 3) ^ g)) << 4) + (col & 7) * 2);
-            const uint32_t w = acc ? *a : 0u;
-            *a = add_bf16x2(w, c0, c1);
-        }
+__device__ __forceinline__ uint4 add_delta8(uint4 v, float c0, float c1) {
+    if constexpr (kRank == 16) {   // columns: c0 c0 c0 c0 c1 c1 c1 c1
+        v.x = add_bf16x2(v.x, c0, c0);
+        v.y = add_bf16x2(v.y, c0, c0);
+        v.z = add_bf16x2(v.z, c1, c1);
+        v.w = add_bf16x2(v.w, c1, c1);
+    } else {                       // columns: c0 c1 c0 c1 ...
+        v.x = add_bf16x2(v.x, c0, c1);
+        v.y = add_bf16x2(v.y, c0, c1);
+        v.z = add_bf16x2(v.z, c0, c1);
+        v.w = add_bf16x2(v.w, c0, c1);
     }
+    return v;
 }
 
 template <int kRank>
-__device__ void run_consumer(int w, int lane, const SgmvParams& p, const CUtensorMap* tmo_st, uint8_t* tiles,
-                             const uint8_t* facts, uint64_t* full, uint64_t* empty, volatile int* abort,
-                             int u_begin, int u_end) {
+__device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tiles, const uint8_t* facts,
+                             uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin, int u_end) {
     const int g = lane >> 2, t4 = lane & 3;
     const int r0 = 16 * w + g;           // rows r0 and r0 + 8 of the 64-token tile
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+    const bool accum = p.accumulate != 0;
     uint32_t pos = 0;
-    int pending = -1;                    // stage whose TMA store may still be reading smem
     for (int u = u_begin; u < u_end; ++u) {
         const Unit un = unit_at(p, u);
         if (un.nx + un.no == 0) continue;
-        float acc0[4] = {0.f, 0.f, 0.f, 0.f}, acc1[4] = {0.f, 0.f, 0.f, 0.f};
+        // four independent accumulation chains: [rank half][32-column window]
+        float acc[2][2][4];
+#pragma unroll
+        for (int i = 0; i < 16; ++i) (&acc[0][0][0])[i] = 0.f;
         for (int c = 0; c < un.nx; ++c, ++pos) {
             const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
-            if (!mbar_wait(&full[s], ph, abort, p.err)) goto done;
-            {
-                const uint8_t* tile = tiles + s * kTileBytes;
-                const uint8_t* fa = facts + s * kFactBytes;
-                const uint8_t* ra = tile + r0 * 128;
-                const uint8_t* rb = ra + 8 * 128;
-                const uint4 xa0 = lds128(ra + ((t4 ^ g) << 4));
-                const uint4 xa1 = lds128(ra + (((4 + t4) ^ g) << 4));
-                const uint4 xb0 = lds128(rb + ((t4 ^ g) << 4));
-                const uint4 xb1 = lds128(rb + (((4 + t4) ^ g) << 4));
-                const uint4 f0 = lds128(fa + g * 32 + (t4 & 1) * 16);
-                const uint4 f1 = lds128(fa + (g + 8) * 32 + (t4 & 1) * 16);
-                {
-                    const uint32_t a[4] = {xa0.x, xb0.x, xa0.y, xb0.y};
-                    mma_bf16_16816(acc0, a, f0.x, f0.y, acc0);
-                    mma_bf16_16816(acc1, a, f1.x, f1.y, acc1);
-                }
-                {
-                    const uint32_t a[4] = {xa0.z, xb0.z, xa0.w, xb0.w};
-                    mma_bf16_16816(acc0, a, f0.z, f0.w, acc0);
-                    mma_bf16_16816(acc1, a, f1.z, f1.w, acc1);
-                }
-                {
-                    const uint32_t a[4] = {xa1.x, xb1.x, xa1.y, xb1.y};
-                    mma_bf16_16816(acc0, a, f0.x, f0.y, acc0);
-                    mma_bf16_16816(acc1, a, f1.x, f1.y, acc1);
-                }
-                {
-                    const uint32_t a[4] = {xa1.z, xb1.z, xa1.w, xb1.w};
-                    mma_bf16_16816(acc0, a, f0.z, f0.w, acc0);
-                    mma_bf16_16816(acc1, a, f1.z, f1.w, acc1);
-                }
+            if (!mbar_wait(&full[s], ph, abort, p.err)) return;
+            const uint8_t* tile = tiles + s * kTileBytes;
+            const uint8_t* fa = facts + s * kFactBytes;
+            const uint8_t* ra = tile + r0 * 128;
+            const uint8_t* rb = ra + 8 * 128;
+            const uint4 f0 = lds128(fa + g * 32 + (t4 & 1) * 16);
+            const uint4 f1 = lds128(fa + (g + 8) * 32 + (t4 & 1) * 16);
+#pragma unroll
+            for (int win = 0; win < 2; ++win) {
+                const uint4 xa = lds128(ra + (((4 * win + t4) ^ g) << 4));
+                const uint4 xb = lds128(rb + (((4 * win + t4) ^ g) << 4));
+                const uint32_t a0[4] = {xa.x, xb.x, xa.y, xb.y};
+                const uint32_t a1[4] = {xa.z, xb.z, xa.w, xb.w};
+                mma_bf16_16816(acc[0][win], a0, f0.x, f0.y, acc[0][win]);
+                mma_bf16_16816(acc[1][win], a0, f1.x, f1.y, acc[1][win]);
+                mma_bf16_16816(acc[0][win], a1, f0.z, f0.w, acc[0][win]);
+                mma_bf16_16816(acc[1][win], a1, f1.z, f1.w, acc[1][win]);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
-        {
-            const float sc = p.scaling * (p.weights ? __ldg(p.weights + un.b) : 1.0f);
-            const uint32_t ha[4] = {pack_bf16x2(acc0[0] * sc, acc0[1] * sc), pack_bf16x2(acc0[2] * sc, acc0[3] * sc),
-                                    pack_bf16x2(acc1[0] * sc, acc1[1] * sc), pack_bf16x2(acc1[2] * sc, acc1[3] * sc)};
-            const int row_tile0 = un.mt * kBM + 16 * w;
-            const bool rows_live = row_tile0 < p.m;
-            for (int j = 0; j < un.no; ++j, ++pos) {
-                const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
-                if (!mbar_wait(&full[s], ph, abort, p.err)) goto done;
-                uint8_t* tile = tiles + s * kTileBytes;
-                float d0[4] = {0.f, 0.f, 0.f, 0.f}, d1[4] = {0.f, 0.f, 0.f, 0.f};
-                if (un.active) {
-                    const uint8_t* fb = facts + s * kFactBytes;
-                    const uint2 b0 = *reinterpret_cast<const uint2*>(fb + g * 32 + t4 * 8);
-                    const uint2 b1 = *reinterpret_cast<const uint2*>(fb + (g + 8) * 32 + t4 * 8);
-                    mma_bf16_16816(d0, ha, b0.x, b0.y, zero);
-                    mma_bf16_16816(d1, ha, b1.x, b1.y, zero);
-                }
-                uint8_t* ra = tile + r0 * 128;
-                uint8_t* rb = ra + 8 * 128;
-                const bool acc = p.accumulate != 0;
-                rmw_row<kRank>(ra, g, 0, t4, d0[0], d0[1], acc);
-                rmw_row<kRank>(rb, g, 0, t4, d0[2], d0[3], acc);
-                rmw_row<kRank>(ra, g, 1, t4, d1[0], d1[1], acc);
-                rmw_row<kRank>(rb, g, 1, t4, d1[2], d1[3], acc);
-                fence_proxy_async_smem();
-                __syncwarp();
-                if (lane == 0) {
-                    if (rows_live) tma_store_3d(tmo_st, tile + w * (16 * 128), j * kChunk, row_tile0, un.b);
-                    bulk_commit();
-                    bulk_wait_read<1>();
-                    if (pending >= 0) mbar_arrive(&empty[pending]);
-                    pending = static_cast<int>(s);
-                }
-                __syncwarp();
+        const float sc = p.scaling * (p.weights ? __ldg(p.weights + un.b) : 1.0f);
+        float h0[4], h1[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            h0[i] = (acc[0][0][i] + acc[0][1][i]) * sc;
+            h1[i] = (acc[1][0][i] + acc[1][1][i]) * sc;
+        }
+        const uint32_t ha[4] = {pack_bf16x2(h0[0], h0[1]), pack_bf16x2(h0[2], h0[3]), pack_bf16x2(h1[0], h1[1]),
+                                pack_bf16x2(h1[2], h1[3])};
+        const int row0 = un.mt * kBM + r0;                   // token rows row0 and row0 + 8
+        __nv_bfloat16* out_b = p.out + static_cast<int64_t>(un.b) * p.m * p.d_out;
+        for (int j = 0; j < un.no; ++j, ++pos) {
+            const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
+            if (!mbar_wait(&full[s], ph, abort, p.err)) return;
+            const uint8_t* tile = tiles + s * kTileBytes;
+            float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+            if (un.active) {
+                const uint8_t* fb = facts + s * kFactBytes;
+                const uint2 b0 = *reinterpret_cast<const uint2*>(fb + g * 32 + t4 * 8);
+                const uint2 b1 = *reinterpret_cast<const uint2*>(fb + (g + 8) * 32 + t4 * 8);
+                mma_bf16_16816(d[0], ha, b0.x, b0.y, zero);
+                mma_bf16_16816(d[1], ha, b1.x, b1.y, zero);
             }
-            if (lane == 0 && pending >= 0) {
-                bulk_wait_read<0>();
-                mbar_arrive(&empty[pending]);
-                pending = -1;
+            const int col0 = j * kChunk;
+            if constexpr (kRank >= 8) {
+                uint4 v[2][2];          // [n8 tile q][row half]
+#pragma unroll
+                for (int q = 0; q < 2; ++q)
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
+                        const uint4 o = accum ? lds128(tile + (r0 + 8 * hr) * 128 + ((((q << 2) + t4) ^ g) << 4))
+                                              : make_uint4(0, 0, 0, 0);
+                        v[q][hr] = add_delta8<kRank>(o, d[q][2 * hr], d[q][2 * hr + 1]);
+                    }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int row = row0 + 8 * hr;
+                    if (row < p.m) {
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            const int col = col0 + 32 * q + 8 * t4;
+                            if (col < p.d_out)
+                                *reinterpret_cast<uint4*>(out_b + static_cast<int64_t>(row) * p.d_out + col) = v[q][hr];
+                        }
+                    }
+                }
+            } else {
+                constexpr int kPer = 16 / kRank;        // logical columns per block
+                uint32_t v[2][2][4];                    // [q][row half][pp]
+#pragma unroll
+                for (int q = 0; q < 2; ++q) {
+                    const int nl = 8 * q + 2 * t4;      // local logical column of c0
+                    const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr)
+#pragma unroll
+                        for (int pp = 0; pp < 4; ++pp) {
+                            const int col = base + pp * kPer;   // even: c0 at col, c1 at col + 1
+                            const uint32_t o = accum ? *reinterpret_cast<const uint32_t*>(
+                                                           tile + (r0 + 8 * hr) * 128 + (((col >> 3) ^ g) << 4) +
+                                                           (col & 7) * 2)
+                                                     : 0u;
+                            v[q][hr][pp] = add_bf16x2(o, d[q][2 * hr], d[q][2 * hr + 1]);
+                        }
+                }
+                __syncwarp();
+                if (lane == 0) mbar_arrive(&empty[s]);
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int row = row0 + 8 * hr;
+                    if (row < p.m) {
+#pragma unroll
+                        for (int q = 0; q < 2; ++q) {
+                            const int nl = 8 * q + 2 * t4;
+                            const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
+#pragma unroll
+                            for (int pp = 0; pp < 4; ++pp) {
+                                const int col = col0 + base + pp * kPer;
+                                if (col < p.d_out)
+                                    *reinterpret_cast<uint32_t*>(out_b + static_cast<int64_t>(row) * p.d_out + col) =
+                                        v[q][hr][pp];
+                            }
+                        }
+                    }
+                }
             }
-            __syncwarp();
         }
     }
-done:
-    if (lane == 0) bulk_wait_all();
-    __syncwarp();
 }
 
 template <int kRank>
 __global__ void __launch_bounds__(kThreads, 1)
     sgmv_index_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmo_ld,
-                      const __grid_constant__ CUtensorMap tmo_st, const __grid_constant__ SgmvParams p) {
+                      const __grid_constant__ SgmvParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* tiles = base;
     uint8_t* facts = tiles + kStages * kTileBytes;
-    uint64_t* full = reinterpret_cast<uint64_t*>(facts + kStages * kFactBytes);
+    DecodeTables* tab = reinterpret_cast<DecodeTables*>(facts + kStages * kFactBytes);
+    uint64_t* full = reinterpret_cast<uint64_t*>(tab + 1);
     uint64_t* empty = full + kStages;
     float* lut_s = reinterpret_cast<float*>(empty + kStages);
     volatile int* abort = reinterpret_cast<volatile int*>(lut_s + kLutFloats);
@@ -352,6 +425,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         fence_mbar_init();
     }
     for (int i = tid; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
+    build_decode_tables(tab, &p.lut[0][0][0], p.ia.levels, tid, blockDim.x);
     __syncthreads();
 
     const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_units / gridDim.x);
@@ -360,16 +434,15 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     uint32_t issued = 0;
     if (warp < kConsumerWarps) {
-        run_consumer<kRank>(warp, lane, p, &tmo_st, tiles, facts, full, empty, abort, u_begin, u_end);
+        run_consumer<kRank>(warp, lane, p, tiles, facts, full, empty, abort, u_begin, u_end);
     } else if (warp == kProducerWarp) {
         if (lane == 0) {
             prefetch_tmap(&tmx);
             prefetch_tmap(&tmo_ld);
-            prefetch_tmap(&tmo_st);
             issued = run_producer(p, &tmx, &tmo_ld, tiles, full, empty, abort, u_begin, u_end);
         }
     } else {
-        run_decoder<kRank>(warp - kFirstDecodeWarp, lane, p, facts, lut_s, full, empty, abort, u_begin, u_end);
+        run_decoder<kRank>(warp - kFirstDecodeWarp, lane, p, facts, tab, lut_s, full, empty, abort, u_begin, u_end);
     }
     __syncthreads();
     // After an aborted pipeline, let the producer's last TMA loads land before the block's
@@ -386,8 +459,8 @@ __global__ void __launch_bounds__(kThreads, 1)
 }
 
 template <int kRank>
-static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, const CUtensorMap& tmo_st,
-                           const SgmvParams& p, int grid, int device, cudaStream_t stream) {
+static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, const SgmvParams& p, int grid,
+                           int device, cudaStream_t stream) {
     static bool configured[64] = {false};
     auto kern = sgmv_index_kernel<kRank>;
     if (!configured[device]) {
@@ -396,7 +469,7 @@ static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, co
         if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(sgmv_index_kernel)");
         configured[device] = true;
     }
-    kern<<<grid, kThreads, kSmemBytes, stream>>>(tmx, tmo_ld, tmo_st, p);
+    kern<<<grid, kThreads, kSmemBytes, stream>>>(tmx, tmo_ld, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "sgmv_index_kernel launch");
     return LITHE_OK;
@@ -447,6 +520,12 @@ extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate
     rc = check_view(idx_b, "idx_b");
     if (rc != LITHE_OK) return rc;
     if (idx_a->num_levels != idx_b->num_levels) return fail_arg("idx_a and idx_b have different num_levels");
+    {
+        const int64_t nb_a = static_cast<int64_t>(rank) * d_in / 64, nb_b = static_cast<int64_t>(d_out) * rank / 64;
+        if ((idx_a->format == LITHE_IDX_PACKED9 && idx_a->offset + idx_a->num_levels * nb_a > 0xffffffffLL) ||
+            (idx_b->format == LITHE_IDX_PACKED9 && idx_b->offset + idx_b->num_levels * nb_b > 0xffffffffLL))
+            return fail_unsupported("packed stream positions of one slot must fit in 32 bits");
+    }
     if (!lut) return fail_arg("lut is NULL");
     if (n_slots < 0) return fail_arg("n_slots must be >= 0");
     if (batch == 0 || m == 0) return LITHE_OK;
@@ -460,12 +539,10 @@ extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate
     rc = current_device_sms(&device, &sms);
     if (rc != LITHE_OK) return rc;
 
-    CUtensorMap tmx, tmo_ld, tmo_st;
+    CUtensorMap tmx, tmo_ld;
     rc = encode_bf16_3d(&tmx, x, d_in, m, batch, kChunk, kBM);
     if (rc != LITHE_OK) return rc;
     rc = encode_bf16_3d(&tmo_ld, out, d_out, m, batch, kChunk, kBM);
-    if (rc != LITHE_OK) return rc;
-    rc = encode_bf16_3d(&tmo_st, out, d_out, m, batch, kChunk, 16);
     if (rc != LITHE_OK) return rc;
 
     SgmvParams p{};
@@ -486,15 +563,16 @@ extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate
     p.a_blocks_per_row = d_in / 64;
     p.b_blocks = static_cast<int32_t>(static_cast<int64_t>(d_out) * rank / 64);
     p.scaling = scaling;
+    p.out = static_cast<__nv_bfloat16*>(out);
     expand_lut(lut, idx_a->num_levels, p.lut);
 
     const int grid = static_cast<int>(p.total_units < sms ? p.total_units : sms);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     switch (rank) {
-        case 16: return launch_rank<16>(tmx, tmo_ld, tmo_st, p, grid, device, s);
-        case 8: return launch_rank<8>(tmx, tmo_ld, tmo_st, p, grid, device, s);
-        case 4: return launch_rank<4>(tmx, tmo_ld, tmo_st, p, grid, device, s);
-        case 2: return launch_rank<2>(tmx, tmo_ld, tmo_st, p, grid, device, s);
-        default: return launch_rank<1>(tmx, tmo_ld, tmo_st, p, grid, device, s);
+        case 16: return launch_rank<16>(tmx, tmo_ld, p, grid, device, s);
+        case 8: return launch_rank<8>(tmx, tmo_ld, p, grid, device, s);
+        case 4: return launch_rank<4>(tmx, tmo_ld, p, grid, device, s);
+        case 2: return launch_rank<2>(tmx, tmo_ld, p, grid, device, s);
+        default: return launch_rank<1>(tmx, tmo_ld, p, grid, device, s);
     }
 }
