@@ -147,23 +147,50 @@ __device__ __forceinline__ uint64_t ldg_nc_u64(const uint64_t* p) {
     return v;
 }
 
+// Raw index words of one block, loaded but not yet unpacked.  Splitting the load
+// (fetch_raw) from the unpacking (finish_raw) lets a caller issue the loads one step ahead
+// and use them a step later, so the load latency overlaps other work.
 template <int kMaxLevels>
-__device__ __forceinline__ void fetch_indices(const IndexView& v, int64_t slot, int64_t blk,
-                                              uint32_t k[kMaxLevels], int32_t* err) {
+struct RawIndices {
+    uint64_t a, b;          // PACKED9: the word holding the block's first index, and the next one
+    int32_t q[kMaxLevels];  // I16 / I32: the raw integers
+    uint32_t r0;            // PACKED9: field of the first index in word a
+};
+
+template <int kMaxLevels>
+__device__ __forceinline__ void fetch_raw(const IndexView& v, int64_t slot, int64_t blk, RawIndices<kMaxLevels>& r) {
     if (v.format == LITHE_IDX_PACKED9) {
         // positions inside one slot fit in 32 bits (checked on the host)
         const uint64_t* w = static_cast<const uint64_t*>(v.base) + slot * v.slot_stride;
         const uint32_t p0 = static_cast<uint32_t>(v.offset) + static_cast<uint32_t>(v.levels) * static_cast<uint32_t>(blk);
         const uint32_t w0 = p0 / 7u;
-        const uint32_t r0 = p0 - 7u * w0;
-        const uint64_t a = ldg_nc_u64(w + w0);
+        r.r0 = p0 - 7u * w0;
+        r.a = ldg_nc_u64(w + w0);
         // the block's last index may sit in the next word; read it only then (never past the stream)
-        const uint64_t b = (r0 + static_cast<uint32_t>(v.levels) > 7u) ? ldg_nc_u64(w + w0 + 1) : 0ull;
+        r.b = (r.r0 + static_cast<uint32_t>(v.levels) > 7u) ? ldg_nc_u64(w + w0 + 1) : 0ull;
+    } else {
 #pragma unroll
         for (int l = 0; l < kMaxLevels; ++l) {
             if (l < v.levels) {
-                const uint32_t r = r0 + l;
-                k[l] = static_cast<uint32_t>((r < 7u ? (a >> (9u * r)) : (b >> (9u * (r - 7u))))) & 511u;
+                const int64_t e = slot * v.slot_stride + v.offset + l * v.level_stride + blk;
+                r.q[l] = v.format == LITHE_IDX_I16 ? static_cast<int32_t>(__ldg(static_cast<const int16_t*>(v.base) + e))
+                                                   : __ldg(static_cast<const int32_t*>(v.base) + e);
+            } else {
+                r.q[l] = 0;
+            }
+        }
+    }
+}
+
+template <int kMaxLevels>
+__device__ __forceinline__ void finish_raw(const IndexView& v, const RawIndices<kMaxLevels>& r,
+                                           uint32_t k[kMaxLevels], int32_t* err) {
+    if (v.format == LITHE_IDX_PACKED9) {
+#pragma unroll
+        for (int l = 0; l < kMaxLevels; ++l) {
+            if (l < v.levels) {
+                const uint32_t f = r.r0 + l;
+                k[l] = static_cast<uint32_t>((f < 7u ? (r.a >> (9u * f)) : (r.b >> (9u * (f - 7u))))) & 511u;
             } else {
                 k[l] = 0;
             }
@@ -172,19 +199,19 @@ __device__ __forceinline__ void fetch_indices(const IndexView& v, int64_t slot, 
         bool bad = false;
 #pragma unroll
         for (int l = 0; l < kMaxLevels; ++l) {
-            if (l < v.levels) {
-                const int64_t e = slot * v.slot_stride + v.offset + l * v.level_stride + blk;
-                int32_t raw;
-                if (v.format == LITHE_IDX_I16) raw = __ldg(static_cast<const int16_t*>(v.base) + e);
-                else raw = __ldg(static_cast<const int32_t*>(v.base) + e);
-                bad |= (raw < 0) | (raw > 511);
-                k[l] = static_cast<uint32_t>(raw) & 511u;
-            } else {
-                k[l] = 0;
-            }
+            bad |= (r.q[l] < 0) | (r.q[l] > 511);
+            k[l] = static_cast<uint32_t>(r.q[l]) & 511u;
         }
         if (bad && err) atomicOr(err, LITHE_DEVERR_INDEX);
     }
+}
+
+template <int kMaxLevels>
+__device__ __forceinline__ void fetch_indices(const IndexView& v, int64_t slot, int64_t blk,
+                                              uint32_t k[kMaxLevels], int32_t* err) {
+    RawIndices<kMaxLevels> r;
+    fetch_raw<kMaxLevels>(v, slot, blk, r);
+    finish_raw<kMaxLevels>(v, r, k, err);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -234,13 +261,29 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
 constexpr uint64_t kWaitLimitNs = 4000000000ull;
 constexpr uint32_t kWaitSpinLimit = 1u << 28;   // second bound, independent of the timer
 
+// try_wait with a suspend-time hint: a waiting warp sleeps in hardware until the phase
+// completes or the hint runs out, instead of spinning and taking issue slots from the warps
+// that do the work.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+    uint32_t ok;
+    asm volatile(
+        "{\n .reg .pred p;\n mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+        " selp.u32 %0, 1, 0, p;\n}\n"
+        : "=r"(ok)
+        : "r"(smem_u32(bar)), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return ok != 0;
+}
+
+constexpr uint32_t kSuspendHintNs = 100000;     // one sleeping try_wait lasts at most ~0.1 ms
+
 static __device__ __noinline__ bool mbar_wait_slow(uint64_t* bar, uint32_t parity, volatile int* abort,
-                                            int32_t* err) {
+                                                   int32_t* err) {
     const uint64_t t0 = global_timer_ns();
     for (uint32_t it = 0; it < kWaitSpinLimit; ++it) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait_sleep(bar, parity, kSuspendHintNs)) return true;
         if (*abort) return false;
-        if ((it & 255u) == 255u && global_timer_ns() - t0 > kWaitLimitNs) break;
+        if (global_timer_ns() - t0 > kWaitLimitNs) break;
     }
     *abort = 1;
     if (err) atomicOr(err, LITHE_DEVERR_TIMEOUT);

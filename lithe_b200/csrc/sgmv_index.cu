@@ -9,10 +9,12 @@
 //   per unit   = d_in/64 "x chunks" (64x64 bf16 activation tiles, TMA, 128B swizzle)
 //              + d_out/64 "out chunks" (64x64 bf16 base-output tiles, TMA load; the updated
 //                values go back with coalesced 16-byte stores straight from registers).
-//   warps      = 4 consumer warps (16 tokens each), 1 TMA producer warp, 4 decoder warps.
+//   warps      = 8 consumer warps in 2 groups that take alternate pipeline positions (each
+//                group has 4 warps of 16 tokens; the groups add their partial x.A^T sums
+//                through shared memory before the expand), 1 TMA producer warp, 4 decoder warps.
 //   pipeline   = kStages shared-memory stages; each stage holds one 8 KB tile and the
 //                512 B decoded factor chunk that goes with it; full barrier = TMA bytes +
-//                one decoder arrival, empty barrier = one arrival per consumer warp.
+//                one decoder arrival, empty barrier = one arrival per warp of the group.
 //
 // Decoded factors.  The codeword c_k has period 16 (device_common.cuh), so
 //   A_j[r, 64c + t] = a_{r,c}[t & 15]     (16 values per (rank row, 64-column chunk))
@@ -34,7 +36,9 @@ namespace lithe {
 
 constexpr int kBM = 64;                 // tokens per work unit
 constexpr int kChunk = 64;              // columns per chunk
-constexpr int kConsumerWarps = 4;
+constexpr int kGroupWarps = 4;                    // consumer warps per group (16 token rows each)
+constexpr int kGroups = 2;                        // consumer groups; group g takes positions pos % 2 == g
+constexpr int kConsumerWarps = kGroupWarps * kGroups;
 constexpr int kDecodeWarps = 4;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kFirstDecodeWarp = kConsumerWarps + 1;
@@ -43,8 +47,10 @@ constexpr int kStages = 16;
 constexpr int kTileBytes = kBM * kChunk * 2;      // 8192
 constexpr int kFactBytes = 16 * 16 * 2;           // 512
 constexpr int kLutFloats = 2 * LITHE_MAX_LEVELS * 16;
+constexpr int kXchgFloats = kConsumerWarps * 32 * 8;   // partial h of every consumer thread
 constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * (kTileBytes + kFactBytes) + sizeof(DecodeTables) +
-                              2 * kStages * sizeof(uint64_t) + kLutFloats * sizeof(float) + 16;
+                              kXchgFloats * sizeof(float) + (2 * kStages + 2) * sizeof(uint64_t) +
+                              kLutFloats * sizeof(float) + 16;
 
 struct SgmvParams {
     IndexView ia, ib;
@@ -92,23 +98,23 @@ __device__ __forceinline__ uint32_t add_bf16x2(uint32_t w, float dlo, float dhi)
 // ---------------------------------------------------------------------------------------
 // Decoder warps
 // ---------------------------------------------------------------------------------------
-// Indices of the block this lane decodes in chunk c of a unit (A chunk c < nx, else B
-// chunk c - nx).  Returns false when the lane's values are structurally zero (rank rows
-// >= kRank, or past the last B block).
+// Issue the index loads of the block this lane decodes in chunk c of a unit (A chunk
+// c < nx, else B chunk c - nx).  Returns false when the lane's values are structurally zero
+// (rank rows >= kRank, or past the last B block); then nothing is loaded.
 template <int kRank>
-__device__ __forceinline__ bool chunk_indices(const SgmvParams& p, const Unit& un, int c, int lane,
-                                              uint32_t k[LITHE_MAX_LEVELS]) {
+__device__ __forceinline__ bool chunk_fetch(const SgmvParams& p, const Unit& un, int c, int lane,
+                                            RawIndices<LITHE_MAX_LEVELS>& raw) {
     const int row = lane >> 1;          // A: rank row r; B: logical column n
     const int half = lane & 1;
     if (c < un.nx) {
         if (row >= kRank) return false;
-        fetch_indices<LITHE_MAX_LEVELS>(p.ia, un.slot, static_cast<int64_t>(row) * p.a_blocks_per_row + c, k, p.err);
+        fetch_raw<LITHE_MAX_LEVELS>(p.ia, un.slot, static_cast<int64_t>(row) * p.a_blocks_per_row + c, raw);
         return true;
     }
     constexpr int kPer = 16 / kRank;
     const int G = (16 * (c - un.nx) + row) / kPer;
     if (G >= p.b_blocks || 8 * half >= kRank) return false;
-    fetch_indices<LITHE_MAX_LEVELS>(p.ib, un.slot, G, k, p.err);
+    fetch_raw<LITHE_MAX_LEVELS>(p.ib, un.slot, G, raw);
     return true;
 }
 
@@ -200,22 +206,25 @@ __device__ void run_decoder(int d, int lane, const SgmvParams& p, uint8_t* facts
         return false;
     };
     bool have = seek(true);
-    uint32_t k_next[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
-    bool live_next = have && un.active && chunk_indices<kRank>(p, un, c, lane, k_next);
+    RawIndices<LITHE_MAX_LEVELS> raw_next;
+    bool live_next = have && un.active && chunk_fetch<kRank>(p, un, c, lane, raw_next);
     while (have) {
         const Unit cur = un;
         const int cc = c;
         const uint32_t cpos = pos;
-        uint32_t k[LITHE_MAX_LEVELS];
-#pragma unroll
-        for (int l = 0; l < LITHE_MAX_LEVELS; ++l) k[l] = k_next[l];
+        const RawIndices<LITHE_MAX_LEVELS> raw = raw_next;
         const bool live = live_next;
+        // loads of the next chunk go out now and are unpacked only one iteration later
         have = seek(false);
-        live_next = have && un.active && chunk_indices<kRank>(p, un, c, lane, k_next);
+        live_next = have && un.active && chunk_fetch<kRank>(p, un, c, lane, raw_next);
 
         const uint32_t s = cpos % kStages, ph = (cpos / kStages) & 1u;
         if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return;
-        if (cur.active) decode_chunk<kRank>(p, tab, lut_s, cur, cc, live, k, facts + s * kFactBytes, lane);
+        if (cur.active) {
+            uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
+            if (live) finish_raw<LITHE_MAX_LEVELS>(cc < cur.nx ? p.ia : p.ib, raw, k, p.err);
+            decode_chunk<kRank>(p, tab, lut_s, cur, cc, live, k, facts + s * kFactBytes, lane);
+        }
         __syncwarp();
         if (lane == 0) mbar_arrive(&full[s]);
     }
@@ -238,10 +247,10 @@ __device__ uint32_t run_producer(const SgmvParams& p, const CUtensorMap* tmx, co
             uint8_t* dst = tiles + s * kTileBytes;
             if (c < un.nx) {
                 mbar_arrive_expect_tx(&full[s], kTileBytes);
-                tma_load_3d(dst, tmx, &full[s], c * kChunk, un.mt * kBM, un.b);
+                tma_load_3d(dst, tmx, &full[s], c * kChunk, un.b * p.m + un.mt * kBM, 0);
             } else if (p.accumulate) {
                 mbar_arrive_expect_tx(&full[s], kTileBytes);
-                tma_load_3d(dst, tmo, &full[s], (c - un.nx) * kChunk, un.mt * kBM, un.b);
+                tma_load_3d(dst, tmo, &full[s], (c - un.nx) * kChunk, un.b * p.m + un.mt * kBM, 0);
             } else {
                 mbar_arrive(&full[s]);
             }
@@ -273,9 +282,13 @@ __device__ __forceinline__ uint4 add_delta8(uint4 v, float c0, float c1) {
 
 template <int kRank>
 __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tiles, const uint8_t* facts,
-                             uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin, int u_end) {
+                             uint64_t* full, uint64_t* empty, float* xchg, uint64_t* xbar, volatile int* abort,
+                             int u_begin, int u_end) {
+    const int grp = w / kGroupWarps;     // this warp's group: positions pos % kGroups == grp
+    const int wr = w % kGroupWarps;      // row block within the tile
     const int g = lane >> 2, t4 = lane & 3;
-    const int r0 = 16 * w + g;           // rows r0 and r0 + 8 of the 64-token tile
+    const int r0 = 16 * wr + g;          // rows r0 and r0 + 8 of the 64-token tile
+    uint32_t n_xchg = 0;                 // exchanges done (mbarrier phase parity)
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
     const bool accum = p.accumulate != 0;
     uint32_t pos = 0;
@@ -287,6 +300,7 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
 #pragma unroll
         for (int i = 0; i < 16; ++i) (&acc[0][0][0])[i] = 0.f;
         for (int c = 0; c < un.nx; ++c, ++pos) {
+            if (static_cast<int>(pos % kGroups) != grp) continue;
             const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
             if (!mbar_wait(&full[s], ph, abort, p.err)) return;
             const uint8_t* tile = tiles + s * kTileBytes;
@@ -309,18 +323,45 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
+        // The two groups each saw half of the x chunks: add the partner warp's partial h
+        // (same rows, other group) through shared memory.  xbar[0] = partials written,
+        // xbar[1] = partials read; both count one arrival per consumer warp.
+        float part[8];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            part[i] = acc[0][0][i] + acc[0][1][i];
+            part[4 + i] = acc[1][0][i] + acc[1][1][i];
+        }
+        {
+            float4* mine = reinterpret_cast<float4*>(xchg + (w * 32 + lane) * 8);
+            mine[0] = make_float4(part[0], part[1], part[2], part[3]);
+            mine[1] = make_float4(part[4], part[5], part[6], part[7]);
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xbar[0]);
+            if (!mbar_wait(&xbar[0], n_xchg & 1u, abort, p.err)) return;
+            const int partner = (w + kGroupWarps) % kConsumerWarps;
+            const float4* other = reinterpret_cast<const float4*>(xchg + (partner * 32 + lane) * 8);
+            const float4 o0 = other[0], o1 = other[1];
+            part[0] += o0.x; part[1] += o0.y; part[2] += o0.z; part[3] += o0.w;
+            part[4] += o1.x; part[5] += o1.y; part[6] += o1.z; part[7] += o1.w;
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&xbar[1]);
+            if (!mbar_wait(&xbar[1], n_xchg & 1u, abort, p.err)) return;
+            ++n_xchg;
+        }
         const float sc = p.scaling * (p.weights ? __ldg(p.weights + un.b) : 1.0f);
         float h0[4], h1[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-            h0[i] = (acc[0][0][i] + acc[0][1][i]) * sc;
-            h1[i] = (acc[1][0][i] + acc[1][1][i]) * sc;
+            h0[i] = part[i] * sc;
+            h1[i] = part[4 + i] * sc;
         }
         const uint32_t ha[4] = {pack_bf16x2(h0[0], h0[1]), pack_bf16x2(h0[2], h0[3]), pack_bf16x2(h1[0], h1[1]),
                                 pack_bf16x2(h1[2], h1[3])};
         const int row0 = un.mt * kBM + r0;                   // token rows row0 and row0 + 8
         __nv_bfloat16* out_b = p.out + static_cast<int64_t>(un.b) * p.m * p.d_out;
         for (int j = 0; j < un.no; ++j, ++pos) {
+            if (static_cast<int>(pos % kGroups) != grp) continue;
             const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
             if (!mbar_wait(&full[s], ph, abort, p.err)) return;
             const uint8_t* tile = tiles + s * kTileBytes;
@@ -410,17 +451,21 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* tiles = base;
     uint8_t* facts = tiles + kStages * kTileBytes;
     DecodeTables* tab = reinterpret_cast<DecodeTables*>(facts + kStages * kFactBytes);
-    uint64_t* full = reinterpret_cast<uint64_t*>(tab + 1);
+    float* xchg = reinterpret_cast<float*>(tab + 1);
+    uint64_t* full = reinterpret_cast<uint64_t*>(xchg + kXchgFloats);
     uint64_t* empty = full + kStages;
-    float* lut_s = reinterpret_cast<float*>(empty + kStages);
+    uint64_t* xbar = empty + kStages;
+    float* lut_s = reinterpret_cast<float*>(xbar + 2);
     volatile int* abort = reinterpret_cast<volatile int*>(lut_s + kLutFloats);
 
     const int tid = threadIdx.x;
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
             mbar_init(&full[s], 2);                 // producer + one decoder warp
-            mbar_init(&empty[s], kConsumerWarps);   // one arrival per consumer warp
+            mbar_init(&empty[s], kGroupWarps);      // one arrival per warp of the consuming group
         }
+        mbar_init(&xbar[0], kConsumerWarps);
+        mbar_init(&xbar[1], kConsumerWarps);
         *abort = 0;
         fence_mbar_init();
     }
@@ -434,7 +479,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     uint32_t issued = 0;
     if (warp < kConsumerWarps) {
-        run_consumer<kRank>(warp, lane, p, tiles, facts, full, empty, abort, u_begin, u_end);
+        run_consumer<kRank>(warp, lane, p, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end);
     } else if (warp == kProducerWarp) {
         if (lane == 0) {
             prefetch_tmap(&tmx);
@@ -533,16 +578,21 @@ extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate
     if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
         return fail_arg("x and out must be 16-byte aligned");
     const int64_t n_mtiles = (static_cast<int64_t>(m) + kBM - 1) / kBM;
-    if (n_mtiles * batch > 0x7fffffffLL) return fail_arg("batch * ceil(m/64) exceeds 2^31");
+    if (n_mtiles * batch > 0x7fffffffLL || static_cast<int64_t>(m) * batch > 0x7fffffffLL)
+        return fail_arg("batch * m exceeds 2^31");
 
     int device = 0, sms = 0;
     rc = current_device_sms(&device, &sms);
     if (rc != LITHE_OK) return rc;
 
     CUtensorMap tmx, tmo_ld;
-    rc = encode_bf16_3d(&tmx, x, d_in, m, batch, kChunk, kBM);
+    // Tensor maps over the flattened (batch * m) rows: measured on B200, a (d, m, batch) map
+    // with a (64, 64, 1) box streams about 15% slower than a 2-D map over the same rows.  The
+    // last tile of a sample may then read the next sample's first rows; those rows are never
+    // stored (stores are bounded by the sample's own m), and rows past the tensor read zeros.
+    rc = encode_bf16_3d(&tmx, x, d_in, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
     if (rc != LITHE_OK) return rc;
-    rc = encode_bf16_3d(&tmo_ld, out, d_out, m, batch, kChunk, kBM);
+    rc = encode_bf16_3d(&tmo_ld, out, d_out, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
     if (rc != LITHE_OK) return rc;
 
     SgmvParams p{};
