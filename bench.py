@@ -45,15 +45,15 @@ FALLBACK_HBM_GBS = 6650.0
 CPU_SAMPLE_TOKENS = 256
 
 
-def algorithmic_bytes(d_in: int, d_out: int, b: int = BATCH, m: int = TOKENS, distinct: int = BATCH,
+def algorithmic_bytes(d_in: int, d_out: int, batch: int = BATCH, m: int = TOKENS, distinct: int = BATCH,
                       accumulate: bool = True) -> float:
     """x read + out read and write (in-place accumulate) + the packed indices of the adapters used."""
     ids = distinct * LEVELS * RANK * (d_in + d_out) / 64 * 8 / 7
-    return b * m * d_in * 2 + (2 if accumulate else 1) * b * m * d_out * 2 + ids
+    return batch * m * d_in * 2 + (2 if accumulate else 1) * batch * m * d_out * 2 + ids
 
 
-def flops(d_in: int, d_out: int, b: int = BATCH, m: int = TOKENS) -> float:
-    return 2.0 * b * m * RANK * (d_in + d_out)
+def flops(d_in: int, d_out: int, batch: int = BATCH, m: int = TOKENS) -> float:
+    return 2.0 * batch * m * RANK * (d_in + d_out)
 
 
 def modules():
@@ -240,12 +240,19 @@ def run_lithe(args):
     layout = PackedLayout.from_modules(modules())
     bank = PackedBank(layout, BANK_SLOTS, dev)
     bank.fill_random(seed=1234)                                  # replicated: identical on every rank
-    slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100 + rank))[:BATCH]
+    if args.shard_batch:
+        # strong scaling: the fixed B=14 batch is split by sample across the ranks
+        from lithe_b200.shard import shard_bounds
+        lo, hi = shard_bounds(BATCH, world, rank)
+        slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100))[:BATCH][lo:hi]
+    else:
+        slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100 + rank))[:BATCH]
+    nb = int(slots.numel())                                      # samples this rank runs
     ids = slots.to(torch.int32).to(dev)
     g = torch.Generator(device=dev)
     g.manual_seed(10 + rank)
-    xs = [torch.randn(BATCH, TOKENS, a, generator=g, device=dev, dtype=torch.bfloat16) for a, _ in SHAPES]
-    outs = [(torch.randn(BATCH, TOKENS, b, generator=g, device=dev, dtype=torch.bfloat16) * 0.05) for _, b in SHAPES]
+    xs = [torch.randn(nb, TOKENS, a, generator=g, device=dev, dtype=torch.bfloat16) for a, _ in SHAPES]
+    outs = [(torch.randn(nb, TOKENS, b, generator=g, device=dev, dtype=torch.bfloat16) * 0.05) for _, b in SHAPES]
     names = layout.names
     stream = torch.cuda.current_stream(dev)
 
@@ -282,26 +289,26 @@ def run_lithe(args):
     per_shape_ms = [statistics.mean(evs[k][i][0].elapsed_time(evs[k][i][1]) for k in range(args.steps))
                     for i in range(len(SHAPES))]
     launches = args.steps * len(SHAPES)
-    tokens_per_step = len(SHAPES) * BATCH * TOKENS * world
+    tokens_per_step = len(SHAPES) * BATCH * TOKENS * (1 if args.shard_batch else world)
     value = tokens_per_step / (ms_per_step / 1000.0)
 
     # ---- end-to-end through the public API with host buffers (pinned), copies timed
     max_in = max(a for a, _ in SHAPES)
     max_out = max(b for _, b in SHAPES)
     if not args.no_e2e:
-        x_host = torch.empty(BATCH * TOKENS * max_in, dtype=torch.bfloat16, pin_memory=True)
-        o_host = torch.empty(BATCH * TOKENS * max_out, dtype=torch.bfloat16, pin_memory=True)
+        x_host = torch.empty(nb * TOKENS * max_in, dtype=torch.bfloat16, pin_memory=True)
+        o_host = torch.empty(nb * TOKENS * max_out, dtype=torch.bfloat16, pin_memory=True)
         x_host.normal_()
         o_host.normal_().mul_(0.05)
-    h2d = sum(BATCH * TOKENS * (a + b) * 2 for a, b in SHAPES)
-    d2h = sum(BATCH * TOKENS * b * 2 for _, b in SHAPES)
+    h2d = sum(nb * TOKENS * (a + b) * 2 for a, b in SHAPES)
+    d2h = sum(nb * TOKENS * b * 2 for _, b in SHAPES)
 
     def e2e_step():
         for i, (a, b) in enumerate(SHAPES):
-            xs[i].copy_(x_host[: BATCH * TOKENS * a].view(BATCH, TOKENS, a), non_blocking=True)
-            outs[i].copy_(o_host[: BATCH * TOKENS * b].view(BATCH, TOKENS, b), non_blocking=True)
+            xs[i].copy_(x_host[: nb * TOKENS * a].view(nb, TOKENS, a), non_blocking=True)
+            outs[i].copy_(o_host[: nb * TOKENS * b].view(nb, TOKENS, b), non_blocking=True)
             packed_codebook_lora_delta_(outs[i], xs[i], bank, names[i], ids, scaling=1.0)
-            o_host[: BATCH * TOKENS * b].view(BATCH, TOKENS, b).copy_(outs[i], non_blocking=True)
+            o_host[: nb * TOKENS * b].view(nb, TOKENS, b).copy_(outs[i], non_blocking=True)
 
     e2e_ms = None
     if not args.no_e2e:
@@ -327,16 +334,16 @@ def run_lithe(args):
                          f"of the 4 shapes, {passes} passes in {el:.1f} s"}
 
     peak, peak_kind = measured_peaks()
-    alg = [algorithmic_bytes(a, b) for a, b in SHAPES]
+    alg = [algorithmic_bytes(a, b, batch=nb, distinct=nb) for a, b in SHAPES]
     achieved = sum(alg) / (sum(per_shape_ms) / 1000.0) / 1e9
     traffic = traffic_per_launch()
     shapes_out = []
     for i, (a, b) in enumerate(SHAPES):
         key = f"{a}x{b}"
         gbs = alg[i] / (per_shape_ms[i] / 1000.0) / 1e9
-        shapes_out.append({"shape": key, "ms": per_shape_ms[i], "tokens_per_s": BATCH * TOKENS / (per_shape_ms[i] / 1e3),
+        shapes_out.append({"shape": key, "ms": per_shape_ms[i], "tokens_per_s": nb * TOKENS / (per_shape_ms[i] / 1e3),
                            "algorithmic_bytes": alg[i], "achieved_gbs": gbs, "frac_of_peak": gbs / peak,
-                           "tflops": flops(a, b) / (per_shape_ms[i] / 1e3) / 1e12,
+                           "tflops": flops(a, b, batch=nb) / (per_shape_ms[i] / 1e3) / 1e12,
                            "dram_bytes": None if traffic is None else traffic.get(key)})
     mean_traffic = None
     if traffic is not None and all(s["dram_bytes"] is not None for s in shapes_out):
@@ -345,12 +352,14 @@ def run_lithe(args):
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True, "scaling": "weak",
+            "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
+            "scaling": "strong" if args.shard_batch else "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded uniform 9-bit packed indices (10,000-slot bank), x ~ N(0,1) bf16",
             "config": {"workload": "flux_sweep_b14", "shapes": [f"{a}->{b}" for a, b in SHAPES], "batch": BATCH,
                        "tokens_per_sample": TOKENS, "rank": RANK, "bank_slots": BANK_SLOTS,
-                       "distinct_adapters": BATCH, "parallelism": f"sample-sharded dp{world}, bank replicated",
+                       "distinct_adapters": BATCH, "parallelism": (f"B=14 split by sample over {world} ranks (rank 0 runs {nb})" if args.shard_batch
+                                       else f"dp{world}: every rank runs its own B=14 batch") + ", bank replicated",
                        "l2": "inputs larger than L2 (>= 396 MB of activations per launch), no flush"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"hbm_gbs of {peak_kind}", "traffic": mean_traffic,
@@ -358,7 +367,7 @@ def run_lithe(args):
                          "kernel": "lithe::sgmv_index_kernel<16>"},
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {
-                "value": len(SHAPES) * BATCH * TOKENS * world / (e2e_ms / 1000.0), "unit": "tokens/s",
+                "value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
                 "api": "lithe_b200.kernels.packed_codebook_lora_delta_ (C ABI lithe_sgmv_index), pinned host buffers"},
             "clocks": clocks.summary(),
@@ -381,6 +390,9 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--shard-batch", action="store_true",
+                    help="strong scaling: split the fixed B=14 batch by sample across ranks (default: weak, "
+                         "every rank runs its own B=14 batch)")
     ap.add_argument("--shapes", default="", help="comma list of d_inxd_out to run (default: all four), "
                     "e.g. 3072x3072 for a single-shape profiling run")
     args = ap.parse_args()
