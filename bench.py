@@ -381,12 +381,159 @@ def run_lithe(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------- decode workloads
+DECODE_PER_LAUNCH = 14
+# Fused packed decode of one Kohya-304 adapter, 153.2 MB of bf16 in 4.56 ms on an A100
+# (serving/README.md:60 of the reference): the only published number for this metric.
+PUBLISHED_KOHYA304_DECODE_GBS = 153.2e6 / 4.56e-3 / 1e9
+
+
+def decode_modules(kind: str):
+    """Module shapes of one adapter: the 342 FLUX.1-dev attention+FFN linears, or Kohya-304."""
+    if kind == "kohya304":
+        shapes = ([(3072, 9216)] * 76 + [(3072, 18432)] * 38 + [(3072, 3072)] * 38 + [(3072, 12288)] * 38
+                  + [(12288, 3072)] * 38 + [(3072, 21504)] * 38 + [(15360, 3072)] * 38)
+        return [{"name": f"m{i}", "shape_a": [RANK, a], "shape_b": [b, RANK]} for i, (a, b) in enumerate(shapes)]
+    mods = []
+    for i in range(19):
+        for t in ("attn.to_q", "attn.to_k", "attn.to_v", "attn.to_out.0", "attn.add_q_proj", "attn.add_k_proj",
+                  "attn.add_v_proj", "attn.to_add_out"):
+            mods.append((f"transformer_blocks.{i}.{t}", 3072, 3072))
+        for ff in ("ff", "ff_context"):
+            mods.append((f"transformer_blocks.{i}.{ff}.net.0.proj", 3072, 12288))
+            mods.append((f"transformer_blocks.{i}.{ff}.net.2", 12288, 3072))
+    for i in range(38):
+        for t in ("to_q", "to_k", "to_v"):
+            mods.append((f"single_transformer_blocks.{i}.attn.{t}", 3072, 3072))
+    return [{"name": n, "shape_a": [RANK, a], "shape_b": [b, RANK]} for n, a, b in mods]
+
+
+def cpu_decode_rate(kind: str, seconds: float):
+    """bf16 GB/s of the oracle's numpy decode of one whole adapter (single thread)."""
+    from oracle import codebook_ref, decode_ref
+    pa, pb = codebook_ref.twin_pools()
+    lay = decode_ref.layout(decode_modules(kind))
+    flat = np.random.default_rng(0).integers(0, 512, lay.num_indices)
+    words = decode_ref.pack9(flat)
+    n, t0 = 0, time.perf_counter()
+    while True:
+        blocks = decode_ref.decode_stream(decode_ref.unpack9(words, lay.num_indices), lay, pa, pb)
+        decode_ref.f32_to_bf16_bits(blocks)
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            break
+    return n * lay.total_blocks * 128 / el / 1e9, n, el
+
+
+def run_decode(args):
+    from lithe_b200 import device_errors
+    from lithe_b200.kernels import PackedBank, PackedLayout
+
+    kind = args.workload.split("_", 1)[1]
+    metric = f"decoded bf16 GB/s ({'Kohya-304' if kind == 'kohya304' else '342-module FLUX'} rank-16 adapters)"
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        rates = [cpu_decode_rate(kind, max(1.0, 30.0 / max(1, args.steps)))[0] for _ in range(args.steps)]
+        v = statistics.median(rates)
+        print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+                          "steps": args.steps, "warmup": args.warmup, "higher_is_better": True, "scaling": "weak",
+                          "vs_baseline": None, "dtype": "u16->f32->bf16", "data": "synthetic uniform 9-bit indices",
+                          "config": {"workload": args.workload},
+                          "cpu_baseline": {"value": v, "unit": "GB/s", "cores": 1, "kind": "port",
+                                           "sample": "oracle numpy decode of one whole adapter per pass"},
+                          "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return
+    init_dist(world, local)
+    dev = torch.device("cuda", local)
+    layout = PackedLayout.from_modules(decode_modules(kind))
+    bank = PackedBank(layout, BANK_SLOTS, dev)
+    bank.fill_random(seed=4321)
+    slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(200 + rank))[:DECODE_PER_LAUNCH]
+    ids = slots.to(torch.int32)
+    out = torch.empty((DECODE_PER_LAUNCH, layout.total_blocks, 64), dtype=torch.bfloat16, device=dev)
+    decoded_bytes = out.numel() * 2
+    index_bytes = DECODE_PER_LAUNCH * layout.num_words * 8
+    stream = torch.cuda.current_stream(dev)
+    ids_dev = ids.to(dev)
+    for _ in range(args.warmup):
+        bank.decode(ids_dev, out=out)
+    torch.cuda.synchronize(dev)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    barrier(world)
+    torch.cuda.synchronize(dev)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            bank.decode(ids_dev, out=out)
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    value = decoded_bytes * world / (ms / 1000.0) / 1e9
+    # end to end: the 14 slots' packed words go up from pinned host memory, the dense factors come back
+    host_words = torch.empty((DECODE_PER_LAUNCH, bank.slot_stride), dtype=torch.int64, pin_memory=True)
+    host_words.copy_(bank.words[ids_dev.long()].cpu())
+    host_out = torch.empty(out.shape, dtype=torch.bfloat16, pin_memory=True)
+    staging = PackedBank(layout, DECODE_PER_LAUNCH, dev)
+    local_ids = torch.arange(DECODE_PER_LAUNCH, dtype=torch.int32, device=dev)
+    e2e_steps = max(1, min(args.steps, 5))
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        staging.words.copy_(host_words, non_blocking=True)
+        staging.decode(local_ids, out=out)
+        host_out.copy_(out, non_blocking=True)
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
+    errors = device_errors(dev)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, n, el = cpu_decode_rate(kind, args.cpu_seconds)
+        cpu = {"value": rate, "unit": "GB/s", "cores": 1, "kind": "port",
+               "sample": f"oracle numpy decode of one whole adapter, {n} passes in {el:.1f} s"}
+    peak, peak_kind = measured_peaks()
+    achieved = (decoded_bytes + index_bytes) / (ms / 1000.0) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": metric, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": (value / PUBLISHED_KOHYA304_DECODE_GBS) if kind == "kohya304" else None,
+            "vs_baseline_note": "A100 figure of the reference (4.56 ms per Kohya-304 adapter)" if kind == "kohya304" else None,
+            "dtype": "u64 packed -> f32 -> bf16", "data": "synthetic: seeded uniform 9-bit packed indices",
+            "config": {"workload": args.workload, "adapters_per_launch": DECODE_PER_LAUNCH, "bank_slots": BANK_SLOTS,
+                       "blocks_per_adapter": layout.total_blocks, "decoded_mb_per_adapter": layout.total_blocks * 128 / 1e6,
+                       "packed_mb_per_adapter": layout.num_words * 8 / 1e6,
+                       "l2": "output (>= 1.25 GB per launch) larger than L2, no flush"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"hbm_gbs of {peak_kind}", "traffic": None,
+                         "algorithmic_bytes_per_launch": decoded_bytes + index_bytes,
+                         "kernel": "lithe::decode_packed_kernel<false>"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": decoded_bytes * world / (e2e_ms / 1000.0) / 1e9, "unit": "GB/s",
+                    "h2d_bytes_per_step": DECODE_PER_LAUNCH * bank.slot_stride * 8, "d2h_bytes_per_step": decoded_bytes,
+                    "ms_per_step": e2e_ms, "api": "PackedBank.decode (C ABI lithe_decode_packed_batch)"},
+            "clocks": clocks.summary(), "gpu_launches": args.steps, "device_errors": errors,
+            "adapters_per_s": DECODE_PER_LAUNCH * world / (ms / 1000.0)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["lithe", "reference"], default="lithe")
+    ap.add_argument("--workload", choices=["flux_sweep_b14", "decode_flux342", "decode_kohya304"],
+                    default="flux_sweep_b14", help="flux_sweep_b14: fused decode+SGMV (default); decode_*: "
+                    "standalone packed decode of 14 resident adapters per launch")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
@@ -404,7 +551,9 @@ def main():
             raise SystemExit(f"--shapes must be a subset of the FLUX shapes, got {args.shapes}")
     if args.warmup < 3 and args.impl == "lithe":
         raise SystemExit("--warmup must be >= 3")
-    if args.impl == "reference":
+    if args.workload.startswith("decode_"):
+        run_decode(args)
+    elif args.impl == "reference":
         run_reference(args)
     else:
         run_lithe(args)

@@ -90,9 +90,12 @@ static int32_t launch_decode(const DecodeParams& p, int32_t n_sel, int32_t out_d
     int device = 0, sms = 0;
     int32_t rc = current_device_sms(&device, &sms);
     if (rc != LITHE_OK) return rc;
+    // Each CTA first builds its 14 KB of decode tables, so CTAs must be long-lived: about 8
+    // resident CTAs per SM in total over all selected slots, each grid-striding over its slot.
     const int threads = 256;
     int64_t blocks = (items + threads - 1) / threads;
-    const int64_t cap = static_cast<int64_t>(sms) * 16;   // grid-stride beyond 16 CTAs per SM
+    int64_t cap = (static_cast<int64_t>(sms) * 8 + n_sel - 1) / n_sel;
+    if (cap < 1) cap = 1;
     if (blocks > cap) blocks = cap;
     dim3 grid(static_cast<unsigned>(blocks), static_cast<unsigned>(n_sel));
     cudaStream_t s = static_cast<cudaStream_t>(stream);

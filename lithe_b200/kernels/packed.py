@@ -228,13 +228,12 @@ class PackedBank:
         self.set_slot(slot, pack_adapter(ad, self.layout)[0])
 
     def fill_random(self, seed: int, slots: Optional[slice] = None) -> None:
-        """Seeded uniform 9-bit indices in every slot (any 63-bit word is 7 valid indices)."""
+        """Seeded uniform 9-bit indices in every slot: int64 random_() draws uniform words in
+        [0, 2^63), i.e. 7 uniform 9-bit fields with the unused top bit clear."""
         g = torch.Generator(device=self.device)
         g.manual_seed(int(seed))
         view = self.words if slots is None else self.words[slots]
-        view.random_(0, 1 << 62, generator=g)
-        hi = torch.randint(0, 2, view.shape, generator=g, device=self.device, dtype=torch.int64)
-        view.add_(hi << 62)
+        view.random_(generator=g)
 
     def views(self, name: str) -> Tuple[_lib.IndexView, _lib.IndexView]:
         i = self.layout.index(name)
@@ -243,11 +242,12 @@ class PackedBank:
         vb = _launch.index_view(self.words, _lib.IDX_PACKED9, L, self.slot_stride, L * self.layout.b_off[i])
         return va, vb
 
-    def decode(self, slot_ids, dtype: torch.dtype = torch.bfloat16) -> torch.Tensor:
-        """(n_sel, total_blocks, 64) decode of the given slots in one launch."""
+    def decode(self, slot_ids, dtype: torch.dtype = torch.bfloat16, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+        """(n_sel, total_blocks, 64) decode of the given slots in one launch (into ``out`` if given)."""
         ids = torch.as_tensor(slot_ids, dtype=torch.int32).reshape(-1).to(self.device)
-        out = torch.empty((ids.numel(), self.layout.total_blocks, self.layout.block_size), dtype=dtype,
-                          device=self.device)
+        if out is None:
+            out = torch.empty((ids.numel(), self.layout.total_blocks, self.layout.block_size), dtype=dtype,
+                              device=self.device)
         return _launch.decode_packed_batch_(self.words, ids, self.layout.total_blocks, self.layout.num_levels,
                                             self.layout.sides_on(self.device), self.lut, out)
 
