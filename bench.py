@@ -288,7 +288,9 @@ def run_lithe(args):
     ms_per_step = total_ms / args.steps
     per_shape_ms = [statistics.mean(evs[k][i][0].elapsed_time(evs[k][i][1]) for k in range(args.steps))
                     for i in range(len(SHAPES))]
-    launches = args.steps * len(SHAPES)
+    from lithe_b200.kernels import _launch as _lk
+    mode = _lk.DEFAULT_MODE
+    launches = args.steps * len(SHAPES) * (2 if mode == "staged" else 1)
     tokens_per_step = len(SHAPES) * BATCH * TOKENS * (1 if args.shard_batch else world)
     value = tokens_per_step / (ms_per_step / 1000.0)
 
@@ -360,11 +362,13 @@ def run_lithe(args):
                        "tokens_per_sample": TOKENS, "rank": RANK, "bank_slots": BANK_SLOTS,
                        "distinct_adapters": BATCH, "parallelism": (f"B=14 split by sample over {world} ranks (rank 0 runs {nb})" if args.shard_batch
                                        else f"dp{world}: every rank runs its own B=14 batch") + ", bank replicated",
-                       "l2": "inputs larger than L2 (>= 396 MB of activations per launch), no flush"},
+                       "l2": "inputs larger than L2 (>= 396 MB of activations per launch), no flush",
+                       "mode": mode},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"hbm_gbs of {peak_kind}", "traffic": mean_traffic,
                          "algorithmic_bytes_per_launch": sum(alg) / len(alg),
-                         "kernel": "lithe::sgmv_index_kernel<16>"},
+                         "kernel": "lithe::sgmv_index_kernel<16, staged>" if mode == "staged" else "lithe::sgmv_index_kernel<16, fused>",
+                         "timed": "the whole op per launch" + (" (decode_chunks_kernel + sgmv_index_kernel)" if mode == "staged" else "")},
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {
                 "value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
@@ -525,24 +529,138 @@ def run_decode(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------- denoise workloads
+DENOISE = {  # workload -> (image tokens, text tokens, batch, steps)
+    "denoise_512": (1024, 512, 14, 16),        # config 3: 512^2, B=14, 16 steps
+    "denoise_256_b96": (256, 512, 96, 4),      # config 4: 256^2, B=96 distinct adapters, 4 steps
+    "denoise_1024": (4096, 512, 14, 28),       # config 5: 1024^2, B=14, 28 steps
+}
+
+
+def run_denoise(args):
+    """Full denoise loop on a random-init FLUX.1-dev-shaped transformer (bf16), three ways:
+    base only, index-resident LoRA (fused kernel on every one of the 342 target linears, 9-bit
+    packed 10,000-slot bank), and a dense resident-LoRA comparator (decoded bf16 factors of the
+    batch's adapters resident in HBM, two cuBLAS bmm + in-place add per linear)."""
+    from lithe_b200.flux_model import FluxShapedTransformer, denoise, lora_targets
+    from lithe_b200.kernels import (PackedBank, PackedLayout, PackedLoRALinear, PerSampleLoRALinear, split_decoded,
+                                    wrap_linears)
+    from lithe_b200.shard import shard_bounds
+
+    img_tok, txt_tok, batch, steps = DENOISE[args.workload]
+    world, rank, local = dist_env()
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference's full denoise loop needs diffusers and "
+                              "FLUX.1-dev weights, absent on this box; its CPU path is timed per linear by the "
+                              "flux_sweep_b14 workload"}), flush=True)
+        return
+    init_dist(world, local)
+    dev = torch.device("cuda", local)
+    torch.manual_seed(0)
+    model = FluxShapedTransformer().to(device=dev, dtype=torch.bfloat16).eval()
+    targets = lora_targets(model)
+    layout = PackedLayout.from_modules([{"name": n, "shape_a": [RANK, m.in_features], "shape_b": [m.out_features, RANK]}
+                                        for n, m in targets])
+    bank = PackedBank(layout, BANK_SLOTS, dev)
+    bank.fill_random(seed=1234)
+    lo, hi = shard_bounds(batch, world, rank) if args.shard_batch else (0, batch)
+    slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(300 if args.shard_batch else 300 + rank))[:batch][lo:hi]
+    nb = int(slots.numel())
+    g = torch.Generator(device=dev)
+    g.manual_seed(7 + (0 if args.shard_batch else rank))
+    lat = torch.randn(batch, img_tok, 64, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous()
+    txt = torch.randn(batch, txt_tok, 4096, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous()
+    pooled = torch.randn(batch, 768, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous()
+    names = [n for n, _ in targets]
+    bases = {n: m for n, m in targets}
+    packed = {n: PackedLoRALinear(bases[n], bank, n, RANK, 1.0) for n in names}
+    ids = slots.to(torch.int32).to(dev)
+    for m in packed.values():
+        m.assign = ids
+    dec = bank.decode(ids, dtype=torch.bfloat16)                   # the dense comparator's resident factors
+    per = [split_decoded(dec[i], layout) for i in range(nb)]
+    dense = {}
+    for n in names:
+        d = PerSampleLoRALinear(bases[n], "sgmv")
+        d.set_factors([(p[n][0].contiguous(), p[n][1].contiguous(), 1.0) for p in per])
+        d._build_stacked(torch.bfloat16)
+        dense[n] = d
+    del dec, per
+
+    def install(kind):
+        table = {"base": bases, "lithe": packed, "dense": dense}[kind]
+        wrap_linears_any(model, names, table)
+
+    stream = torch.cuda.current_stream(dev)
+    results = {}
+    with torch.no_grad():
+        for kind in ("base", "lithe", "dense"):
+            install(kind)
+            denoise(model, lat, txt, pooled, 1)                       # warm-up (one step)
+            torch.cuda.synchronize(dev)
+            barrier(world)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local) as clocks:
+                e0.record(stream)
+                denoise(model, lat, txt, pooled, steps)
+                e1.record(stream)
+                torch.cuda.synchronize(dev)
+            barrier(world)
+            results[kind] = (max_over_ranks(e0.elapsed_time(e1) / 1000.0, world), clocks.summary())
+    t_base, t_lithe, t_dense = results["base"][0], results["lithe"][0], results["dense"][0]
+    if rank == 0:
+        print(json.dumps({
+            "metric": f"{steps}-step denoise wall time", "value": t_lithe, "unit": "s", "n_gpus": world, "steps": steps,
+            "warmup": 1, "ms_per_step": 1000.0 * t_lithe / steps, "higher_is_better": False,
+            "scaling": "strong" if args.shard_batch else "weak", "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic: random-init FLUX.1-dev-shaped transformer, seeded uniform 9-bit packed adapters",
+            "config": {"workload": args.workload, "image_tokens": img_tok, "text_tokens": txt_tok, "batch": batch,
+                       "rank_batch": nb, "lora_linears": len(names), "bank_slots": BANK_SLOTS,
+                       "parallelism": (f"B={batch} split by sample over {world} ranks" if args.shard_batch
+                                       else f"dp{world}: every rank its own B={batch}") + ", bank replicated"},
+            "base_only_s": t_base, "lithe_s": t_lithe, "dense_resident_lora_s": t_dense,
+            "lithe_lora_overhead_s": t_lithe - t_base, "dense_lora_overhead_s": t_dense - t_base,
+            "overhead_ratio_lithe_vs_dense": (t_lithe - t_base) / max(1e-9, t_dense - t_base),
+            "clocks": results["lithe"][1], "gpu_launches": steps * len(names)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
+def wrap_linears_any(model, names, table):
+    """Point model.<name> at table[name] (swaps between plain, packed and dense wrappers)."""
+    for n in names:
+        parent_name, _, child = n.rpartition(".")
+        parent = model.get_submodule(parent_name) if parent_name else model
+        setattr(parent, child, table[n])
+
+
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=300)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["lithe", "reference"], default="lithe")
-    ap.add_argument("--workload", choices=["flux_sweep_b14", "decode_flux342", "decode_kohya304"],
+    ap.add_argument("--workload", choices=["flux_sweep_b14", "decode_flux342", "decode_kohya304", "denoise_512",
+                                           "denoise_256_b96", "denoise_1024"],
                     default="flux_sweep_b14", help="flux_sweep_b14: fused decode+SGMV (default); decode_*: "
                     "standalone packed decode of 14 resident adapters per launch")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--mode", choices=["staged", "fused"], default=None,
+                    help="form of the fused op: fused (decode inside the SGMV kernel per 64-token tile, default) "
+                         "or staged (decode once per call into a workspace)")
     ap.add_argument("--shard-batch", action="store_true",
                     help="strong scaling: split the fixed B=14 batch by sample across ranks (default: weak, "
                          "every rank runs its own B=14 batch)")
     ap.add_argument("--shapes", default="", help="comma list of d_inxd_out to run (default: all four), "
                     "e.g. 3072x3072 for a single-shape profiling run")
     args = ap.parse_args()
+    if args.mode:
+        from lithe_b200.kernels import _launch
+        _launch.DEFAULT_MODE = args.mode
     if args.shapes:
         global SHAPES
         want = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
@@ -553,6 +671,8 @@ def main():
         raise SystemExit("--warmup must be >= 3")
     if args.workload.startswith("decode_"):
         run_decode(args)
+    elif args.workload.startswith("denoise_"):
+        run_denoise(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

@@ -106,6 +106,28 @@ LITHE_API int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate,
                          int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank,
                          const float* lut, float scaling, int32_t* err_flag, void* stream);
 
+/* Bytes of device workspace lithe_sgmv_index_ws needs for a (batch, d_in, d_out) call:
+ * batch * (d_in/64 + ceil(d_out/64)) * 512. */
+LITHE_API int64_t lithe_sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out);
+
+/*
+ * lithe_sgmv_index in two launches on the same stream, with the same arguments, contract and
+ * results (bit for bit).  A first kernel decodes every routed sample's A and B factors once
+ * into `workspace` (512 bytes per 64-column chunk, 16 distinct values per block thanks to the
+ * codebook's period-16 structure); the SGMV kernel then copies each chunk next to its
+ * activation tile instead of re-decoding it for every 64-token tile.  Preferable when d_in is
+ * large (decode-bound shrink).  Replaces the same reference code as lithe_sgmv_index.
+ *   workspace        device, 16-byte aligned, >= lithe_sgmv_workspace_bytes(batch, d_in, d_out);
+ *                    contents on entry do not matter; calls sharing one workspace must be
+ *                    ordered on one stream.
+ */
+LITHE_API int32_t lithe_sgmv_index_ws(const void* x, void* out, int32_t accumulate,
+                         const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                         int64_t n_slots, const int32_t* ids, const float* weights,
+                         int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank,
+                         const float* lut, float scaling, int32_t* err_flag,
+                         void* workspace, int64_t workspace_bytes, void* stream);
+
 /*
  * Whole-adapter decode of a packed stream into dense 64-value blocks (replaces
  * _decode_packed_kernel / decode_packed, lithe/kernels/packed.py:151-177,205-222).

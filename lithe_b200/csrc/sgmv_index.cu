@@ -42,7 +42,8 @@ constexpr int kConsumerWarps = kGroupWarps * kGroups;
 constexpr int kDecodeWarps = 4;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kFirstDecodeWarp = kConsumerWarps + 1;
-constexpr int kThreads = 32 * (kConsumerWarps + 1 + kDecodeWarps);
+constexpr int kThreads = 32 * (kConsumerWarps + 1 + kDecodeWarps);     // fused mode
+constexpr int kThreadsStaged = 32 * (kConsumerWarps + 1);                // staged mode: no decoder warps
 constexpr int kStages = 16;
 constexpr int kTileBytes = kBM * kChunk * 2;      // 8192
 constexpr int kFactBytes = 16 * 16 * 2;           // 512
@@ -65,6 +66,8 @@ struct SgmvParams {
     int32_t b_blocks;           // d_out * rank / 64
     float scaling;
     __nv_bfloat16* out;
+    const uint8_t* ws;          // staged mode: decoded factor chunks, (batch, n_chunks, 512 B)
+    int32_t n_chunks;           // n_xchunks + n_ochunks (per-sample stride of ws, in chunks)
     float lut[2][LITHE_MAX_LEVELS][16];
 };
 
@@ -233,8 +236,11 @@ __device__ void run_decoder(int d, int lane, const SgmvParams& p, uint8_t* facts
 // ---------------------------------------------------------------------------------------
 // Producer (one lane)
 // ---------------------------------------------------------------------------------------
+// Staged mode: the producer also bulk-copies the unit's decoded factor chunk (512 B, written
+// by decode_chunks_kernel) into the stage, so one arrival + the TMA bytes complete a stage.
+template <bool kStaged>
 __device__ uint32_t run_producer(const SgmvParams& p, const CUtensorMap* tmx, const CUtensorMap* tmo,
-                                 uint8_t* tiles, uint64_t* full, uint64_t* empty, volatile int* abort,
+                                 uint8_t* tiles, uint8_t* facts, uint64_t* full, uint64_t* empty, volatile int* abort,
                                  int u_begin, int u_end) {
     uint32_t pos = 0;
     for (int u = u_begin; u < u_end; ++u) {
@@ -245,15 +251,19 @@ __device__ uint32_t run_producer(const SgmvParams& p, const CUtensorMap* tmx, co
             const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
             if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return pos;
             uint8_t* dst = tiles + s * kTileBytes;
-            if (c < un.nx) {
-                mbar_arrive_expect_tx(&full[s], kTileBytes);
-                tma_load_3d(dst, tmx, &full[s], c * kChunk, un.b * p.m + un.mt * kBM, 0);
-            } else if (p.accumulate) {
-                mbar_arrive_expect_tx(&full[s], kTileBytes);
-                tma_load_3d(dst, tmo, &full[s], (c - un.nx) * kChunk, un.b * p.m + un.mt * kBM, 0);
-            } else {
+            const bool tile = c < un.nx || p.accumulate;
+            const bool fact = kStaged && un.active;
+            const uint32_t bytes = (tile ? kTileBytes : 0u) + (fact ? static_cast<uint32_t>(kFactBytes) : 0u);
+            if (bytes == 0) {
                 mbar_arrive(&full[s]);
+                continue;
             }
+            mbar_arrive_expect_tx(&full[s], bytes);
+            if (c < un.nx) tma_load_3d(dst, tmx, &full[s], c * kChunk, un.b * p.m + un.mt * kBM, 0);
+            else if (p.accumulate) tma_load_3d(dst, tmo, &full[s], (c - un.nx) * kChunk, un.b * p.m + un.mt * kBM, 0);
+            if (fact)
+                bulk_load_1d(facts + s * kFactBytes,
+                             p.ws + (static_cast<int64_t>(un.b) * p.n_chunks + c) * kFactBytes, kFactBytes, &full[s]);
         }
     }
     return pos;
@@ -442,8 +452,8 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
     }
 }
 
-template <int kRank>
-__global__ void __launch_bounds__(kThreads, 1)
+template <int kRank, bool kStaged>
+__global__ void __launch_bounds__(kStaged ? kThreadsStaged : kThreads, 1)
     sgmv_index_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmo_ld,
                       const __grid_constant__ SgmvParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -461,7 +471,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     const int tid = threadIdx.x;
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], 2);                 // producer + one decoder warp
+            mbar_init(&full[s], kStaged ? 1 : 2);   // producer (+ one decoder warp in fused mode)
             mbar_init(&empty[s], kGroupWarps);      // one arrival per warp of the consuming group
         }
         mbar_init(&xbar[0], kConsumerWarps);
@@ -469,8 +479,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         *abort = 0;
         fence_mbar_init();
     }
-    for (int i = tid; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
-    build_decode_tables(tab, &p.lut[0][0][0], p.ia.levels, tid, blockDim.x);
+    if constexpr (!kStaged) {
+        for (int i = tid; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
+        build_decode_tables(tab, &p.lut[0][0][0], p.ia.levels, tid, blockDim.x);
+    }
     __syncthreads();
 
     const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_units / gridDim.x);
@@ -484,9 +496,9 @@ __global__ void __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             prefetch_tmap(&tmx);
             prefetch_tmap(&tmo_ld);
-            issued = run_producer(p, &tmx, &tmo_ld, tiles, full, empty, abort, u_begin, u_end);
+            issued = run_producer<kStaged>(p, &tmx, &tmo_ld, tiles, facts, full, empty, abort, u_begin, u_end);
         }
-    } else {
+    } else if constexpr (!kStaged) {
         run_decoder<kRank>(warp - kFirstDecodeWarp, lane, p, facts, tab, lut_s, full, empty, abort, u_begin, u_end);
     }
     __syncthreads();
@@ -503,18 +515,60 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
 }
 
+// Staged mode, phase 1: decode every routed sample's factor chunks once into the workspace,
+// in the exact 512-byte layout the decoder warps write into a stage (decode_chunk).  One warp
+// per (sample, chunk); every CTA builds the decode tables once and grid-strides.
 template <int kRank>
+__global__ void __launch_bounds__(256) decode_chunks_kernel(const __grid_constant__ SgmvParams p, uint8_t* ws,
+                                                            int32_t batch) {
+    __shared__ DecodeTables tab;
+    __shared__ float lut_s[kLutFloats];
+    for (int i = threadIdx.x; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
+    build_decode_tables(&tab, &p.lut[0][0][0], p.ia.levels, threadIdx.x, blockDim.x);
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const int64_t total = static_cast<int64_t>(batch) * p.n_chunks;
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        const int b = static_cast<int>(w / p.n_chunks);
+        const int c = static_cast<int>(w - static_cast<int64_t>(b) * p.n_chunks);
+        const int32_t sid = __ldg(p.ids + b);
+        if (sid < 0 || static_cast<int64_t>(sid) >= p.n_slots) continue;   // no factors needed
+        Unit un;
+        un.b = b;
+        un.mt = 0;
+        un.slot = sid;
+        un.active = true;
+        un.nx = p.n_xchunks;
+        un.no = p.n_ochunks;
+        RawIndices<LITHE_MAX_LEVELS> raw;
+        const bool live = chunk_fetch<kRank>(p, un, c, lane, raw);
+        uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
+        if (live) finish_raw<LITHE_MAX_LEVELS>(c < un.nx ? p.ia : p.ib, raw, k, p.err);
+        decode_chunk<kRank>(p, &tab, lut_s, un, c, live, k, ws + w * kFactBytes, lane);
+    }
+}
+
+template <int kRank, bool kStaged>
 static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, const SgmvParams& p, int grid,
-                           int device, cudaStream_t stream) {
+                           int device, int sms, int32_t batch, uint8_t* ws, cudaStream_t stream) {
     static bool configured[64] = {false};
-    auto kern = sgmv_index_kernel<kRank>;
+    auto kern = sgmv_index_kernel<kRank, kStaged>;
     if (!configured[device]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmemBytes));
         if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(sgmv_index_kernel)");
         configured[device] = true;
     }
-    kern<<<grid, kThreads, kSmemBytes, stream>>>(tmx, tmo_ld, p);
+    if constexpr (kStaged) {
+        const int64_t warps_needed = static_cast<int64_t>(batch) * p.n_chunks;
+        int64_t blocks = (warps_needed + 7) / 8;
+        if (blocks > 2LL * sms) blocks = 2LL * sms;
+        decode_chunks_kernel<kRank><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p, ws, batch);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return fail_cuda(e, "decode_chunks_kernel launch");
+    }
+    kern<<<grid, kStaged ? kThreadsStaged : kThreads, kSmemBytes, stream>>>(tmx, tmo_ld, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "sgmv_index_kernel launch");
     return LITHE_OK;
@@ -547,12 +601,19 @@ static IndexView to_view(const lithe_index_view* v) {
 
 }  // namespace lithe
 
-extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate, const lithe_index_view* idx_a,
-                                    const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids,
-                                    const float* weights, int32_t batch, int32_t m, int32_t d_in, int32_t d_out,
-                                    int32_t rank, const float* lut, float scaling, int32_t* err_flag, void* stream) {
-    using namespace lithe;
-    clear_error();
+namespace lithe {
+
+int64_t sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out) {
+    if (batch <= 0 || d_in <= 0 || d_out <= 0) return 0;
+    return static_cast<int64_t>(batch) * (d_in / kChunk + (d_out + kChunk - 1) / kChunk) * kFactBytes;
+}
+
+// Shared by the C entry points.  ws == nullptr: fused mode (decoder warps in the SGMV kernel);
+// otherwise staged mode with ws_bytes >= sgmv_workspace_bytes(batch, d_in, d_out).
+int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lithe_index_view* idx_a,
+                        const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids, const float* weights,
+                        int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank, const float* lut,
+                        float scaling, int32_t* err_flag, void* ws, int64_t ws_bytes, void* stream) {
     if (batch < 0 || m < 0) return fail_arg("batch (%d) and m (%d) must be >= 0", batch, m);
     if (rank != 1 && rank != 2 && rank != 4 && rank != 8 && rank != 16)
         return fail_unsupported("rank must be one of 1, 2, 4, 8, 16; got %d", rank);
@@ -616,13 +677,53 @@ extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate
     p.out = static_cast<__nv_bfloat16*>(out);
     expand_lut(lut, idx_a->num_levels, p.lut);
 
+    p.n_chunks = p.n_xchunks + p.n_ochunks;
+    p.ws = static_cast<const uint8_t*>(ws);
+    if (ws) {
+        if (reinterpret_cast<uintptr_t>(ws) % 16) return fail_arg("workspace must be 16-byte aligned");
+        const int64_t need = sgmv_workspace_bytes(batch, d_in, d_out);
+        if (ws_bytes < need)
+            return fail_arg("workspace holds %lld bytes, this call needs %lld", (long long)ws_bytes, (long long)need);
+    }
+
     const int grid = static_cast<int>(p.total_units < sms ? p.total_units : sms);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    uint8_t* w = static_cast<uint8_t*>(ws);
+#define LITHE_LAUNCH(R)                                                                         \
+    return ws ? launch_rank<R, true>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)          \
+              : launch_rank<R, false>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)
     switch (rank) {
-        case 16: return launch_rank<16>(tmx, tmo_ld, p, grid, device, s);
-        case 8: return launch_rank<8>(tmx, tmo_ld, p, grid, device, s);
-        case 4: return launch_rank<4>(tmx, tmo_ld, p, grid, device, s);
-        case 2: return launch_rank<2>(tmx, tmo_ld, p, grid, device, s);
-        default: return launch_rank<1>(tmx, tmo_ld, p, grid, device, s);
+        case 16: LITHE_LAUNCH(16);
+        case 8: LITHE_LAUNCH(8);
+        case 4: LITHE_LAUNCH(4);
+        case 2: LITHE_LAUNCH(2);
+        default: LITHE_LAUNCH(1);
     }
+#undef LITHE_LAUNCH
+}
+
+}  // namespace lithe
+
+extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate, const lithe_index_view* idx_a,
+                                    const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids,
+                                    const float* weights, int32_t batch, int32_t m, int32_t d_in, int32_t d_out,
+                                    int32_t rank, const float* lut, float scaling, int32_t* err_flag, void* stream) {
+    lithe::clear_error();
+    return lithe::sgmv_index_impl(x, out, accumulate, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
+                                  rank, lut, scaling, err_flag, nullptr, 0, stream);
+}
+
+extern "C" int64_t lithe_sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out) {
+    return lithe::sgmv_workspace_bytes(batch, d_in, d_out);
+}
+
+extern "C" int32_t lithe_sgmv_index_ws(const void* x, void* out, int32_t accumulate, const lithe_index_view* idx_a,
+                                       const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids,
+                                       const float* weights, int32_t batch, int32_t m, int32_t d_in, int32_t d_out,
+                                       int32_t rank, const float* lut, float scaling, int32_t* err_flag,
+                                       void* workspace, int64_t workspace_bytes, void* stream) {
+    lithe::clear_error();
+    if (batch > 0 && m > 0 && !workspace) return lithe::fail_arg("workspace is NULL");
+    return lithe::sgmv_index_impl(x, out, accumulate, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
+                                  rank, lut, scaling, err_flag, workspace, workspace_bytes, stream);
 }

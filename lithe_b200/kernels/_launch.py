@@ -77,10 +77,27 @@ def level_major_view(idx: torch.Tensor) -> _lib.IndexView:
     return index_view(idx, fmt, idx.shape[1], idx.shape[1] * idx.shape[2], 0, idx.shape[2])
 
 
+# Which form of the fused op the layers use: "fused" decodes the factor chunks inside the SGMV
+# kernel for every 64-token tile (lithe_sgmv_index); "staged" decodes each routed adapter's
+# chunks once per call into a workspace (lithe_sgmv_index_ws) and streams them with the tiles.
+# Results are bit-identical; on B200 the fused form is faster on every FLUX shape measured
+# (the staged main loop pays a second bulk copy per stage), so it is the default.
+DEFAULT_MODE = "fused"
+
+
+def workspace_bytes(batch: int, d_in: int, d_out: int) -> int:
+    return int(_lib.lib().lithe_sgmv_workspace_bytes(batch, d_in, d_out))
+
+
 def sgmv_index_(x: torch.Tensor, out: torch.Tensor, *, accumulate: bool, view_a: _lib.IndexView,
                 view_b: _lib.IndexView, n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor],
-                rank: int, lut: np.ndarray, scaling: float, err: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """lithe_sgmv_index on torch tensors; ``out`` (B, M, d_out) bf16 is written in place."""
+                rank: int, lut: np.ndarray, scaling: float, err: Optional[torch.Tensor] = None,
+                mode: Optional[str] = None, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """lithe_sgmv_index(_ws) on torch tensors; ``out`` (B, M, d_out) bf16 is written in place.
+
+    ``mode`` "fused" or "staged" (None: DEFAULT_MODE); a staged call takes ``workspace``
+    (uint8 CUDA tensor) or allocates one from torch's caching allocator.
+    """
     _require_cuda(x, "x")
     if x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
         raise TypeError(f"x and out must be bfloat16 (got {x.dtype}, {out.dtype})")
@@ -98,13 +115,23 @@ def sgmv_index_(x: torch.Tensor, out: torch.Tensor, *, accumulate: bool, view_a:
     if err is None:
         err = error_word(x.device)
     bsz, m, d_in = x.shape
+    mode = mode or DEFAULT_MODE
+    if mode not in ("staged", "fused"):
+        raise ValueError(f"mode must be 'staged' or 'fused', got {mode!r}")
+    common = (x.data_ptr(), out.data_ptr(), 1 if accumulate else 0, ctypes.byref(view_a), ctypes.byref(view_b),
+              int(n_slots), ids.data_ptr(), weights.data_ptr() if weights is not None else None,
+              bsz, m, d_in, out.shape[2], int(rank), lut_array(lut), float(scaling), err.data_ptr())
     with torch.cuda.device(x.device):
-        rc = _lib.lib().lithe_sgmv_index(
-            x.data_ptr(), out.data_ptr(), 1 if accumulate else 0, ctypes.byref(view_a), ctypes.byref(view_b),
-            int(n_slots), ids.data_ptr(), weights.data_ptr() if weights is not None else None,
-            bsz, m, d_in, out.shape[2], int(rank), lut_array(lut), float(scaling), err.data_ptr(),
-            stream_handle(x.device))
-    _lib.check(rc, "lithe_sgmv_index")
+        if mode == "fused":
+            rc = _lib.lib().lithe_sgmv_index(*common, stream_handle(x.device))
+        else:
+            need = workspace_bytes(bsz, d_in, out.shape[2])
+            if workspace is None or workspace.numel() < need:
+                workspace = torch.empty(max(need, 16), dtype=torch.uint8, device=x.device)
+            _require_cuda(workspace, "workspace")
+            rc = _lib.lib().lithe_sgmv_index_ws(*common, workspace.data_ptr(), workspace.numel(),
+                                                stream_handle(x.device))
+    _lib.check(rc, "lithe_sgmv_index" if mode == "fused" else "lithe_sgmv_index_ws")
     return out
 
 

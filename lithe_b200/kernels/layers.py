@@ -6,6 +6,9 @@
                      delta tensor, no second pass over the output).
 ``PackedLoRALinear`` the same over a shared ``PackedBank`` (9-bit packed residency): many
                      modules and thousands of slots in one device tensor.
+``PerSampleLoRALinear`` decoded (dense bf16) factors per slot, the dense resident-LoRA
+                     comparator (lithe/kernels/layers.py:28-95): per-sample delta with two
+                     batched cuBLAS products (``kernel="sgmv"``) or a per-sample loop.
 Routing: with ``assign`` unset every sample uses slot 0 (lithe/kernels/layers.py:263-265);
 otherwise ``assign`` (B,) gives the slot of every sample, -1 for none.
 """
@@ -98,6 +101,70 @@ class PackedLoRALinear(nn.Module):
             assign = torch.zeros(x3.shape[0], dtype=torch.int32, device=x.device)
         packed_codebook_lora_delta_(out3, x3, self.bank, self.name, assign, scaling=self.scaling,
                                     weights=self.weights)
+        return out
+
+
+class PerSampleLoRALinear(nn.Module):
+    """y = W x + scale_j * B_j A_j x for the slot j of every sample, from decoded factors.
+
+    ``set_factors([(A (r, d_in), B (d_out, r), scale), ...])`` installs the slots by reference;
+    with ``per_sample=False`` slot 0 applies to every sample.  The batched form stacks the
+    factors once and runs two cuBLAS bmm calls plus an in-place add per forward; this is the
+    dense comparator of the index-resident kernel, not part of the index-resident path.
+    """
+
+    def __init__(self, base: nn.Linear, kernel: str = "sgmv"):
+        super().__init__()
+        if kernel not in ("sgmv", "loop"):
+            raise ValueError(f"kernel must be 'sgmv' or 'loop', got {kernel!r}")
+        self.base = base
+        for p in self.base.parameters():
+            p.requires_grad_(False)
+        self.kernel = kernel
+        self.factors = []
+        self.per_sample = False
+        self.assign: Optional[torch.Tensor] = None
+        self._stacked = None
+
+    def set_factors(self, factors, per_sample: bool = True) -> None:
+        self.factors = list(factors)
+        self.per_sample = per_sample
+        self._stacked = None
+
+    def clear(self) -> None:
+        self.set_factors([], per_sample=False)
+
+    def _build_stacked(self, dtype):
+        if self._stacked is None or self._stacked[0].dtype != dtype:
+            a = torch.stack([f[0] for f in self.factors]).to(dtype).contiguous()
+            b = torch.stack([f[1] for f in self.factors]).to(dtype).contiguous()
+            s = torch.tensor([float(f[2]) for f in self.factors], dtype=torch.float32, device=a.device)
+            self._stacked = (a, b, s)
+        return self._stacked
+
+    def forward(self, x: torch.Tensor) -> torch.Tensor:
+        out = self.base(x)
+        if not self.factors:
+            return out
+        _inference_only(out)
+        if not self.per_sample:
+            a, b, sc = self.factors[0]
+            return out + nn.functional.linear(nn.functional.linear(x, a.to(x.dtype)), b.to(x.dtype)) * sc
+        x3, out3 = _as3d(x, out)
+        bsz = x3.shape[0]
+        if self.kernel == "loop":
+            slots = [i % len(self.factors) for i in range(bsz)] if self.assign is None else self.assign.tolist()
+            for i, j in enumerate(slots):
+                a, b, sc = self.factors[j]
+                out3[i] += nn.functional.linear(nn.functional.linear(x3[i], a.to(x.dtype)), b.to(x.dtype)) * sc
+            return out
+        a, b, sc = self._build_stacked(x.dtype)
+        if self.assign is not None or bsz != a.shape[0]:
+            idx = (self.assign.to(device=x.device, dtype=torch.long) if self.assign is not None
+                   else torch.arange(bsz, device=x.device) % a.shape[0])
+            a, b, sc = a.index_select(0, idx), b.index_select(0, idx), sc.index_select(0, idx)
+        mid = torch.bmm(x3, a.transpose(1, 2)) * sc.to(x.dtype).view(-1, 1, 1)
+        out3.baddbmm_(mid, b.transpose(1, 2))
         return out
 
 

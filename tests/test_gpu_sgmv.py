@@ -33,7 +33,7 @@ def _banks(ads, fmt):
     return _launch.level_major_view(ia), _launch.level_major_view(ib), (ia, ib)
 
 
-def run_fused(x, ads, assign, fmt="packed", accumulate=False, out=None, weights=None, scaling=1.0):
+def run_fused(x, ads, assign, fmt="packed", accumulate=False, out=None, weights=None, scaling=1.0, mode=None):
     va, vb, keep = _banks(ads, fmt)
     d_out = ads[0].modules[0]["shape_b"][0]
     r = ads[0].rank
@@ -43,7 +43,7 @@ def run_fused(x, ads, assign, fmt="packed", accumulate=False, out=None, weights=
     w = None if weights is None else torch.tensor(weights, dtype=torch.float32, device="cuda")
     lut = cb.kernel_lut(*cb.twin_pools())
     _launch.sgmv_index_(x, out, accumulate=accumulate, view_a=va, view_b=vb, n_slots=len(ads), ids=ids, weights=w,
-                        rank=r, lut=lut, scaling=scaling)
+                        rank=r, lut=lut, scaling=scaling, mode=mode)
     torch.cuda.synchronize()
     del keep
     return out
@@ -305,3 +305,38 @@ def test_flux_shapes_full_batch(d_in, d_out):
         got = out[b, rows].float().cpu()
         assert max_abs_rel(got, want) <= MAX_ABS_REL and rel_fro(got, want) < REL_FRO, b
     assert device_errors() == 0
+
+
+@pytest.mark.parametrize("seq,d_in,d_out,r", [(130, 1024, 4096, 16), (77, 512, 640, 8), (1, 256, 384, 4),
+                                              (33, 256, 128, 1), (64, 4096, 1024, 16)])
+@pytest.mark.parametrize("fmt", ["packed", "i16"])
+def test_staged_and_fused_modes_are_bit_identical(seq, d_in, d_out, r, fmt):
+    """lithe_sgmv_index_ws (decode once into a workspace) == lithe_sgmv_index (decode per tile)."""
+    ads = [random_adapter([("l", d_in, d_out)], rank=r, seed=s + 20) for s in range(3)]
+    x = torch.randn(5, seq, d_in, generator=torch.Generator().manual_seed(seq)).bfloat16().cuda()
+    base = (torch.randn(5, seq, d_out, generator=torch.Generator().manual_seed(d_out)) * 0.1).bfloat16().cuda()
+    assign = [2, -1, 0, 1, 2]
+    for acc in (False, True):
+        a = run_fused(x, ads, assign, fmt, accumulate=acc, out=base.clone() if acc else None, weights=[1.0, 1.0, 0.5, 2.0, 1.0],
+                      scaling=0.75, mode="staged")
+        b = run_fused(x, ads, assign, fmt, accumulate=acc, out=base.clone() if acc else None, weights=[1.0, 1.0, 0.5, 2.0, 1.0],
+                      scaling=0.75, mode="fused")
+        assert torch.equal(a, b)
+    assert device_errors() == 0
+
+
+def test_staged_mode_workspace_checks():
+    ads = [random_adapter([("l", 256, 256)], rank=16, seed=1)]
+    x = torch.randn(2, 8, 256, dtype=torch.bfloat16, device="cuda")
+    need = _launch.workspace_bytes(2, 256, 256)
+    assert need == 2 * (4 + 4) * 512
+    small = torch.empty(need - 512, dtype=torch.uint8, device="cuda")
+    va, vb, keep = _banks(ads, "packed")
+    out = torch.empty(2, 8, 256, dtype=torch.bfloat16, device="cuda")
+    ids = torch.zeros(2, dtype=torch.int32, device="cuda")
+    from lithe_b200 import _lib
+    import ctypes
+    rc = _lib.lib().lithe_sgmv_index_ws(x.data_ptr(), out.data_ptr(), 0, ctypes.byref(va), ctypes.byref(vb), 1,
+                                        ids.data_ptr(), None, 2, 8, 256, 256, 16, _launch.lut_array(cb.kernel_lut(*cb.twin_pools())),
+                                        1.0, None, small.data_ptr(), small.numel(), None)
+    assert rc == _lib.ERR_ARG and b"workspace" in _lib.lib().lithe_last_error()

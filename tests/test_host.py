@@ -167,3 +167,14 @@ def test_flux_target_count():
         names += [f"single_transformer_blocks.{i}.attn.{t}" for t in ("to_q", "to_k", "to_v")]
         names += [f"single_transformer_blocks.{i}.{t}" for t in ("proj_mlp", "proj_out", "norm.linear")]
     assert sum(_match(n, FLUX_TARGET_MODULES) for n in names) == 342
+
+
+def test_flux_shaped_model_targets_342_linears():
+    from lithe_b200.flux_model import FluxShapedTransformer, lora_targets
+    with torch.device("meta"):
+        model = FluxShapedTransformer()
+    targets = lora_targets(model)
+    assert len(targets) == 342
+    shapes = sorted({(m.in_features, m.out_features) for _, m in targets})
+    assert shapes == [(3072, 3072), (3072, 12288), (12288, 3072)]
+    assert 11.5e9 < sum(p.numel() for p in model.parameters()) < 12.5e9
