@@ -115,8 +115,10 @@ LITHE_API int64_t lithe_sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_
  * results (bit for bit).  A first kernel decodes every routed sample's A and B factors once
  * into `workspace` (512 bytes per 64-column chunk, 16 distinct values per block thanks to the
  * codebook's period-16 structure); the SGMV kernel then copies each chunk next to its
- * activation tile instead of re-decoding it for every 64-token tile.  Preferable when d_in is
- * large (decode-bound shrink).  Replaces the same reference code as lithe_sgmv_index.
+ * activation tile instead of re-decoding it for every 64-token tile.  Measured on B200 it is
+ * slower than lithe_sgmv_index on every FLUX shape (the main loop pays a second bulk copy per
+ * stage, more than the decode it saves); it is kept for callers that decode once and reuse the
+ * workspace layout.  Replaces the same reference code as lithe_sgmv_index.
  *   workspace        device, 16-byte aligned, >= lithe_sgmv_workspace_bytes(batch, d_in, d_out);
  *                    contents on entry do not matter; calls sharing one workspace must be
  *                    ordered on one stream.
