@@ -130,6 +130,35 @@ LITHE_API int32_t lithe_sgmv_index_ws(const void* x, void* out, int32_t accumula
                          const float* lut, float scaling, int32_t* err_flag,
                          void* workspace, int64_t workspace_bytes, void* stream);
 
+/* Size of the built-in workspace of lithe_sgmv_index_noalloc (4 MiB per device). */
+#define LITHE_NOALLOC_WS_BYTES (4LL << 20)
+
+/*
+ * lithe_sgmv_index_ws without the caller's workspace: an entry point that allocates no memory
+ * of any kind.  It has no counterpart in the reference, which allocates its outputs and
+ * scratch through PyTorch on every call.  It is meant for callers that cannot allocate device
+ * memory on the request path: a C or C++ host that binds this library without PyTorch, whose
+ * only allocator is cudaMalloc (which synchronises the device and can fail under memory
+ * pressure in the middle of serving), or a serving loop that runs under a fixed memory budget.
+ * The decoded factors go to a static device array of LITHE_NOALLOC_WS_BYTES that is part of the
+ * library's image on each device; results equal lithe_sgmv_index's bit for bit.
+ *   - Limit: lithe_sgmv_workspace_bytes(batch, d_in, d_out) must be <= LITHE_NOALLOC_WS_BYTES
+ *     (e.g. batch 34 at d_in 3072, d_out 12288); a larger call returns LITHE_ERR_UNSUPPORTED
+ *     and launches nothing.  Use lithe_sgmv_index or lithe_sgmv_index_ws for it.
+ *   - Set-up: the first call on each device looks up the array's device address with that
+ *     device current (a runtime call); make that first call before any stream capture starts.
+ *   - Nothing has to start at zero: every workspace byte the SGMV kernel reads is written by
+ *     the same call's decode kernel.
+ *   - Races: all calls on one device share the one array.  Two calls in flight at the same
+ *     time on that device (different streams, or host threads without ordering) overwrite each
+ *     other's factors; issue them on one stream or order them with events.
+ */
+LITHE_API int32_t lithe_sgmv_index_noalloc(const void* x, void* out, int32_t accumulate,
+                         const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                         int64_t n_slots, const int32_t* ids, const float* weights,
+                         int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank,
+                         const float* lut, float scaling, int32_t* err_flag, void* stream);
+
 /*
  * Whole-adapter decode of a packed stream into dense 64-value blocks (replaces
  * _decode_packed_kernel / decode_packed, lithe/kernels/packed.py:151-177,205-222).

@@ -29,6 +29,7 @@ DTYPE_BF16 = 0
 DTYPE_F32 = 1
 
 MAX_LEVELS = 4
+NOALLOC_WS_BYTES = 4 << 20       # LITHE_NOALLOC_WS_BYTES
 ABI_VERSION = 1
 
 # Every symbol include/lithe_b200.h declares, with (restype, argtypes).
@@ -62,6 +63,10 @@ _SIGNATURES.update({
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64,
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32,
         _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p]),
+    "lithe_sgmv_index_noalloc": (_c.c_int32, [
+        _c.c_void_p, _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64,
+        _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32,
+        _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p, _c.c_void_p]),
     "lithe_decode_packed": (_c.c_int32, [
         _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_void_p, _c.POINTER(_c.c_float), _c.c_void_p,
         _c.c_int32, _c.c_void_p]),

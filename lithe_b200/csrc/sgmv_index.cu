@@ -29,6 +29,8 @@
 // columns repeated 4 times, so delta = h . B^T is 2 mma.m16n8k16 (n = 16 logical
 // columns, k = 16 ranks) and each thread adds its 2 results to 8 output values per row.
 // The stage is released as soon as the tile is in registers; the stores need no proxy fence.
+#include <mutex>
+
 #include "device_common.cuh"
 #include "host_common.h"
 
@@ -726,4 +728,56 @@ extern "C" int32_t lithe_sgmv_index_ws(const void* x, void* out, int32_t accumul
     if (batch > 0 && m > 0 && !workspace) return lithe::fail_arg("workspace is NULL");
     return lithe::sgmv_index_impl(x, out, accumulate, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
                                   rank, lut, scaling, err_flag, workspace, workspace_bytes, stream);
+}
+
+// ---- lithe_sgmv_index_noalloc: the staged form over a static device workspace ----
+
+namespace lithe {
+
+// The workspace of lithe_sgmv_index_noalloc: one array per device, part of the module image,
+// so calls never allocate.  256-byte alignment covers the 16-byte bulk-copy rule.
+static __device__ __align__(256) uint8_t g_noalloc_ws[LITHE_NOALLOC_WS_BYTES];
+
+// Device address of g_noalloc_ws on the current device, looked up on the first call per device.
+static int32_t noalloc_workspace(void** ptr) {
+    static std::mutex mu;
+    static void* addr[64] = {};
+    int device = 0;
+    cudaError_t e = cudaGetDevice(&device);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
+    if (device < 0 || device >= 64) return fail_unsupported("device ordinal %d", device);
+    std::lock_guard<std::mutex> lock(mu);
+    if (!addr[device]) {
+        void* a = nullptr;
+        e = cudaGetSymbolAddress(&a, g_noalloc_ws);
+        if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(noalloc workspace)");
+        if (!a) return fail_arg("cudaGetSymbolAddress returned NULL for the noalloc workspace");
+        addr[device] = a;
+    }
+    *ptr = addr[device];
+    return LITHE_OK;
+}
+
+}  // namespace lithe
+
+extern "C" int32_t lithe_sgmv_index_noalloc(const void* x, void* out, int32_t accumulate,
+                                            const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                                            int64_t n_slots, const int32_t* ids, const float* weights,
+                                            int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank,
+                                            const float* lut, float scaling, int32_t* err_flag, void* stream) {
+    lithe::clear_error();
+    if (batch <= 0 || m <= 0)   // validated and, when empty, a no-op, exactly as lithe_sgmv_index
+        return lithe::sgmv_index_impl(x, out, accumulate, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in,
+                                      d_out, rank, lut, scaling, err_flag, nullptr, 0, stream);
+    const int64_t need = lithe::sgmv_workspace_bytes(batch, d_in, d_out);
+    if (need > LITHE_NOALLOC_WS_BYTES)
+        return lithe::fail_unsupported(
+            "lithe_sgmv_index_noalloc: batch %d x (d_in %d, d_out %d) needs %lld workspace bytes, the built-in "
+            "workspace holds %lld; use lithe_sgmv_index or lithe_sgmv_index_ws",
+            batch, d_in, d_out, (long long)need, (long long)LITHE_NOALLOC_WS_BYTES);
+    void* ws = nullptr;
+    const int32_t rc = lithe::noalloc_workspace(&ws);
+    if (rc != LITHE_OK) return rc;
+    return lithe::sgmv_index_impl(x, out, accumulate, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
+                                  rank, lut, scaling, err_flag, ws, LITHE_NOALLOC_WS_BYTES, stream);
 }
