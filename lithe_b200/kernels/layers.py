@@ -14,7 +14,7 @@ otherwise ``assign`` (B,) gives the slot of every sample, -1 for none.
 """
 from __future__ import annotations
 
-from typing import Callable, Dict, Iterable, Optional
+from typing import Callable, Dict, Iterable, Optional, Tuple
 
 import torch
 from torch import nn
@@ -74,19 +74,29 @@ class IndexLoRALinear(nn.Module):
 
 
 class PackedLoRALinear(nn.Module):
-    """y = W x + per-sample delta from module ``name`` of a shared packed bank."""
+    """y = W x + per-sample delta from module ``name`` of a shared packed bank.
 
-    def __init__(self, base: nn.Linear, bank: PackedBank, name: str, rank: int, scaling: float):
+    ``rows`` = (r0, r1) serves one split target of a fused module (B rows [r0, r1), e.g. the
+    k projection of a Kohya ``attn_qkv``) straight from the resident slot.
+    """
+
+    def __init__(self, base: nn.Linear, bank: PackedBank, name: str, rank: int, scaling: float,
+                 rows: Optional[Tuple[int, int]] = None):
         super().__init__()
         self.base = base
         for p in self.base.parameters():
             p.requires_grad_(False)
         i = bank.layout.index(name)
-        if bank.layout.shapes_a[i] != (rank, base.in_features) or bank.layout.shapes_b[i] != (base.out_features, rank):
-            raise ValueError(f"{name}: bank shapes {bank.layout.shapes_a[i]}, {bank.layout.shapes_b[i]} do not "
-                             f"match the linear ({base.in_features} -> {base.out_features}, r={rank})")
+        sa, sb = bank.layout.shapes_a[i], bank.layout.shapes_b[i]
+        d_out = sb[0] if rows is None else int(rows[1]) - int(rows[0])
+        if sa != (rank, base.in_features) or sb[1] != rank or d_out != base.out_features:
+            raise ValueError(f"{name}: bank shapes {sa}, {sb} (rows {rows}) do not match the linear "
+                             f"({base.in_features} -> {base.out_features}, r={rank})")
+        if rows is not None:
+            bank.views(name, rows)           # validates the range and its block alignment
         self.bank = bank
         self.name = name
+        self.rows = None if rows is None else (int(rows[0]), int(rows[1]))
         self.rank = int(rank)
         self.scaling = float(scaling)
         self.assign: Optional[torch.Tensor] = None
@@ -100,7 +110,7 @@ class PackedLoRALinear(nn.Module):
         if assign is None:
             assign = torch.zeros(x3.shape[0], dtype=torch.int32, device=x.device)
         packed_codebook_lora_delta_(out3, x3, self.bank, self.name, assign, scaling=self.scaling,
-                                    weights=self.weights)
+                                    weights=self.weights, rows=self.rows)
         return out
 
 
@@ -182,6 +192,33 @@ def wrap_linears(model: nn.Module, paths: Iterable[str],
         setattr(parent, child, module)
         wrapped[path] = module
     return wrapped
+
+
+def wrap_packed(model: nn.Module, bank: PackedBank, key_format: str = "diffusers",
+                paths: Optional[Iterable[str]] = None, scaling: Optional[float] = None) -> Dict[str, PackedLoRALinear]:
+    """Serve every linear the bank's layout covers from the resident packed bank.
+
+    For a Kohya-format layout (304 fused modules) each diffusers linear (494) reads its own B
+    rows of the fused module in place (``lithe_b200.kohya.split_targets``).  ``paths`` limits
+    the wrapped set (e.g. the 342 attention / feed-forward linears); ``scaling`` defaults to
+    the layout's alpha / rank.  Set ``.assign`` on the returned modules to route samples.
+    """
+    from .. import kohya
+    lay = bank.layout
+    targets = kohya.split_targets(lay.names, lay.shapes_a, lay.shapes_b, key_format, lay.block_size)
+    want = list(targets) if paths is None else list(paths)
+    missing = [p for p in want if p not in targets]
+    if missing:
+        raise KeyError(f"the bank's layout does not cover {missing[:3]}{'...' if len(missing) > 3 else ''}")
+    s = lay.scaling if scaling is None else float(scaling)
+
+    def factory(path, lin):
+        name, r0, r1 = targets[path]
+        rank = lay.shapes_a[lay.index(name)][0]
+        full = r0 == 0 and r1 == lay.shapes_b[lay.index(name)][0]
+        return PackedLoRALinear(lin, bank, name, rank, s, rows=None if full else (r0, r1))
+
+    return wrap_linears(model, want, factory)
 
 
 def pools_on(device, dtype=torch.float32):

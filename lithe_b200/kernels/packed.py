@@ -235,11 +235,27 @@ class PackedBank:
         view = self.words if slots is None else self.words[slots]
         view.random_(generator=g)
 
-    def views(self, name: str) -> Tuple[_lib.IndexView, _lib.IndexView]:
+    def views(self, name: str, rows: Optional[Tuple[int, int]] = None) -> Tuple[_lib.IndexView, _lib.IndexView]:
+        """C-ABI index views of module ``name``: A, and B (or only B rows [r0, r1) of it).
+
+        A row range starts the B view at block r0*rank/block_size of the module's B stream,
+        so one fused module (Kohya q/k/v) serves each of its split targets in place.
+        """
         i = self.layout.index(name)
         L = self.layout.num_levels
+        b_first = 0
+        if rows is not None:
+            r0, r1 = (int(v) for v in rows)
+            d_out, rank = self.layout.shapes_b[i]
+            bs = self.layout.block_size
+            if not 0 <= r0 < r1 <= d_out:
+                raise ValueError(f"{name}: rows {r0}:{r1} outside [0, {d_out})")
+            if (r0 * rank) % bs or (r1 * rank) % bs:
+                raise ValueError(f"{name}: split at rows {r0}:{r1} is not block aligned")
+            b_first = r0 * rank // bs
         va = _launch.index_view(self.words, _lib.IDX_PACKED9, L, self.slot_stride, L * self.layout.a_off[i])
-        vb = _launch.index_view(self.words, _lib.IDX_PACKED9, L, self.slot_stride, L * self.layout.b_off[i])
+        vb = _launch.index_view(self.words, _lib.IDX_PACKED9, L, self.slot_stride,
+                                L * (self.layout.b_off[i] + b_first))
         return va, vb
 
     def decode(self, slot_ids, dtype: torch.dtype = torch.bfloat16, out: Optional[torch.Tensor] = None) -> torch.Tensor:

@@ -16,7 +16,7 @@ allocating a delta (the path the layer wrappers use).
 """
 from __future__ import annotations
 
-from typing import Optional
+from typing import Optional, Tuple
 
 import torch
 
@@ -90,18 +90,20 @@ def shared_codebook_lora_delta(x: torch.Tensor, idx_A: torch.Tensor, pools_A: to
 
 def packed_codebook_lora_delta_(out: torch.Tensor, x: torch.Tensor, bank, name: str, assign: torch.Tensor,
                                 scaling: Optional[float] = None, weights: Optional[torch.Tensor] = None,
-                                accumulate: bool = True) -> torch.Tensor:
+                                accumulate: bool = True, rows: Optional[Tuple[int, int]] = None) -> torch.Tensor:
     """out (B, M, d_out) bf16 += per-sample delta of module ``name`` of a ``PackedBank``, in place.
 
     The packed counterpart of ``shared_codebook_lora_delta_``: the kernel reads the bank's
-    9-bit packed words directly.  ``scaling`` defaults to the layout's alpha / rank.
+    9-bit packed words directly.  ``scaling`` defaults to the layout's alpha / rank.  ``rows``
+    = (r0, r1) applies only B rows [r0, r1) of the module (d_out = r1 - r0): one target of a
+    fused Kohya module, read in place from the resident slot.
     """
     i = bank.layout.index(name)
     rank, d_in = bank.layout.shapes_a[i]
-    d_out = bank.layout.shapes_b[i][0]
+    d_out = bank.layout.shapes_b[i][0] if rows is None else int(rows[1]) - int(rows[0])
     if x.dim() != 3 or x.shape[-1] != d_in or out.shape != (x.shape[0], x.shape[1], d_out):
         raise ValueError(f"{name}: x must be (B, M, {d_in}) and out (B, M, {d_out})")
-    va, vb = bank.views(name)
+    va, vb = bank.views(name, rows)
     ids = assign.to(device=x.device, dtype=torch.int32).contiguous()
     w = None if weights is None else weights.to(device=x.device, dtype=torch.float32).contiguous()
     return _launch.sgmv_index_(x.contiguous(), out, accumulate=accumulate, view_a=va, view_b=vb,

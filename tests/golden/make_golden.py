@@ -21,6 +21,10 @@ reference itself.  Fixtures:
                     shapes of the reference's GPU test
   small.lithe       a .lithe file written by the reference's save_lithe (+ small_lithe.npz
                     with its indices and header fields)
+  kohya_split.npz   lithe.kohya on two Kohya-format adapters (rank 4 at d=64 as in the
+                    reference's tests, rank 16 at d=128): diffusers_paths and every
+                    split_indices entry; and split_spec over the full Kohya-304 FLUX.1-dev
+                    module set (19 double x 10 + 38 single x 3 modules)
 """
 from __future__ import annotations
 
@@ -38,7 +42,7 @@ REF = os.environ.get("LITHE_REF", "/root/reference")
 sys.path.insert(0, REF)
 
 from lithe import codebook as cb  # noqa: E402
-from lithe import fileio, quant, serve  # noqa: E402
+from lithe import fileio, kohya, quant, serve  # noqa: E402
 from lithe.kernels import packed, shared  # noqa: E402
 
 SMALL = [("blk.0.q", 128, 192), ("blk.0.mlp", 128, 320), ("blk.0.out", 320, 128), ("odd", 96, 40),
@@ -178,6 +182,51 @@ def make_lithe_file():
                         header=np.array(json.dumps(fileio.read_header(HERE / "small.lithe"))), **arrays)
 
 
+def kohya_like(seed, d, mlp, rank):
+    mods = [("lora_unet_double_blocks_0_img_attn_qkv", d, 3 * d),
+            ("lora_unet_double_blocks_0_txt_attn_qkv", d, 3 * d),
+            ("lora_unet_double_blocks_0_txt_mlp_0", d, mlp),
+            ("lora_unet_double_blocks_0_img_mod_lin", d, 6 * d),
+            ("lora_unet_single_blocks_0_linear1", d, 3 * d + mlp),
+            ("lora_unet_single_blocks_0_linear2", d + mlp, d),
+            ("lora_unet_single_blocks_0_modulation_lin", d, 3 * d)]
+    return adapter(mods, rank=rank, seed=seed, key_format="kohya")
+
+
+def kohya_304_names(hidden=3072, mlp=12288, rank=16):
+    mods = []
+    for i in range(19):
+        for s in ("img", "txt"):
+            mods += [(f"lora_unet_double_blocks_{i}_{s}_attn_qkv", hidden, 3 * hidden),
+                     (f"lora_unet_double_blocks_{i}_{s}_attn_proj", hidden, hidden),
+                     (f"lora_unet_double_blocks_{i}_{s}_mlp_0", hidden, mlp),
+                     (f"lora_unet_double_blocks_{i}_{s}_mlp_2", mlp, hidden),
+                     (f"lora_unet_double_blocks_{i}_{s}_mod_lin", hidden, 6 * hidden)]
+    for i in range(38):
+        mods += [(f"lora_unet_single_blocks_{i}_linear1", hidden, 3 * hidden + mlp),
+                 (f"lora_unet_single_blocks_{i}_linear2", hidden + mlp, hidden),
+                 (f"lora_unet_single_blocks_{i}_modulation_lin", hidden, 3 * hidden)]
+    return mods
+
+
+def make_kohya():
+    arrays = {}
+    for tag, (seed, d, mlp, rank) in {"r4": (5, 64, 128, 4), "r16": (11, 128, 256, 16)}.items():
+        ad = kohya_like(seed, d, mlp, rank)
+        arrays[f"{tag}/modules"] = np.array(json.dumps(ad.modules))
+        arrays[f"{tag}/paths"] = np.array(json.dumps(kohya.diffusers_paths(ad)))
+        for name in ad.indices:
+            arrays[f"{tag}/idx/{name}/A"] = ad.indices[name]["A"]
+            arrays[f"{tag}/idx/{name}/B"] = ad.indices[name]["B"]
+        for path, (ia, ib, sa, sb) in kohya.split_indices(ad).items():
+            arrays[f"{tag}/split/{path}/A"] = np.asarray(ia)
+            arrays[f"{tag}/split/{path}/B"] = np.asarray(ib)
+            arrays[f"{tag}/split/{path}/shapes"] = np.array([*sa, *sb])
+    spec = {name: kohya.split_spec(name, [16, d_in], [d_out, 16]) for name, d_in, d_out in kohya_304_names()}
+    arrays["k304/spec"] = np.array(json.dumps(spec))
+    np.savez_compressed(HERE / "kohya_split.npz", **arrays)
+
+
 if __name__ == "__main__":
     torch.set_num_threads(max(1, os.cpu_count() or 1))
     make_codebook()
@@ -186,6 +235,7 @@ if __name__ == "__main__":
     make_config1()
     make_shared()
     make_lithe_file()
+    make_kohya()
     for p in sorted(HERE.iterdir()):
         if p.suffix in (".npz", ".lithe"):
             print(f"{p.name:22s} {p.stat().st_size:>9d} B")
