@@ -628,6 +628,236 @@ def run_denoise(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------- hot-swap workload
+HOTSWAP_PER_STEP = 14          # adapters made resident per step
+HOTSWAP_FILES = 4              # distinct .lithe files written for the file-path leg (cycled)
+
+
+def _hotswap_payloads(n_indices: int, n: int, seed: int):
+    return [np.random.default_rng(seed + i).integers(0, 512, n_indices).astype("<u2") for i in range(n)]
+
+
+def _write_lithe_files(modules, payloads, folder: Path):
+    """Kohya-format .lithe files of the given raw payloads (written in parallel: LZMA preset 9e)."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    from lithe_b200.fileio import LitheAdapter, save_lithe
+    from lithe_b200.kernels import PackedLayout
+    lay = PackedLayout.from_modules(modules)
+    n_a = [b - a for a, b in zip(lay.a_off, lay.b_off)]
+    n_b = [sb[0] * sb[1] // lay.block_size for sb in lay.shapes_b]
+
+    def split(raw):                       # the payload order: every A matrix, then every B matrix
+        out, pos = {}, 0
+        for side, counts in (("A", n_a), ("B", n_b)):
+            for name, n in zip(lay.names, counts):
+                out.setdefault(name, {})[side] = raw[pos:pos + 3 * n].reshape(3, n)
+                pos += 3 * n
+        return out
+
+    def one(i):
+        ad = LitheAdapter(modules=modules, indices=split(payloads[i]), rank=16, alpha=16.0, key_format="kohya")
+        path = folder / f"adapter{i}.lithe"
+        save_lithe(path, ad)
+        return path
+
+    with ThreadPoolExecutor(max_workers=len(payloads)) as pool:
+        return list(pool.map(one, range(len(payloads))))
+
+
+def cpu_hotswap_rate(paths, seconds: float):
+    """Oracle port of the reference's resident-slot load, one thread: load_lithe's LZMA +
+    checksum + split, flat_indices' reorder, pack_indices' packing (numpy)."""
+    from lithe_b200.fileio import read_payload
+    from oracle import decode_ref
+    t0 = time.perf_counter()
+    n = 0
+    while True:
+        header, raw = read_payload(paths[n % len(paths)])
+        decode_ref.pack_raw(raw, header["modules"])
+        n += 1
+        el = time.perf_counter() - t0
+        if el >= seconds:
+            return n / el, n, el
+
+
+def run_hotswap(args):
+    """.lithe -> resident-slot loading into a 10,000-slot Kohya-304 bank (41 GB).
+
+    value: device pack of 14 raw payloads already in HBM into 14 slots per step (14 launches of
+    lithe_pack_raw); e2e: the same from pinned host blobs (H2D inside the timed region, the
+    device error word read back per step); plus the .lithe-file path through SlotLoader (host
+    LZMA in a thread pool) and the single-adapter cold-swap latencies."""
+    from lithe_b200 import kohya
+    from lithe_b200.kernels import PackedBank, PackedLayout, SlotLoader
+    from lithe_b200.kernels import _launch as _lk
+
+    metric = "Kohya-304 adapters made resident per second (raw .lithe payload -> packed bank slot)"
+    world, rank, local = dist_env()
+    mods = kohya.kohya_flux_modules(rank=16)
+    layout = PackedLayout.from_modules(mods)
+    n_idx = layout.num_indices
+    tmp = Path(tempfile.mkdtemp(prefix="lithe_hotswap_"))
+    if args.impl == "reference":
+        if rank != 0:
+            return
+        paths = _write_lithe_files(mods, _hotswap_payloads(n_idx, HOTSWAP_FILES, 900), tmp)
+        steps = max(1, min(args.steps, 20))
+        rates = [cpu_hotswap_rate(paths, 0.0)[0] for _ in range(steps)]
+        v = statistics.median(rates)
+        print(json.dumps({"impl": "reference", "metric": metric, "value": v, "unit": "adapters/s", "n_gpus": args.gpus,
+                          "steps": steps, "warmup": 0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+                          "dtype": "u16 -> 9-bit packed u64", "data": "synthetic uniform 9-bit indices",
+                          "config": {"workload": args.workload},
+                          "cpu_baseline": {"value": v, "unit": "adapters/s", "cores": 1, "kind": "port",
+                                           "sample": "oracle port of load_lithe + pack_adapter, one adapter per step"},
+                          "e2e": {"value": v, "unit": "adapters/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}),
+              flush=True)
+        return
+    init_dist(world, local)
+    dev = torch.device("cuda", local)
+    bank = PackedBank(layout, BANK_SLOTS, dev)
+    payloads = _hotswap_payloads(n_idx, HOTSWAP_PER_STEP, 1000 + 100 * rank)
+    staging = torch.from_numpy(np.stack(payloads).view(np.int16)).to(dev)
+    slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(500 + rank))[:HOTSWAP_PER_STEP].tolist()
+    stream = torch.cuda.current_stream(dev)
+    err = _lk.error_word(dev)
+
+    def step_device():
+        for i, s in enumerate(slots):
+            bank.load_raw(s, staging[i], err)
+
+    for _ in range(args.warmup):
+        step_device()
+    torch.cuda.synchronize(dev)
+    # eager: one Python call + launch per adapter (host launch overhead included)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(args.steps):
+        step_device()
+    e1.record(stream)
+    torch.cuda.synchronize(dev)
+    eager_ms = e0.elapsed_time(e1) / args.steps
+    # timed: the 14 launches of a step captured once in a CUDA graph (device time of the packs)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        step_device()
+    for _ in range(args.warmup):
+        graph.replay()
+    torch.cuda.synchronize(dev)
+    barrier(world)
+    with ClockSampler(local) as clocks:
+        e0.record(stream)
+        for _ in range(args.steps):
+            graph.replay()
+        e1.record(stream)
+        torch.cuda.synchronize(dev)
+    barrier(world)
+    ms = max_over_ranks(e0.elapsed_time(e1) / args.steps, world)
+    value = HOTSWAP_PER_STEP * world / (ms / 1000.0)
+    del graph
+
+    # e2e: raw blobs in pinned host memory -> slots (H2D in the timed region, error word read back)
+    pinned = [torch.from_numpy(p.view(np.int16)).pin_memory() for p in payloads]
+    dstage = [torch.empty(n_idx, dtype=torch.int16, device=dev) for _ in range(2)]
+    err_host = torch.empty(1, dtype=torch.int32, pin_memory=True)
+
+    def step_e2e():
+        for i, s in enumerate(slots):
+            dstage[i % 2].copy_(pinned[i], non_blocking=True)
+            bank.load_raw(s, dstage[i % 2], err)
+        err_host.copy_(err, non_blocking=True)
+
+    step_e2e()
+    torch.cuda.synchronize(dev)
+    e2e_steps = max(1, min(args.steps, 10))
+    barrier(world)
+    f0, f1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    f0.record(stream)
+    for _ in range(e2e_steps):
+        step_e2e()
+    f1.record(stream)
+    torch.cuda.synchronize(dev)
+    e2e_ms = max_over_ranks(f0.elapsed_time(f1) / e2e_steps, world)
+
+    # .lithe files -> slots through SlotLoader (host LZMA + checksum in a thread pool), wall clock
+    paths = _write_lithe_files(mods, payloads[:HOTSWAP_FILES], tmp)
+    threads = os.cpu_count() or 1
+    loader = SlotLoader(bank, threads=threads, depth=4)
+    file_paths = [paths[i % len(paths)] for i in range(HOTSWAP_PER_STEP)]
+    loader.load_many(slots[:2], file_paths[:2])                       # warm-up
+    torch.cuda.synchronize(dev)
+    t0 = time.perf_counter()
+    loader.load_many(slots, file_paths)
+    torch.cuda.synchronize(dev)
+    files_s = time.perf_counter() - t0
+    one_t0 = time.perf_counter()
+    loader.load(slots[0], paths[0])
+    torch.cuda.synchronize(dev)
+    one_file_ms = (time.perf_counter() - one_t0) * 1000.0
+    # cold swap from a decompressed int16 blob in (pageable) host memory, then optionally decoded
+    from lithe_b200.fileio import read_payload
+    header, raw = read_payload(paths[1])
+    lat = []
+    for _ in range(5):
+        t = time.perf_counter()
+        loader.load_payload(slots[1], header, raw)
+        torch.cuda.synchronize(dev)
+        lat.append((time.perf_counter() - t) * 1000.0)
+    blob_ms = statistics.median(lat)
+    dec_out = torch.empty((1, layout.total_blocks, 64), dtype=torch.bfloat16, device=dev)
+    ids1 = torch.tensor([slots[1]], dtype=torch.int32, device=dev)
+    lat = []
+    for _ in range(5):
+        t = time.perf_counter()
+        loader.load_payload(slots[1], header, raw)
+        bank.decode(ids1, out=dec_out)
+        torch.cuda.synchronize(dev)
+        lat.append((time.perf_counter() - t) * 1000.0)
+    blob_dec_ms = statistics.median(lat)
+    errors = _lk.device_errors(dev)
+
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        rate, n, el = cpu_hotswap_rate(paths, args.cpu_seconds)
+        cpu = {"value": rate, "unit": "adapters/s", "cores": 1, "kind": "port",
+               "sample": f"oracle port of load_lithe + pack_adapter (LZMA, checksum, reorder, 9-bit pack), "
+                         f"{n} Kohya-304 files in {el:.1f} s"}
+    peak, peak_kind = measured_peaks()
+    per_adapter_bytes = 2 * n_idx + 8 * layout.num_words
+    achieved = HOTSWAP_PER_STEP * per_adapter_bytes / (ms / 1000.0) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": metric, "value": value, "unit": "adapters/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "u16 -> 9-bit packed u64", "data": "synthetic: seeded uniform 9-bit indices",
+            "config": {"workload": args.workload, "adapters_per_step": HOTSWAP_PER_STEP, "bank_slots": BANK_SLOTS,
+                       "raw_mb_per_adapter": 2 * n_idx / 1e6, "packed_mb_per_adapter": 8 * layout.num_words / 1e6,
+                       "l2": f"{HOTSWAP_PER_STEP * per_adapter_bytes / 1e6:.0f} MB moved per step (> L2), no flush"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                         "peak_source": f"hbm_gbs of {peak_kind}", "traffic": None,
+                         "algorithmic_bytes_per_launch": per_adapter_bytes,
+                         "timed": "14 launches per step replayed from one CUDA graph",
+                         "kernel": "lithe::pack_raw_kernel"},
+            "cpu_baseline": cpu,
+            "e2e": {"value": HOTSWAP_PER_STEP * world / (e2e_ms / 1000.0), "unit": "adapters/s",
+                    "h2d_bytes_per_step": HOTSWAP_PER_STEP * 2 * n_idx, "d2h_bytes_per_step": 4, "ms_per_step": e2e_ms,
+                    "api": "pinned raw blob -> cudaMemcpyAsync -> lithe_pack_raw"},
+            "lithe_files": {"adapters_per_s": HOTSWAP_PER_STEP / files_s, "threads": threads,
+                            "one_file_ms": one_file_ms,
+                            "host_lzma_checksum_s_per_file": loader.stats["host_s"] / max(1, loader.stats["files"]),
+                            "api": "SlotLoader.load_many (.lithe -> LZMA -> pinned -> H2D -> lithe_pack_raw)"},
+            "eager_ms_per_step": eager_ms, "cold_swap_raw_blob_ms": blob_ms, "cold_swap_raw_blob_then_decode_ms": blob_dec_ms,
+            "cold_swap_reference_a100_ms": 10.0,
+            "clocks": clocks.summary(),
+            "gpu_launches": args.steps * HOTSWAP_PER_STEP, "device_errors": errors}), flush=True)
+    import shutil
+    shutil.rmtree(tmp, ignore_errors=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def wrap_linears_any(model, names, table):
     """Point model.<name> at table[name] (swaps between plain, packed and dense wrappers)."""
     for n in names:
@@ -643,7 +873,7 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["lithe", "reference"], default="lithe")
     ap.add_argument("--workload", choices=["flux_sweep_b14", "decode_flux342", "decode_kohya304", "denoise_512",
-                                           "denoise_256_b96", "denoise_1024"],
+                                           "denoise_256_b96", "denoise_1024", "hotswap_kohya304"],
                     default="flux_sweep_b14", help="flux_sweep_b14: fused decode+SGMV (default); decode_*: "
                     "standalone packed decode of 14 resident adapters per launch")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")
@@ -673,6 +903,8 @@ def main():
         run_decode(args)
     elif args.workload.startswith("denoise_"):
         run_denoise(args)
+    elif args.workload == "hotswap_kohya304":
+        run_hotswap(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

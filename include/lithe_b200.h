@@ -187,6 +187,31 @@ LITHE_API int32_t lithe_decode_packed_batch(const uint64_t* bank, int64_t slot_s
                                   int32_t num_levels, const int8_t* sides, const float* lut,
                                   void* out, int32_t out_dtype, int32_t* err_flag, void* stream);
 
+/* One (module, side) of a .lithe payload: its packed blocks [first_block, first_block + n_blocks)
+ * come from raw[raw_offset + level * n_blocks + j], j = block - first_block. */
+typedef struct {
+    int64_t raw_offset;
+    int64_t first_block;
+    int64_t n_blocks;
+} lithe_pack_segment;
+
+/*
+ * Pack a raw .lithe index payload into one bank slot on the device (replaces the host-side
+ * load_lithe -> flat_indices -> pack_indices chain, lithe/fileio.py:119-152 and
+ * lithe/kernels/packed.py:38-52,125-143, that the reference runs for every adapter it makes
+ * resident).
+ *   raw        device uint16 (n_raw): every module's A matrix in header order, then every
+ *              module's B matrix, each (num_levels, n_blocks) row-major (the decompressed payload)
+ *   segments   device, n_segments entries sorted by first_block, covering blocks
+ *              [0, n_raw / num_levels) in packed (module A, module B, ...) order
+ *   words      device uint64 (n_words = ceil(n_raw / 7)), e.g. a bank slot
+ * Values above 511 and blocks the table does not cover set LITHE_DEVERR_INDEX in *err_flag
+ * (the value is masked to 9 bits / written as 0).  No allocation, no host synchronisation.
+ */
+LITHE_API int32_t lithe_pack_raw(const uint16_t* raw, int64_t n_raw, const lithe_pack_segment* segments,
+                       int32_t n_segments, int32_t num_levels, uint64_t* words, int64_t n_words,
+                       int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

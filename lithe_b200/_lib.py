@@ -53,6 +53,11 @@ class IndexView(ctypes.Structure):
     ]
 
 
+class PackSegment(ctypes.Structure):
+    """lithe_pack_segment: one (module, side) of a raw .lithe payload."""
+    _fields_ = [("raw_offset", ctypes.c_int64), ("first_block", ctypes.c_int64), ("n_blocks", ctypes.c_int64)]
+
+
 _SIGNATURES.update({
     "lithe_sgmv_index": (_c.c_int32, [
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64,
@@ -67,6 +72,9 @@ _SIGNATURES.update({
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64,
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32,
         _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p, _c.c_void_p]),
+    "lithe_pack_raw": (_c.c_int32, [
+        _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_int64, _c.c_void_p,
+        _c.c_void_p]),
     "lithe_decode_packed": (_c.c_int32, [
         _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_void_p, _c.POINTER(_c.c_float), _c.c_void_p,
         _c.c_int32, _c.c_void_p]),

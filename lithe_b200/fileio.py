@@ -19,7 +19,7 @@ import lzma
 import struct
 from dataclasses import dataclass, field
 from pathlib import Path
-from typing import Any, Dict, List
+from typing import Any, Dict, List, Tuple
 
 import numpy as np
 
@@ -118,7 +118,12 @@ def read_header(path) -> Dict[str, Any]:
     return _split_file(path)[0]
 
 
-def load_lithe(path, verify: bool = True) -> LitheAdapter:
+def read_payload(path, verify: bool = True) -> Tuple[Dict[str, Any], bytes]:
+    """(header, raw uint16-LE index payload) of a .lithe file, checked as ``load_lithe`` checks it.
+
+    The raw payload is every module's (L, nA) A matrix, then every module's (L, nB) B matrix
+    (``lithe/fileio.py:5-13``); the resident-bank loader copies it to the device as is.
+    """
     header, body = _split_file(path)
     try:
         raw = lzma.decompress(body)
@@ -132,13 +137,21 @@ def load_lithe(path, verify: bool = True) -> LitheAdapter:
             raise ValueError(f"{path}: codebook hash mismatch")
     if len(raw) % 2:
         raise ValueError(f"{path}: odd-length uint16 stream")
+    levels, bs = int(cbh["num_levels"]), int(cbh["block_size"])
+    total = sum(levels * (num_blocks(m["shape_a"], bs) + num_blocks(m["shape_b"], bs)) for m in header["modules"])
+    if total != len(raw) // 2:
+        raise ValueError(f"{path}: stream length {len(raw) // 2} does not match header")
+    return header, raw
+
+
+def load_lithe(path, verify: bool = True) -> LitheAdapter:
+    header, raw = read_payload(path, verify)
+    cbh = header["codebook"]
     stream = np.frombuffer(raw, dtype="<u2")
     levels, bs = int(cbh["num_levels"]), int(cbh["block_size"])
     modules = header["modules"]
     count_a = [levels * num_blocks(m["shape_a"], bs) for m in modules]
     count_b = [levels * num_blocks(m["shape_b"], bs) for m in modules]
-    if sum(count_a) + sum(count_b) != stream.size:
-        raise ValueError(f"{path}: stream length {stream.size} does not match header")
     indices: Dict[str, Dict[str, np.ndarray]] = {}
     pos = 0
     for m, c in zip(modules, count_a):

@@ -8,13 +8,13 @@
 """
 from ._launch import device_errors, raise_device_errors
 from .layers import IndexLoRALinear, PackedLoRALinear, PerSampleLoRALinear, wrap_linears, wrap_packed
-from .packed import (PackedBank, PackedLayout, decode_packed, flat_indices, pack_adapter, pack_indices,
-                     split_decoded, unpack_indices)
+from .packed import (PackedBank, PackedLayout, SlotLoader, decode_packed, flat_indices, pack_adapter,
+                     pack_indices, split_decoded, unpack_indices)
 from .shared import packed_codebook_lora_delta_, shared_codebook_lora_delta, shared_codebook_lora_delta_
 
 __all__ = [
     "IndexLoRALinear", "PackedLoRALinear", "PerSampleLoRALinear", "wrap_linears", "wrap_packed",
-    "PackedBank", "PackedLayout", "decode_packed", "flat_indices", "pack_adapter", "pack_indices",
+    "PackedBank", "PackedLayout", "SlotLoader", "decode_packed", "flat_indices", "pack_adapter", "pack_indices",
     "split_decoded", "unpack_indices",
     "shared_codebook_lora_delta", "shared_codebook_lora_delta_", "packed_codebook_lora_delta_",
     "device_errors", "raise_device_errors",

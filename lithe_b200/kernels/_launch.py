@@ -178,3 +178,27 @@ def decode_packed_batch_(bank: torch.Tensor, slot_ids: torch.Tensor, n_blocks: i
             stream_handle(bank.device))
     _lib.check(rc, "lithe_decode_packed_batch")
     return out
+
+
+def pack_raw_(raw: torch.Tensor, segments: torch.Tensor, levels: int, words: torch.Tensor,
+              err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """lithe_pack_raw: raw (n,) uint16/int16 payload on the device -> packed ``words`` in place.
+
+    ``segments`` is the (n_segments, 3) int64 device table of (raw_offset, first_block, n_blocks).
+    """
+    _require_cuda(raw, "raw")
+    if raw.dtype not in (torch.int16, torch.uint16) or raw.dim() != 1 or not raw.is_contiguous():
+        raise ValueError("raw must be a contiguous 1-D 16-bit tensor")
+    if segments.dtype != torch.int64 or segments.dim() != 2 or segments.shape[1] != 3 \
+            or not segments.is_contiguous() or segments.device != raw.device:
+        raise ValueError("segments must be a contiguous (n, 3) int64 tensor on raw's device")
+    if words.dtype not in (torch.int64, torch.uint64) or not words.is_contiguous() or words.device != raw.device:
+        raise ValueError("words must be a contiguous 64-bit tensor on raw's device")
+    if err is None:
+        err = error_word(raw.device)
+    with torch.cuda.device(raw.device):
+        rc = _lib.lib().lithe_pack_raw(raw.data_ptr(), raw.numel(), segments.data_ptr(), segments.shape[0],
+                                       int(levels), words.data_ptr(), words.numel(), err.data_ptr(),
+                                       stream_handle(raw.device))
+    _lib.check(rc, "lithe_pack_raw")
+    return words

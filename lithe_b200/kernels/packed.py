@@ -106,9 +106,34 @@ class PackedLayout:
         return cls.from_modules(ad.modules, ad.num_levels, ad.block_size, float(ad.alpha) / ad.rank)
 
     def matches(self, ad) -> bool:
-        return (len(ad.modules) == len(self.names)
+        return self.matches_modules(ad.modules)
+
+    def matches_modules(self, modules: Sequence[dict]) -> bool:
+        return (len(modules) == len(self.names)
                 and all(m["name"] == n and tuple(m["shape_a"]) == a and tuple(m["shape_b"]) == b
-                        for m, n, a, b in zip(ad.modules, self.names, self.shapes_a, self.shapes_b)))
+                        for m, n, a, b in zip(modules, self.names, self.shapes_a, self.shapes_b)))
+
+    def raw_segments(self) -> np.ndarray:
+        """(2 * n_modules, 3) int64 (raw_offset, first_block, n_blocks) in packed order: where each
+        module side's blocks sit in a raw .lithe payload (all A matrices, then all B matrices,
+        each (L, n) row-major) -- the table ``lithe_pack_raw`` reads."""
+        L = self.num_levels
+        n_a = [b - a for a, b in zip(self.a_off, self.b_off)]
+        n_b = [(self.a_off[i + 1] if i + 1 < len(self.a_off) else self.total_blocks) - self.b_off[i]
+               for i in range(len(self.names))]
+        a_raw = np.concatenate([[0], np.cumsum(n_a)[:-1]]) * L if self.names else np.zeros(0, np.int64)
+        b_raw = (sum(n_a) + np.concatenate([[0], np.cumsum(n_b)[:-1]])) * L if self.names else np.zeros(0, np.int64)
+        rows = []
+        for i in range(len(self.names)):
+            rows.append((int(a_raw[i]), self.a_off[i], n_a[i]))
+            rows.append((int(b_raw[i]), self.b_off[i], n_b[i]))
+        return np.asarray(rows, dtype=np.int64).reshape(-1, 3)
+
+    def segments_on(self, device) -> torch.Tensor:
+        key = "seg:" + str(device)
+        if key not in self._sides_dev:
+            self._sides_dev[key] = torch.from_numpy(self.raw_segments()).to(device).contiguous()
+        return self._sides_dev[key]
 
 
 def flat_indices(ad, layout: PackedLayout) -> np.ndarray:
@@ -191,7 +216,7 @@ class PackedBank:
     aligned.  ``views(name)`` gives the C-ABI index views of one module for the fused kernel.
     """
 
-    def __init__(self, layout: PackedLayout, n_slots: int, device, pools=None):
+    def __init__(self, layout: PackedLayout, n_slots: int, device, pools=None, sigmas=None):
         self.layout = layout
         self.device = torch.device(device)
         self.slot_stride = layout.num_words + (layout.num_words & 1)
@@ -199,6 +224,8 @@ class PackedBank:
         pa, pb = pools if pools is not None else cb.twin_pools()
         self.pool_a, self.pool_b = pa, pb
         self.lut = _lut(pa, pb, layout.num_levels)
+        # (sigma_a, sigma_b) the pools were built from; None when custom pools were given
+        self.sigmas = (list(cb.SIGMA_A), list(cb.SIGMA_B)) if pools is None else sigmas
 
     @property
     def n_slots(self) -> int:
@@ -212,7 +239,8 @@ class PackedBank:
     def from_adapters(cls, ads: Sequence, device, n_slots: Optional[int] = None) -> "PackedBank":
         words0, layout = pack_adapter(ads[0])
         bank = cls(layout, n_slots or len(ads), device,
-                   pools=cb.twin_pools(ads[0].block_size, ads[0].n_bits, ads[0].sigma_a, ads[0].sigma_b))
+                   pools=cb.twin_pools(ads[0].block_size, ads[0].n_bits, ads[0].sigma_a, ads[0].sigma_b),
+                   sigmas=(list(ads[0].sigma_a), list(ads[0].sigma_b)))
         bank.set_slot(0, words0)
         for i, ad in enumerate(ads[1:], start=1):
             bank.set_slot(i, pack_adapter(ad, layout)[0])
@@ -226,6 +254,30 @@ class PackedBank:
 
     def load_adapter(self, slot: int, ad) -> None:
         self.set_slot(slot, pack_adapter(ad, self.layout)[0])
+
+    def check_header(self, header: dict, what: str = "adapter") -> None:
+        """Raise ValueError unless a .lithe header describes this bank's layout and codebook."""
+        cbh = header["codebook"]
+        lay = self.layout
+        if int(cbh["n_bits"]) != INDEX_BITS or int(cbh["num_levels"]) != lay.num_levels \
+                or int(cbh["block_size"]) != lay.block_size:
+            raise ValueError(f"{what}: codebook ({cbh['n_bits']} bits, {cbh['num_levels']} levels, block "
+                             f"{cbh['block_size']}) does not match the bank")
+        if self.sigmas is not None and (list(cbh["sigma_a"]) != list(self.sigmas[0])
+                                        or list(cbh["sigma_b"]) != list(self.sigmas[1])):
+            raise ValueError(f"{what}: codebook scales differ from the bank's pools")
+        if not lay.matches_modules(header["modules"]):
+            raise ValueError(f"{what}: modules do not match the bank's layout")
+
+    def load_raw(self, slot: int, raw: torch.Tensor, err: Optional[torch.Tensor] = None) -> None:
+        """Pack a raw .lithe payload already on the device ((n,) int16, stream order of the
+        file) into ``slot`` with one kernel launch on the current stream."""
+        if not 0 <= slot < self.n_slots:
+            raise IndexError(f"slot {slot} outside [0, {self.n_slots})")
+        if raw.numel() != self.layout.num_indices:
+            raise ValueError(f"payload has {raw.numel()} indices, the layout needs {self.layout.num_indices}")
+        _launch.pack_raw_(raw, self.layout.segments_on(self.device), self.layout.num_levels,
+                          self.words[slot, : self.layout.num_words], err)
 
     def fill_random(self, seed: int, slots: Optional[slice] = None) -> None:
         """Seeded uniform 9-bit indices in every slot: int64 random_() draws uniform words in
@@ -269,3 +321,91 @@ class PackedBank:
 
     def decode_slot(self, slot: int) -> Dict[str, Tuple[torch.Tensor, torch.Tensor]]:
         return split_decoded(self.decode([slot])[0], self.layout)
+
+
+class SlotLoader:
+    """Makes .lithe files resident in a ``PackedBank``: the reference's load_lithe + pack_adapter
+    + H2D (``lithe/fileio.py:119-152``, ``lithe/kernels/packed.py:125-143``) as a pipeline.
+
+    * host: LZMA decompression and the checksum run in a thread pool (``lzma`` and ``hashlib``
+      release the GIL), ``threads`` files at a time;
+    * copy: each raw payload goes through one of ``depth`` pinned host buffers to a device
+      staging buffer on the loader's own stream (no pageable copies, no per-file allocation);
+    * device: ``lithe_pack_raw`` reorders and packs it into the slot on that stream.
+
+    Ordering against serving: the loader's stream first waits for the caller's current stream
+    (kernels already queued that read a slot finish before it is overwritten), and the
+    caller's current stream waits for the loader's stream before ``load``/``load_many`` return,
+    so work queued afterwards sees the new slots.  Routing samples to a new slot is then just a
+    change of the ``assign`` ids: the index-resident path has no decode-on-swap.
+    """
+
+    def __init__(self, bank: PackedBank, threads: int = 4, depth: int = 2):
+        if bank.device.type != "cuda":
+            raise ValueError("SlotLoader needs a bank on a CUDA device")
+        self.bank = bank
+        self.threads = max(1, int(threads))
+        n = bank.layout.num_indices
+        self.pinned = [torch.empty(n, dtype=torch.int16, pin_memory=True) for _ in range(max(1, depth))]
+        self.staging = [torch.empty(n, dtype=torch.int16, device=bank.device) for _ in self.pinned]
+        self.done = [None] * len(self.pinned)
+        self.stream = torch.cuda.Stream(device=bank.device)
+        self.stats = {"files": 0, "raw_bytes": 0, "host_s": 0.0}
+
+    def _stage(self, i: int, slot: int, header: dict, raw: bytes, what: str) -> None:
+        self.bank.check_header(header, what)
+        k = i % len(self.pinned)
+        if self.done[k] is not None:
+            self.done[k].synchronize()          # the previous copy out of this pinned buffer is done
+        src = np.frombuffer(raw, dtype="<i2")
+        self.pinned[k].numpy()[:] = src                # host copy into the pinned buffer
+        with torch.cuda.stream(self.stream):
+            self.staging[k].copy_(self.pinned[k], non_blocking=True)
+            self.bank.load_raw(slot, self.staging[k])
+            ev = torch.cuda.Event()
+            ev.record(self.stream)
+        self.done[k] = ev
+        self.stats["files"] += 1
+        self.stats["raw_bytes"] += len(raw)
+
+    def load_many(self, slots: Sequence[int], paths: Sequence, verify: bool = True) -> None:
+        """Load ``paths[i]`` into ``slots[i]`` for every i (slots must be distinct)."""
+        import time
+        from concurrent.futures import ThreadPoolExecutor
+
+        from ..fileio import read_payload
+        if len(slots) != len(paths):
+            raise ValueError("slots and paths differ in length")
+        if len(set(int(s) for s in slots)) != len(slots):
+            raise ValueError("slots must be distinct")
+        for s in slots:
+            if not 0 <= int(s) < self.bank.n_slots:
+                raise IndexError(f"slot {s} outside [0, {self.bank.n_slots})")
+        self.stream.wait_stream(torch.cuda.current_stream(self.bank.device))
+
+        def work(path):
+            t0 = time.perf_counter()
+            header, raw = read_payload(path, verify)
+            return header, raw, time.perf_counter() - t0
+
+        try:
+            with ThreadPoolExecutor(max_workers=self.threads) as pool:
+                for i, (slot, path, fut) in enumerate(zip(slots, paths, [pool.submit(work, p) for p in paths])):
+                    header, raw, dt = fut.result()
+                    self.stats["host_s"] += dt
+                    self._stage(i, int(slot), header, raw, str(path))
+        finally:
+            torch.cuda.current_stream(self.bank.device).wait_stream(self.stream)
+
+    def load(self, slot: int, path, verify: bool = True) -> None:
+        self.load_many([slot], [path], verify)
+
+    def load_payload(self, slot: int, header: dict, raw: bytes) -> None:
+        """Stage an already decompressed payload (``fileio.read_payload``) into ``slot``."""
+        if not 0 <= int(slot) < self.bank.n_slots:
+            raise IndexError(f"slot {slot} outside [0, {self.bank.n_slots})")
+        self.stream.wait_stream(torch.cuda.current_stream(self.bank.device))
+        try:
+            self._stage(self.stats["files"], int(slot), header, raw, "payload")
+        finally:
+            torch.cuda.current_stream(self.bank.device).wait_stream(self.stream)

@@ -7,6 +7,7 @@ Restates, from the reference implementation:
   layout (A blocks then B blocks per module)   lithe/kernels/packed.py:100-117
   stream order ((block, level)-major)          lithe/kernels/packed.py:125-133
   whole-adapter decode, bf16 output            lithe/kernels/packed.py:241-257
+  raw .lithe payload split (A all, B all)      lithe/fileio.py:5-13,139-149
 Everything here is exact integer or fp32 arithmetic; float32 sums are formed in the
 reference's order, so results are comparable bit for bit.
 """
@@ -155,3 +156,32 @@ def split(decoded: np.ndarray, lay: Layout) -> Dict[str, Tuple[np.ndarray, np.nd
         na, nb = sa[0] * sa[1], sb[0] * sb[1]
         res[name] = (flat[ao * BLOCK: ao * BLOCK + na].reshape(sa), flat[bo * BLOCK: bo * BLOCK + nb].reshape(sb))
     return res
+
+
+def split_raw(raw, modules: Sequence[dict], levels: int = 3, block: int = BLOCK) -> Dict[str, Dict[str, np.ndarray]]:
+    """A .lithe payload (uint16: every module's (L, nA) A matrix, then every (L, nB) B matrix,
+    row-major) -> name -> {"A", "B"} index matrices, as load_lithe splits it."""
+    v = np.frombuffer(raw, dtype="<u2") if isinstance(raw, (bytes, bytearray)) else np.asarray(raw).reshape(-1)
+    out: Dict[str, Dict[str, np.ndarray]] = {}
+    pos = 0
+    for side, key in ((0, "A"), (1, "B")):
+        for m in modules:
+            n = levels * num_blocks(m["shape_a" if side == 0 else "shape_b"], block)
+            out.setdefault(m["name"], {})[key] = v[pos:pos + n].reshape(levels, -1)
+            pos += n
+    if pos != v.size:
+        raise ValueError("payload length does not match the modules")
+    return out
+
+
+def raw_payload(indices: Dict[str, Dict[str, np.ndarray]], modules: Sequence[dict]) -> np.ndarray:
+    """Inverse of split_raw: the uint16 payload save_lithe compresses (LitheAdapter.raw_stream)."""
+    parts = [np.asarray(indices[m["name"]]["A"]).reshape(-1) for m in modules]
+    parts += [np.asarray(indices[m["name"]]["B"]).reshape(-1) for m in modules]
+    return np.concatenate(parts).astype("<u2")
+
+
+def pack_raw(raw, modules: Sequence[dict], levels: int = 3, block: int = BLOCK) -> np.ndarray:
+    """Packed slot words of a raw payload: load_lithe's split, flat_indices' (block, level)
+    order, pack_indices' 7 x 9-bit words."""
+    return pack9(stream(split_raw(raw, modules, levels, block), layout(modules, levels, block)))
