@@ -187,6 +187,38 @@ LITHE_API int32_t lithe_decode_packed_batch(const uint64_t* bank, int64_t slot_s
                                   int32_t num_levels, const int8_t* sides, const float* lut,
                                   void* out, int32_t out_dtype, int32_t* err_flag, void* stream);
 
+/*
+ * Operands of lithe_lora_gemm's fused expand, for one linear (rank 16; same arguments and
+ * routing as lithe_sgmv_index):
+ *   h      device bf16 (batch * m, 16): h[b*m + i] = bf16( w_b * scaling * x[b, i] @ A_j^T ),
+ *          the same values lithe_sgmv_index feeds its expand; zero rows for unrouted samples
+ *   b_dec  device bf16 (batch, d_out, 16): B_j of every sample, decoded and rounded to bf16
+ *          (zero for unrouted samples)
+ * Two launches on `stream`: the B decode and the fused kernel in shrink-only form (x is read
+ * once, no output tiles).
+ */
+LITHE_API int32_t lithe_lora_prep(const void* x, const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                        int64_t n_slots, const int32_t* ids, const float* weights, int32_t batch, int32_t m,
+                        int32_t d_in, int32_t d_out, int32_t rank, const float* lut, float scaling, void* h,
+                        void* b_dec, int32_t* err_flag, void* stream);
+
+/*
+ * Base linear with the per-sample LoRA expand inside the GEMM (tcgen05, TMEM accumulators, TMA):
+ *   out[r, :] = x[r, :] . w^T + bias + h[r, :] . b_dec[r / rows_per_sample]^T
+ * Replaces nn.Linear's GEMM + the delta's read-modify-write pass of the output
+ * (lithe/kernels/layers.py:131, lithe/serve.py:96-97) for layers whose shapes it supports.
+ *   x        device bf16 (rows, k), k-contiguous        w     device bf16 (n, k) (nn.Linear weight)
+ *   bias     device bf16 (n) or NULL                      out   device bf16 (rows, n), written
+ *   h        device bf16 (rows, rank): the scaled, bf16-rounded shrink (lithe_lora_prep), or NULL
+ *            for the plain GEMM
+ *   b_dec    device bf16 (rows / rows_per_sample, n, rank): every sample's decoded B factor
+ * n must be a multiple of 256, k of 64; with h, rank 16 and rows_per_sample a multiple of 128
+ * dividing rows (otherwise LITHE_ERR_UNSUPPORTED: use cuBLAS + lithe_sgmv_index).
+ */
+LITHE_API int32_t lithe_lora_gemm(const void* x, const void* w, const void* bias, void* out, int32_t rows, int32_t n,
+                        int32_t k, const void* h, const void* b_dec, int32_t rows_per_sample, int32_t rank,
+                        int32_t* err_flag, void* stream);
+
 /* One (module, side) of a .lithe payload: its packed blocks [first_block, first_block + n_blocks)
  * come from raw[raw_offset + level * n_blocks + j], j = block - first_block. */
 typedef struct {

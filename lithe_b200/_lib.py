@@ -72,6 +72,13 @@ _SIGNATURES.update({
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64,
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32,
         _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p, _c.c_void_p]),
+    "lithe_lora_prep": (_c.c_int32, [
+        _c.c_void_p, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int32,
+        _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p,
+        _c.c_void_p, _c.c_void_p, _c.c_void_p]),
+    "lithe_lora_gemm": (_c.c_int32, [
+        _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_void_p,
+        _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_void_p]),
     "lithe_pack_raw": (_c.c_int32, [
         _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_int64, _c.c_void_p,
         _c.c_void_p]),

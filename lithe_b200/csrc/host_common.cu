@@ -96,6 +96,28 @@ int32_t encode_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t
     return LITHE_OK;
 }
 
+int32_t encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                       uint32_t box_rows, int swizzle_bytes) {
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int32_t rc = get_encoder(&enc);
+    if (rc != LITHE_OK) return rc;
+    CUtensorMapSwizzle sw = CU_TENSOR_MAP_SWIZZLE_NONE;
+    if (swizzle_bytes == 128) sw = CU_TENSOR_MAP_SWIZZLE_128B;
+    else if (swizzle_bytes == 64) sw = CU_TENSOR_MAP_SWIZZLE_64B;
+    else if (swizzle_bytes == 32) sw = CU_TENSOR_MAP_SWIZZLE_32B;
+    const cuuint64_t dims[2] = {inner, rows};
+    const cuuint64_t strides[1] = {inner * 2};
+    const cuuint32_t box[2] = {box_inner, box_rows};
+    const cuuint32_t estr[2] = {1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, sw, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail_arg("cuTensorMapEncodeTiled failed (CUresult %d) for dims (%llu,%llu) box (%u,%u)",
+                        static_cast<int>(r), (unsigned long long)inner, (unsigned long long)rows, box_inner, box_rows);
+    return LITHE_OK;
+}
+
 void expand_lut(const float* lut, int levels, float out[2][LITHE_MAX_LEVELS][16]) {
     for (int s = 0; s < 2; ++s)
         for (int l = 0; l < LITHE_MAX_LEVELS; ++l)

@@ -27,6 +27,9 @@ int32_t current_device_sms(int* device, int* sms);
 // (b0, b1, 1) and 128-byte swizzle.  Returns LITHE_OK or an error code.
 int32_t encode_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                        uint32_t b0, uint32_t b1);
+// 2-D bf16 tensor map (rows of `inner` elements), box (box_inner, box_rows), swizzle 0/32/64/128 B.
+int32_t encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner,
+                       uint32_t box_rows, int swizzle_bytes);
 
 // Fill the kernel-side lookup table lut_dev[side][level][16] from the host-side
 // [2][levels][10] array of the C ABI.

@@ -70,6 +70,7 @@ struct SgmvParams {
     __nv_bfloat16* out;
     const uint8_t* ws;          // staged mode: decoded factor chunks, (batch, n_chunks, 512 B)
     int32_t n_chunks;           // n_xchunks + n_ochunks (per-sample stride of ws, in chunks)
+    __nv_bfloat16* h_out;       // shrink-only mode (lithe_lora_prep): h rows (batch * m, 16), else null
     float lut[2][LITHE_MAX_LEVELS][16];
 };
 
@@ -306,7 +307,20 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
     uint32_t pos = 0;
     for (int u = u_begin; u < u_end; ++u) {
         const Unit un = unit_at(p, u);
-        if (un.nx + un.no == 0) continue;
+        if (un.nx + un.no == 0) {
+            if (p.h_out && grp == 0) {              // unrouted sample: its h rows are zero
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int row = un.mt * kBM + r0 + 8 * hr;
+                    if (row < p.m) {
+                        uint32_t* hrow = reinterpret_cast<uint32_t*>(p.h_out + (static_cast<int64_t>(un.b) * p.m + row) * 16);
+                        hrow[t4] = 0u;
+                        hrow[4 + t4] = 0u;
+                    }
+                }
+            }
+            continue;
+        }
         // four independent accumulation chains: [rank half][32-column window]
         float acc[2][2][4];
 #pragma unroll
@@ -371,6 +385,21 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
         const uint32_t ha[4] = {pack_bf16x2(h0[0], h0[1]), pack_bf16x2(h0[2], h0[3]), pack_bf16x2(h1[0], h1[1]),
                                 pack_bf16x2(h1[2], h1[3])};
         const int row0 = un.mt * kBM + r0;                   // token rows row0 and row0 + 8
+        if (p.h_out) {
+            // shrink-only: store h (ranks 2 t4, 2 t4 + 1 and 8 + 2 t4, 9 + 2 t4 of rows row0, row0 + 8)
+            if (grp == 0) {
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    const int row = row0 + 8 * hr;
+                    if (row < p.m) {
+                        uint32_t* hrow = reinterpret_cast<uint32_t*>(p.h_out + (static_cast<int64_t>(un.b) * p.m + row) * 16);
+                        hrow[t4] = ha[hr];
+                        hrow[4 + t4] = ha[2 + hr];
+                    }
+                }
+            }
+            continue;
+        }
         __nv_bfloat16* out_b = p.out + static_cast<int64_t>(un.b) * p.m * p.d_out;
         for (int j = 0; j < un.no; ++j, ++pos) {
             if (static_cast<int>(pos % kGroups) != grp) continue;
@@ -551,6 +580,54 @@ __global__ void __launch_bounds__(256) decode_chunks_kernel(const __grid_constan
     }
 }
 
+// lithe_lora_prep, B side: every sample's rank-16 B factor decoded into (batch, d_out, 16)
+// bf16, row o = B[o, :] (the operand of the GEMM's fused expand).  For rank 16 a B block G
+// holds four identical rows 4G .. 4G + 3, so one warp decodes a 64-column chunk (16 logical
+// columns x 2 rank halves, the lanes of decode_chunk) and writes each 8-value half 4 times.
+// The values are the fp32 level sums rounded to bf16, exactly as the expand path uses them.
+__global__ void __launch_bounds__(256) decode_bdec_kernel(const __grid_constant__ SgmvParams p,
+                                                          __nv_bfloat16* bdec, int32_t batch) {
+    __shared__ DecodeTables tab;
+    __shared__ float lut_s[kLutFloats];
+    for (int i = threadIdx.x; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
+    build_decode_tables(&tab, &p.lut[0][0][0], p.ia.levels, threadIdx.x, blockDim.x);
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const uint32_t half = lane & 1;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const int64_t total = static_cast<int64_t>(batch) * p.n_ochunks;
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        const int b = static_cast<int>(w / p.n_ochunks);
+        const int j = static_cast<int>(w - static_cast<int64_t>(b) * p.n_ochunks);
+        const int32_t sid = __ldg(p.ids + b);
+        Unit un;
+        un.b = b;
+        un.mt = 0;
+        un.slot = sid;
+        un.active = sid >= 0 && static_cast<int64_t>(sid) < p.n_slots;
+        un.nx = p.n_xchunks;
+        un.no = p.n_ochunks;
+        RawIndices<LITHE_MAX_LEVELS> raw;
+        const bool live = un.active && chunk_fetch<16>(p, un, un.nx + j, lane, raw);
+        float v[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) v[i] = 0.f;
+        if (live) {
+            uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
+            finish_raw<LITHE_MAX_LEVELS>(p.ib, raw, k, p.err);
+            decode_values(p, &tab, lut_s, 1, k, half, v);
+        }
+        const int G = 16 * j + (lane >> 1);
+        if (4 * G < p.d_out) {
+            const uint4 q = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                                       pack_bf16x2(v[6], v[7]));
+            __nv_bfloat16* dst = bdec + (static_cast<int64_t>(b) * p.d_out + 4 * G) * 16 + 8 * half;
+#pragma unroll
+            for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(dst + i * 16) = q;
+        }
+    }
+}
+
 template <int kRank, bool kStaged>
 static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, const SgmvParams& p, int grid,
                            int device, int sms, int32_t batch, uint8_t* ws, cudaStream_t stream) {
@@ -615,7 +692,8 @@ int64_t sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out) {
 int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lithe_index_view* idx_a,
                         const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids, const float* weights,
                         int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank, const float* lut,
-                        float scaling, int32_t* err_flag, void* ws, int64_t ws_bytes, void* stream) {
+                        float scaling, int32_t* err_flag, void* ws, int64_t ws_bytes, void* stream,
+                        void* h_out = nullptr, void* bdec_out = nullptr) {
     if (batch < 0 || m < 0) return fail_arg("batch (%d) and m (%d) must be >= 0", batch, m);
     if (rank != 1 && rank != 2 && rank != 4 && rank != 8 && rank != 16)
         return fail_unsupported("rank must be one of 1, 2, 4, 8, 16; got %d", rank);
@@ -637,6 +715,14 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     if (!lut) return fail_arg("lut is NULL");
     if (n_slots < 0) return fail_arg("n_slots must be >= 0");
     if (batch == 0 || m == 0) return LITHE_OK;
+    const bool prep = h_out != nullptr;
+    if (prep) {
+        if (rank != 16) return fail_unsupported("lithe_lora_prep supports rank 16, got %d", rank);
+        if (!bdec_out) return fail_arg("b_dec is NULL");
+        if (reinterpret_cast<uintptr_t>(h_out) % 16 || reinterpret_cast<uintptr_t>(bdec_out) % 16)
+            return fail_arg("h and b_dec must be 16-byte aligned");
+        out = h_out;                  // only used for the alignment check and an unused tensor map below
+    }
     if (!x || !out || !ids) return fail_arg("x, out and ids must be non-NULL");
     if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
         return fail_arg("x and out must be 16-byte aligned");
@@ -655,8 +741,12 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     // stored (stores are bounded by the sample's own m), and rows past the tensor read zeros.
     rc = encode_bf16_3d(&tmx, x, d_in, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
     if (rc != LITHE_OK) return rc;
-    rc = encode_bf16_3d(&tmo_ld, out, d_out, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
-    if (rc != LITHE_OK) return rc;
+    if (prep) {
+        tmo_ld = tmx;                 // no out tiles in shrink-only mode
+    } else {
+        rc = encode_bf16_3d(&tmo_ld, out, d_out, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
+        if (rc != LITHE_OK) return rc;
+    }
 
     SgmvParams p{};
     p.ia = to_view(idx_a);
@@ -681,6 +771,24 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
 
     p.n_chunks = p.n_xchunks + p.n_ochunks;
     p.ws = static_cast<const uint8_t*>(ws);
+    p.h_out = nullptr;
+    if (prep) {
+        cudaStream_t s = static_cast<cudaStream_t>(stream);
+        // B side first: every sample's decoded factor, (batch, d_out, 16)
+        const int64_t warps_needed = static_cast<int64_t>(batch) * p.n_ochunks;
+        int64_t blocks = (warps_needed + 7) / 8;
+        if (blocks > 2LL * sms) blocks = 2LL * sms;
+        decode_bdec_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(bdec_out), batch);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return fail_cuda(e, "decode_bdec_kernel launch");
+        // A side: the fused kernel in shrink-only form (x tiles only, h stored after the shrink)
+        p.h_out = static_cast<__nv_bfloat16*>(h_out);
+        p.n_ochunks = 0;
+        p.accumulate = 1;             // unrouted samples skip all work (their h rows are zeroed)
+        p.n_chunks = p.n_xchunks;
+        p.out = nullptr;
+        ws = nullptr;
+    }
     if (ws) {
         if (reinterpret_cast<uintptr_t>(ws) % 16) return fail_arg("workspace must be 16-byte aligned");
         const int64_t need = sgmv_workspace_bytes(batch, d_in, d_out);
@@ -713,6 +821,16 @@ extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate
     lithe::clear_error();
     return lithe::sgmv_index_impl(x, out, accumulate, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
                                   rank, lut, scaling, err_flag, nullptr, 0, stream);
+}
+
+extern "C" int32_t lithe_lora_prep(const void* x, const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                                   int64_t n_slots, const int32_t* ids, const float* weights, int32_t batch, int32_t m,
+                                   int32_t d_in, int32_t d_out, int32_t rank, const float* lut, float scaling, void* h,
+                                   void* b_dec, int32_t* err_flag, void* stream) {
+    lithe::clear_error();
+    if (batch > 0 && m > 0 && (!h || !b_dec)) return lithe::fail_arg("h and b_dec must be non-NULL");
+    return lithe::sgmv_index_impl(x, h, 1, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out, rank, lut,
+                                  scaling, err_flag, nullptr, 0, stream, h, b_dec);
 }
 
 extern "C" int64_t lithe_sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out) {

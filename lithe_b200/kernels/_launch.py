@@ -202,3 +202,63 @@ def pack_raw_(raw: torch.Tensor, segments: torch.Tensor, levels: int, words: tor
                                        stream_handle(raw.device))
     _lib.check(rc, "lithe_pack_raw")
     return words
+
+
+def lora_gemm_(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], out: torch.Tensor,
+               h: Optional[torch.Tensor] = None, b_dec: Optional[torch.Tensor] = None, rows_per_sample: int = 0,
+               err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """lithe_lora_gemm: out (rows, n) = x (rows, k) . weight^T + bias [+ h . b_dec[sample]^T], bf16."""
+    _require_cuda(x, "x")
+    for t, name in ((x, "x"), (weight, "weight"), (out, "out")):
+        if t.dtype != torch.bfloat16 or not t.is_contiguous() or t.device != x.device:
+            raise ValueError(f"{name} must be a contiguous bfloat16 tensor on x's device")
+    if x.dim() != 2 or weight.dim() != 2 or out.dim() != 2:
+        raise ValueError("x (rows, k), weight (n, k) and out (rows, n) must be 2-D")
+    rows, k = x.shape
+    n = weight.shape[0]
+    if weight.shape[1] != k or tuple(out.shape) != (rows, n):
+        raise ValueError(f"shapes disagree: x {tuple(x.shape)}, weight {tuple(weight.shape)}, out {tuple(out.shape)}")
+    if bias is not None and (bias.dtype != torch.bfloat16 or bias.numel() != n or not bias.is_contiguous()):
+        raise ValueError("bias must be a contiguous (n,) bfloat16 tensor")
+    rank = 0
+    if h is not None:
+        if b_dec is None or h.dtype != torch.bfloat16 or b_dec.dtype != torch.bfloat16 \
+                or not h.is_contiguous() or not b_dec.is_contiguous():
+            raise ValueError("h and b_dec must be contiguous bfloat16 tensors")
+        rank = h.shape[-1]
+        if h.numel() != rows * rank or b_dec.shape[-2:] != (n, rank):
+            raise ValueError("h must be (rows, rank) and b_dec (samples, n, rank)")
+    if err is None:
+        err = error_word(x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.lib().lithe_lora_gemm(
+            x.data_ptr(), weight.data_ptr(), bias.data_ptr() if bias is not None else None, out.data_ptr(), rows, n,
+            k, h.data_ptr() if h is not None else None, b_dec.data_ptr() if b_dec is not None else None,
+            int(rows_per_sample), int(rank), err.data_ptr(), stream_handle(x.device))
+    _lib.check(rc, "lithe_lora_gemm")
+    return out
+
+
+def lora_prep_(x: torch.Tensor, *, view_a: _lib.IndexView, view_b: _lib.IndexView, n_slots: int, ids: torch.Tensor,
+               weights: Optional[torch.Tensor], d_out: int, lut: np.ndarray, scaling: float, h: torch.Tensor,
+               b_dec: torch.Tensor, err: Optional[torch.Tensor] = None) -> None:
+    """lithe_lora_prep: h (B*M, 16) and b_dec (B, d_out, 16), bf16, for lithe_lora_gemm's fused expand."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.dim() != 3 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous (B, M, d_in) bfloat16 tensor")
+    bsz, m, d_in = x.shape
+    if h.dtype != torch.bfloat16 or h.numel() != bsz * m * 16 or not h.is_contiguous() or h.device != x.device:
+        raise ValueError("h must be a contiguous (B*M, 16) bfloat16 tensor on x's device")
+    if b_dec.dtype != torch.bfloat16 or b_dec.numel() != bsz * d_out * 16 or not b_dec.is_contiguous() \
+            or b_dec.device != x.device:
+        raise ValueError("b_dec must be a contiguous (B, d_out, 16) bfloat16 tensor on x's device")
+    if ids.dtype != torch.int32 or ids.numel() != bsz or ids.device != x.device or not ids.is_contiguous():
+        raise ValueError("ids must be a contiguous (B,) int32 tensor on x's device")
+    if err is None:
+        err = error_word(x.device)
+    with torch.cuda.device(x.device):
+        rc = _lib.lib().lithe_lora_prep(
+            x.data_ptr(), ctypes.byref(view_a), ctypes.byref(view_b), int(n_slots), ids.data_ptr(),
+            weights.data_ptr() if weights is not None else None, bsz, m, d_in, int(d_out), 16, lut_array(lut),
+            float(scaling), h.data_ptr(), b_dec.data_ptr(), err.data_ptr(), stream_handle(x.device))
+    _lib.check(rc, "lithe_lora_prep")

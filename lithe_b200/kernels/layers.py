@@ -81,7 +81,7 @@ class PackedLoRALinear(nn.Module):
     """
 
     def __init__(self, base: nn.Linear, bank: PackedBank, name: str, rank: int, scaling: float,
-                 rows: Optional[Tuple[int, int]] = None):
+                 rows: Optional[Tuple[int, int]] = None, fused_gemm: bool = False):
         super().__init__()
         self.base = base
         for p in self.base.parameters():
@@ -101,8 +101,26 @@ class PackedLoRALinear(nn.Module):
         self.scaling = float(scaling)
         self.assign: Optional[torch.Tensor] = None
         self.weights: Optional[torch.Tensor] = None
+        # fused_gemm: compute the base linear with lithe_lora_gemm and apply the expand inside it
+        # (after lithe_lora_prep) where the shapes allow it -- rank 16, out_features % 256 == 0,
+        # in_features % 64 == 0, tokens per sample % 128 == 0 -- instead of cuBLAS followed by
+        # the fused decode/SGMV kernel's read-modify-write of the output.  The base product is
+        # then ours, not cuBLAS's (same math, different fp32 summation order).
+        self.fused_gemm = bool(fused_gemm)
+
+    def _gemm_ok(self, x3: torch.Tensor) -> bool:
+        w = self.base.weight
+        b = self.base.bias
+        return (self.rank == 16 and w.dtype == torch.bfloat16 and w.is_contiguous() and x3.dtype == torch.bfloat16
+                and (b is None or (b.dtype == torch.bfloat16 and b.is_contiguous()))
+                and w.shape[0] % 256 == 0 and w.shape[1] % 64 == 0 and x3.shape[1] % 128 == 0 and x3.shape[0] > 0)
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        x3 = x.unsqueeze(1) if x.dim() == 2 else x
+        if self.fused_gemm and x3.dim() == 3 and self._gemm_ok(x3):
+            if torch.is_grad_enabled() and (x.requires_grad or self.base.weight.requires_grad):
+                raise RuntimeError("lithe_b200 layers are inference-only (run under torch.no_grad())")
+            return self._forward_fused_gemm(x, x3.contiguous())
         out = self.base(x)
         _inference_only(out)
         x3, out3 = _as3d(x, out)
@@ -112,6 +130,24 @@ class PackedLoRALinear(nn.Module):
         packed_codebook_lora_delta_(out3, x3, self.bank, self.name, assign, scaling=self.scaling,
                                     weights=self.weights, rows=self.rows)
         return out
+
+    def _forward_fused_gemm(self, x: torch.Tensor, x3: torch.Tensor) -> torch.Tensor:
+        bsz, m, d_in = x3.shape
+        d_out = self.base.out_features
+        assign = self.assign
+        if assign is None:
+            assign = torch.zeros(bsz, dtype=torch.int32, device=x.device)
+        ids = assign.to(device=x.device, dtype=torch.int32).contiguous()
+        w = None if self.weights is None else self.weights.to(device=x.device, dtype=torch.float32).contiguous()
+        va, vb = self.bank.views(self.name, self.rows)
+        h = torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device)
+        b_dec = torch.empty(bsz, d_out, 16, dtype=torch.bfloat16, device=x.device)
+        _launch.lora_prep_(x3, view_a=va, view_b=vb, n_slots=self.bank.n_slots, ids=ids, weights=w, d_out=d_out,
+                           lut=self.bank.lut, scaling=self.scaling, h=h, b_dec=b_dec)
+        out = torch.empty(bsz * m, d_out, dtype=torch.bfloat16, device=x.device)
+        _launch.lora_gemm_(x3.view(bsz * m, d_in), self.base.weight, self.base.bias, out, h=h, b_dec=b_dec,
+                           rows_per_sample=m)
+        return out.view(*x.shape[:-1], d_out)
 
 
 class PerSampleLoRALinear(nn.Module):
@@ -195,13 +231,15 @@ def wrap_linears(model: nn.Module, paths: Iterable[str],
 
 
 def wrap_packed(model: nn.Module, bank: PackedBank, key_format: str = "diffusers",
-                paths: Optional[Iterable[str]] = None, scaling: Optional[float] = None) -> Dict[str, PackedLoRALinear]:
+                paths: Optional[Iterable[str]] = None, scaling: Optional[float] = None,
+                fused_gemm: bool = False) -> Dict[str, PackedLoRALinear]:
     """Serve every linear the bank's layout covers from the resident packed bank.
 
     For a Kohya-format layout (304 fused modules) each diffusers linear (494) reads its own B
     rows of the fused module in place (``lithe_b200.kohya.split_targets``).  ``paths`` limits
     the wrapped set (e.g. the 342 attention / feed-forward linears); ``scaling`` defaults to
-    the layout's alpha / rank.  Set ``.assign`` on the returned modules to route samples.
+    the layout's alpha / rank; ``fused_gemm`` selects the expand-in-GEMM path where eligible.
+    Set ``.assign`` on the returned modules to route samples.
     """
     from .. import kohya
     lay = bank.layout
@@ -216,7 +254,7 @@ def wrap_packed(model: nn.Module, bank: PackedBank, key_format: str = "diffusers
         name, r0, r1 = targets[path]
         rank = lay.shapes_a[lay.index(name)][0]
         full = r0 == 0 and r1 == lay.shapes_b[lay.index(name)][0]
-        return PackedLoRALinear(lin, bank, name, rank, s, rows=None if full else (r0, r1))
+        return PackedLoRALinear(lin, bank, name, rank, s, rows=None if full else (r0, r1), fused_gemm=fused_gemm)
 
     return wrap_linears(model, want, factory)
 

@@ -1,0 +1,186 @@
+"""lithe_lora_gemm (tcgen05 GEMM with the LoRA expand fused into the accumulator) against a
+torch fp32 reference of the same op: out = x W^T + bias + h Bdec_sample^T, rounded to bf16.
+Tolerance (bf16 inputs, fp32 accumulation in a different order, one bf16 rounding of the
+output): max |got - ref| <= 1e-2 * max |ref| and relative Frobenius error < 5e-3."""
+import pytest
+import torch
+
+from lithe_b200 import device_errors
+from lithe_b200.kernels import _launch
+from tests.helpers import rel_fro
+
+pytestmark = pytest.mark.gpu
+
+
+def reference(x, w, bias, h=None, bd=None, rps=None):
+    ref = x.float() @ w.float().T
+    if bias is not None:
+        ref += bias.float()
+    if h is not None:
+        samples = x.shape[0] // rps
+        hs = h.float().view(samples, rps, -1)
+        ref += torch.bmm(hs, bd.float().transpose(1, 2)).reshape(x.shape[0], -1)
+    return ref
+
+
+def check(got, ref):
+    err = (got.float() - ref).abs().max().item()
+    assert err <= 1e-2 * ref.abs().max().item(), err
+    assert rel_fro(got.float().cpu(), ref.cpu()) < 5e-3
+
+
+@pytest.mark.parametrize("rows,n,k,bias", [(128, 256, 64, True), (300, 512, 192, False), (1000, 768, 1024, True),
+                                           (4096, 3072, 3072, True), (2048, 12288, 3072, True),
+                                           (2048, 3072, 12288, False)])
+def test_plain_gemm(rows, n, k, bias):
+    g = torch.Generator(device="cuda").manual_seed(rows + n + k)
+    x = torch.randn(rows, k, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    b = torch.randn(n, generator=g, device="cuda").bfloat16() if bias else None
+    out = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+    _launch.lora_gemm_(x, w, b, out)
+    torch.cuda.synchronize()
+    check(out, reference(x, w, b))
+    assert device_errors() == 0
+
+
+@pytest.mark.parametrize("samples,rps,n,k", [(1, 128, 256, 64), (3, 256, 512, 320), (14, 512, 3072, 3072),
+                                             (4, 1024, 12288, 3072)])
+def test_fused_expand(samples, rps, n, k):
+    g = torch.Generator(device="cuda").manual_seed(samples * rps + n)
+    rows = samples * rps
+    x = torch.randn(rows, k, generator=g, device="cuda").bfloat16()
+    w = (torch.randn(n, k, generator=g, device="cuda") * 0.02).bfloat16()
+    b = torch.randn(n, generator=g, device="cuda").bfloat16()
+    h = torch.randn(rows, 16, generator=g, device="cuda").bfloat16()
+    bd = (torch.randn(samples, n, 16, generator=g, device="cuda") * 0.1).bfloat16()
+    out = torch.empty(rows, n, dtype=torch.bfloat16, device="cuda")
+    _launch.lora_gemm_(x, w, b, out, h=h, b_dec=bd, rows_per_sample=rps)
+    torch.cuda.synchronize()
+    ref = reference(x, w, b, h, bd, rps)
+    check(out, ref)
+    # the expand really is per sample: zero one sample's factor and only its rows change
+    bd2 = bd.clone()
+    bd2[samples - 1] = 0
+    out2 = torch.empty_like(out)
+    _launch.lora_gemm_(x, w, b, out2, h=h, b_dec=bd2, rows_per_sample=rps)
+    torch.cuda.synchronize()
+    assert torch.equal(out2[: (samples - 1) * rps], out[: (samples - 1) * rps])
+    check(out2, reference(x, w, b, h, bd2, rps))
+    assert device_errors() == 0
+
+
+def test_unsupported_shapes_are_rejected():
+    x = torch.zeros(128, 64, dtype=torch.bfloat16, device="cuda")
+    w = torch.zeros(200, 64, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(NotImplementedError):
+        _launch.lora_gemm_(x, w, None, torch.empty(128, 200, dtype=torch.bfloat16, device="cuda"))
+    w = torch.zeros(256, 64, dtype=torch.bfloat16, device="cuda")
+    h = torch.zeros(128, 16, dtype=torch.bfloat16, device="cuda")
+    bd = torch.zeros(2, 256, 16, dtype=torch.bfloat16, device="cuda")
+    with pytest.raises(NotImplementedError):        # 64 rows per sample: not a multiple of 128
+        _launch.lora_gemm_(x, w, None, torch.empty(128, 256, dtype=torch.bfloat16, device="cuda"), h=h, b_dec=bd,
+                           rows_per_sample=64)
+
+
+# ------------------------------------------------------------------ prep + the fused layer path
+from lithe_b200 import kohya  # noqa: E402
+from lithe_b200.kernels import PackedBank, PackedLoRALinear  # noqa: E402
+from tests.helpers import max_abs_rel, oracle_factors, random_adapter  # noqa: E402
+
+
+def _prep(bank, name, x, ids, weights, scaling, rows=None):
+    va, vb = bank.views(name, rows)
+    i = bank.layout.index(name)
+    d_out = bank.layout.shapes_b[i][0] if rows is None else rows[1] - rows[0]
+    h = torch.full((x.shape[0] * x.shape[1], 16), 7.0, dtype=torch.bfloat16, device="cuda")
+    bd = torch.full((x.shape[0], d_out, 16), 7.0, dtype=torch.bfloat16, device="cuda")
+    _launch.lora_prep_(x, view_a=va, view_b=vb, n_slots=bank.n_slots, ids=ids, weights=weights, d_out=d_out,
+                       lut=bank.lut, scaling=scaling, h=h, b_dec=bd)
+    torch.cuda.synchronize()
+    return h, bd
+
+
+def test_prep_matches_oracle():
+    d_in, d_out = 512, 768
+    ads = [random_adapter([("l", d_in, d_out)], rank=16, seed=s) for s in range(3)]
+    bank = PackedBank.from_adapters(ads, "cuda")
+    g = torch.Generator().manual_seed(5)
+    x = torch.randn(4, 200, d_in, generator=g).bfloat16().cuda()
+    assign, wts, sc = [2, -1, 0, 1], [1.0, 1.0, 0.5, 2.0], 0.75
+    ids = torch.tensor(assign, dtype=torch.int32, device="cuda")
+    h, bd = _prep(bank, "l", x, ids, torch.tensor(wts, device="cuda"), sc)
+    facs = [oracle_factors(a)["l"] for a in ads]
+    hv = h.view(4, 200, 16)
+    for b, j in enumerate(assign):
+        if j < 0:
+            assert not hv[b].any() and not bd[b].any()
+            continue
+        a_f, b_f = (torch.from_numpy(f) for f in facs[j])
+        assert torch.equal(bd[b].cpu(), b_f.bfloat16())                 # bit-exact decode
+        want = wts[b] * sc * (x[b].float().cpu() @ a_f.T)
+        assert max_abs_rel(hv[b].float().cpu(), want) <= 2e-2 and rel_fro(hv[b].float().cpu(), want) < 1e-2
+    assert device_errors() == 0
+
+
+@pytest.mark.parametrize("m", [256, 128, 512])
+def test_fused_gemm_layer_matches_truth_and_default_path(m):
+    d_in, d_out = 1024, 768
+    ads = [random_adapter([("l", d_in, d_out)], rank=16, seed=s) for s in range(4)]
+    bank = PackedBank.from_adapters(ads, "cuda")
+    torch.manual_seed(0)
+    base = torch.nn.Linear(d_in, d_out).cuda().bfloat16()
+    layer = PackedLoRALinear(base, bank, "l", 16, 0.5)
+    assign = [3, 0, -1, 2]
+    layer.assign = torch.tensor(assign, dtype=torch.int32, device="cuda")
+    x = torch.randn(4, m, d_in, generator=torch.Generator().manual_seed(m)).bfloat16().cuda()
+    with torch.no_grad():
+        y0 = layer(x)
+        layer.fused_gemm = True
+        y1 = layer(x)
+    facs = [oracle_factors(a)["l"] for a in ads]
+    ref = x.float() @ base.weight.float().T + base.bias.float()
+    for b, j in enumerate(assign):
+        if j >= 0:
+            a_f, b_f = (torch.from_numpy(f).cuda() for f in facs[j])
+            ref[b] += 0.5 * (x[b].float() @ a_f.T) @ b_f.T
+    for y in (y0, y1):
+        check(y.view(-1, d_out), ref.view(-1, d_out))
+    with torch.no_grad():                                   # the unrouted sample sees the base linear only
+        check(y1[2], x[2].float() @ base.weight.float().T + base.bias.float())
+    assert device_errors() == 0
+
+
+def test_fused_gemm_layer_serves_a_kohya_row_range():
+    mods = kohya.kohya_flux_modules(rank=16, double_blocks=1, single_blocks=1, hidden=256, mlp_ratio=4)
+    from lithe_b200.fileio import LitheAdapter
+    import numpy as np
+    ads = []
+    for s in range(2):
+        rng = np.random.default_rng(s)
+        idx = {mm["name"]: {"A": rng.integers(0, 512, (3, mm["shape_a"][0] * mm["shape_a"][1] // 64)).astype(np.uint16),
+                            "B": rng.integers(0, 512, (3, mm["shape_b"][0] * mm["shape_b"][1] // 64)).astype(np.uint16)}
+               for mm in mods}
+        ads.append(LitheAdapter(modules=mods, indices=idx, rank=16, alpha=16.0, key_format="kohya"))
+    bank = PackedBank.from_adapters(ads, "cuda")
+    name, rows = "lora_unet_double_blocks_0_img_attn_qkv", (256, 512)        # to_k
+    base = torch.nn.Linear(256, 256).cuda().bfloat16()
+    layer = PackedLoRALinear(base, bank, name, 16, 1.0, rows=rows)
+    layer.assign = torch.tensor([1, 0], dtype=torch.int32, device="cuda")
+    x = torch.randn(2, 256, 256, generator=torch.Generator().manual_seed(9)).bfloat16().cuda()
+    with torch.no_grad():
+        y0 = layer(x)
+        layer.fused_gemm = True
+        y1 = layer(x)
+    ref = x.float() @ base.weight.float().T + base.bias.float()
+    for b, j in enumerate([1, 0]):
+        ia, ib, sa, sb = kohya.split_indices(ads[j])["transformer_blocks.0.attn.to_k"]
+        from oracle import decode_ref
+        from tests.helpers import oracle_pools
+        pa, pb = oracle_pools()
+        a_f = torch.from_numpy(decode_ref.decode_factor(ia, sa, pa)).cuda()
+        b_f = torch.from_numpy(decode_ref.decode_factor(ib, sb, pb)).cuda()
+        ref[b] += (x[b].float() @ a_f.T) @ b_f.T
+    check(y0.view(-1, 256), ref.view(-1, 256))
+    check(y1.view(-1, 256), ref.view(-1, 256))
+    assert device_errors() == 0
