@@ -874,6 +874,111 @@ def run_hotswap(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------- fused LoRA GEMM workload
+LORA_GEMM_SHAPES = [  # (tag, tokens per sample, d_in, d_out, linears per forward) at 1024^2, B = 14
+    ("img_sq", 4096, 3072, 3072, 76), ("img_up", 4096, 3072, 12288, 19), ("img_dn", 4096, 12288, 3072, 19),
+    ("txt_sq", 512, 3072, 3072, 76), ("txt_up", 512, 3072, 12288, 19), ("txt_dn", 512, 12288, 3072, 19),
+    ("single_sq", 4608, 3072, 3072, 114)]
+
+
+def run_lora_gemm(args):
+    """The 342-linear LoRA forward of a 1024^2 B=14 FLUX step as fused-expand GEMMs: per shape,
+    lithe_lora_prep + lithe_lora_gemm (the LoRA-serving linear), the plain tcgen05 GEMM and
+    cuBLAS's bf16 GEMM (torch.nn.functional.linear), interleaved, best of `steps` rounds."""
+    import torch.nn.functional as F
+    from lithe_b200.kernels import PackedBank, PackedLayout, PackedLoRALinear
+    from lithe_b200.kernels import _launch as _lk
+
+    world, rank, local = dist_env()
+    metric = "fused LoRA linear TFLOP/s (base GEMM + rank-16 expand, 342 FLUX linears at 1024^2, B=14)"
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no fused base-GEMM path; its LoRA "
+                              "linear is nn.Linear + a delta pass, timed per linear by the flux_sweep_b14 workload"}))
+        return
+    init_dist(world, local)
+    dev = torch.device("cuda", local)
+    batch = BATCH
+    rows_override = args.rows
+    total_flops = total_ours = total_cublas = total_plain = 0.0
+    per = []
+    gen = torch.Generator(device=dev)
+    gen.manual_seed(11 + rank)
+    err = _lk.error_word(dev)
+    for tag, m, d_in, d_out, count in LORA_GEMM_SHAPES:
+        if args.shapes and tag not in args.shapes.split(","):
+            continue
+        mm = m if not rows_override else max(256, rows_override // batch // 256 * 256)
+        lay = PackedLayout.from_modules([{"name": "l", "shape_a": [RANK, d_in], "shape_b": [d_out, RANK]}])
+        bank = PackedBank(lay, 1000, dev)
+        bank.fill_random(seed=3)
+        base = torch.nn.Linear(d_in, d_out).to(device=dev, dtype=torch.bfloat16)
+        layer = PackedLoRALinear(base, bank, "l", RANK, 1.0, fused_gemm=True)
+        layer.assign = torch.randperm(1000, generator=torch.Generator().manual_seed(5))[:batch].to(torch.int32).to(dev)
+        x = torch.randn(batch, mm, d_in, device=dev, dtype=torch.bfloat16, generator=gen)
+        x2 = x.view(-1, d_in)
+        out = torch.empty(batch * mm, d_out, device=dev, dtype=torch.bfloat16)
+        fs = {"ours": lambda: layer(x), "plain": lambda: _lk.lora_gemm_(x2, base.weight, base.bias, out),
+              "cublas": lambda: F.linear(x2, base.weight, base.bias)}
+        best = {k: float("inf") for k in fs}
+        stream = torch.cuda.current_stream(dev)
+        with torch.no_grad():
+            for f in fs.values():
+                for _ in range(max(1, args.warmup)):
+                    f()
+            torch.cuda.synchronize(dev)
+            window = 5            # calls per event window: host launch work overlaps the GPU as in a forward
+            for _ in range(args.steps):
+                for k, f in fs.items():
+                    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                    for _ in range(window):
+                        f()
+                    e1.record(stream)
+                    torch.cuda.synchronize(dev)
+                    best[k] = min(best[k], e0.elapsed_time(e1) / 1000.0 / window)
+        fl = 2.0 * batch * mm * d_out * (d_in + RANK)
+        per.append({"tag": tag, "rows": batch * mm, "d_in": d_in, "d_out": d_out,
+                    **{k + "_us": round(v * 1e6, 1) for k, v in best.items()},
+                    "ours_tflops": round(fl / best["ours"] / 1e12, 1)})
+        c = 1 if rows_override else count
+        total_flops += c * fl
+        total_ours += c * best["ours"]
+        total_plain += c * best["plain"]
+        total_cublas += c * best["cublas"]
+        del bank, layer, base, x, out
+        torch.cuda.empty_cache()
+    errors = _lk.device_errors(dev)
+    ms = max_over_ranks(total_ours * 1000.0, world)
+    value = total_flops * world / (ms / 1000.0) / 1e12
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("bf16_tflops", 1590.0)
+    if rank == 0:
+        print(json.dumps({
+            "metric": metric, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16 (fp32 accumulate)", "data": "synthetic: N(0,1) activations, random-init linears, seeded "
+            "uniform 9-bit packed adapters", "timing": "best of `steps` interleaved rounds per shape, CUDA events around 5 back-to-back calls",
+            "config": {"workload": args.workload, "batch": batch, "rank": RANK,
+                       "step": "342 linears of one 1024^2 forward" if not rows_override else f"rows override {rows_override}"},
+            "roofline": {"bound": "tensor", "achieved": value / world, "peak": peak, "unit": "TFLOP/s",
+                         "frac": value / world / peak,
+                         "peak_source": "bf16_tflops (burst cuBLAS 8192^3) of " +
+                                        ("measured" if "bf16_tflops" in peaks else "fallback"),
+                         "kernel": "lithe::lg::lora_gemm_pair_kernel (+ lithe_lora_prep)", "traffic": None},
+            "vs_cublas_plain_gemm": total_cublas / total_ours, "ours_plain_vs_cublas": total_cublas / total_plain,
+            "lora_prep_and_expand_ms_per_step": (total_ours - total_plain) * 1000.0,
+            "per_shape": per, "cpu_baseline": None, "e2e": None,
+            "gpu_launches": 5 * 5 * sum(1 for _ in per) * args.steps, "device_errors": errors}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def wrap_linears_any(model, names, table):
     """Point model.<name> at table[name] (swaps between plain, packed and dense wrappers)."""
     for n in names:
@@ -889,7 +994,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["lithe", "reference"], default="lithe")
     ap.add_argument("--workload", choices=["flux_sweep_b14", "decode_flux342", "decode_kohya304", "denoise_512",
-                                           "denoise_256_b96", "denoise_1024", "hotswap_kohya304"],
+                                           "denoise_256_b96", "denoise_1024", "hotswap_kohya304",
+                                           "lora_gemm_flux"],
                     default="flux_sweep_b14", help="flux_sweep_b14: fused decode+SGMV (default); decode_*: "
                     "standalone packed decode of 14 resident adapters per launch")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")
@@ -902,12 +1008,14 @@ def main():
                     help="strong scaling: split the fixed B=14 batch by sample across ranks (default: weak, "
                          "every rank runs its own B=14 batch)")
     ap.add_argument("--shapes", default="", help="comma list of d_inxd_out to run (default: all four), "
-                    "e.g. 3072x3072 for a single-shape profiling run")
+                    "e.g. 3072x3072 for a single-shape profiling run; for lora_gemm_flux, shape tags (img_sq, ...)")
+    ap.add_argument("--rows", type=int, default=0, help="lora_gemm_flux: total rows per shape instead of B x tokens "
+                    "(a small case for profiling)")
     args = ap.parse_args()
     if args.mode:
         from lithe_b200.kernels import _launch
         _launch.DEFAULT_MODE = args.mode
-    if args.shapes:
+    if args.shapes and args.workload == "flux_sweep_b14":
         global SHAPES
         want = [tuple(int(v) for v in s.split("x")) for s in args.shapes.split(",")]
         SHAPES = [sh for sh in SHAPES if sh in want]
@@ -921,6 +1029,8 @@ def main():
         run_denoise(args)
     elif args.workload == "hotswap_kohya304":
         run_hotswap(args)
+    elif args.workload == "lora_gemm_flux":
+        run_lora_gemm(args)
     elif args.impl == "reference":
         run_reference(args)
     else:

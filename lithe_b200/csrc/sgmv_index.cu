@@ -180,7 +180,7 @@ __device__ __forceinline__ void decode_chunk(const SgmvParams& p, const DecodeTa
 // Decoder warp d fills the factor chunk of every pipeline position pos with
 // pos % kDecodeWarps == d.  The indices of its next chunk are fetched before it waits for
 // and decodes the current one, so the index-load latency overlaps the decode.
-template <int kRank>
+template <int kRank, int kDec>
 __device__ void run_decoder(int d, int lane, const SgmvParams& p, uint8_t* facts, const DecodeTables* tab,
                             const float* lut_s, uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin,
                             int u_end) {
@@ -198,7 +198,7 @@ __device__ void run_decoder(int d, int lane, const SgmvParams& p, uint8_t* facts
             first = false;
             const int n = un.nx + un.no;
             if (c < n) {
-                const int skip = (d - static_cast<int>(pos % kDecodeWarps) + kDecodeWarps) % kDecodeWarps;
+                const int skip = (d - static_cast<int>(pos % kDec) + kDec) % kDec;
                 if (c + skip < n) {
                     c += skip;
                     pos += skip;
@@ -483,8 +483,8 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
     }
 }
 
-template <int kRank, bool kStaged>
-__global__ void __launch_bounds__(kStaged ? kThreadsStaged : kThreads, 1)
+template <int kRank, bool kStaged, int kDec>
+__global__ void __launch_bounds__(kStaged ? kThreadsStaged : 32 * (kConsumerWarps + 1 + kDec), 1)
     sgmv_index_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmo_ld,
                       const __grid_constant__ SgmvParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -530,7 +530,8 @@ __global__ void __launch_bounds__(kStaged ? kThreadsStaged : kThreads, 1)
             issued = run_producer<kStaged>(p, &tmx, &tmo_ld, tiles, facts, full, empty, abort, u_begin, u_end);
         }
     } else if constexpr (!kStaged) {
-        run_decoder<kRank>(warp - kFirstDecodeWarp, lane, p, facts, tab, lut_s, full, empty, abort, u_begin, u_end);
+        run_decoder<kRank, kDec>(warp - kFirstDecodeWarp, lane, p, facts, tab, lut_s, full, empty, abort, u_begin,
+                                 u_end);
     }
     __syncthreads();
     // After an aborted pipeline, let the producer's last TMA loads land before the block's
@@ -628,11 +629,11 @@ __global__ void __launch_bounds__(256) decode_bdec_kernel(const __grid_constant_
     }
 }
 
-template <int kRank, bool kStaged>
+template <int kRank, bool kStaged, int kDec = kDecodeWarps>
 static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, const SgmvParams& p, int grid,
                            int device, int sms, int32_t batch, uint8_t* ws, cudaStream_t stream) {
     static bool configured[64] = {false};
-    auto kern = sgmv_index_kernel<kRank, kStaged>;
+    auto kern = sgmv_index_kernel<kRank, kStaged, kDec>;
     if (!configured[device]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmemBytes));
@@ -647,7 +648,7 @@ static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, co
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "decode_chunks_kernel launch");
     }
-    kern<<<grid, kStaged ? kThreadsStaged : kThreads, kSmemBytes, stream>>>(tmx, tmo_ld, p);
+    kern<<<grid, kStaged ? kThreadsStaged : 32 * (kConsumerWarps + 1 + kDec), kSmemBytes, stream>>>(tmx, tmo_ld, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "sgmv_index_kernel launch");
     return LITHE_OK;
@@ -802,6 +803,9 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
 #define LITHE_LAUNCH(R)                                                                         \
     return ws ? launch_rank<R, true>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)          \
               : launch_rank<R, false>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)
+    // Shrink-only form (lithe_lora_prep): every 8 KB x tile needs an A-chunk decode and no
+    // output tile is streamed, so the decode dominates; it runs with 8 decoder warps.
+    if (prep) return launch_rank<16, false, 2 * kDecodeWarps>(tmx, tmo_ld, p, grid, device, sms, batch, w, s);
     switch (rank) {
         case 16: LITHE_LAUNCH(16);
         case 8: LITHE_LAUNCH(8);

@@ -60,8 +60,28 @@ def stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
 
+_lut_cache: dict = {}
+
+
 def lut_array(lut: np.ndarray) -> ctypes.Array:
-    return _lib.float_array(np.asarray(lut, dtype=np.float32).reshape(-1))
+    """The level LUT as a ctypes float array (cached per LUT array object; LUTs are immutable)."""
+    key = id(lut)
+    hit = _lut_cache.get(key)
+    if hit is not None and hit[0] is lut:
+        return hit[1]
+    arr = _lib.float_array(np.asarray(lut, dtype=np.float32).reshape(-1))
+    if len(_lut_cache) > 256:
+        _lut_cache.clear()
+    _lut_cache[key] = (lut, arr)
+    return arr
+
+
+def device_ctx(device: torch.device):
+    """torch.cuda.device(device), or a no-op when it is already the current device."""
+    import contextlib
+    if device.index is None or device.index == torch.cuda.current_device():
+        return contextlib.nullcontext()
+    return torch.cuda.device(device)
 
 
 def index_view(base: torch.Tensor, fmt: int, levels: int, slot_stride: int, offset: int,
@@ -230,7 +250,7 @@ def lora_gemm_(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tenso
             raise ValueError("h must be (rows, rank) and b_dec (samples, n, rank)")
     if err is None:
         err = error_word(x.device)
-    with torch.cuda.device(x.device):
+    with device_ctx(x.device):
         rc = _lib.lib().lithe_lora_gemm(
             x.data_ptr(), weight.data_ptr(), bias.data_ptr() if bias is not None else None, out.data_ptr(), rows, n,
             k, h.data_ptr() if h is not None else None, b_dec.data_ptr() if b_dec is not None else None,
@@ -256,7 +276,7 @@ def lora_prep_(x: torch.Tensor, *, view_a: _lib.IndexView, view_b: _lib.IndexVie
         raise ValueError("ids must be a contiguous (B,) int32 tensor on x's device")
     if err is None:
         err = error_word(x.device)
-    with torch.cuda.device(x.device):
+    with device_ctx(x.device):
         rc = _lib.lib().lithe_lora_prep(
             x.data_ptr(), ctypes.byref(view_a), ctypes.byref(view_b), int(n_slots), ids.data_ptr(),
             weights.data_ptr() if weights is not None else None, bsz, m, d_in, int(d_out), 16, lut_array(lut),

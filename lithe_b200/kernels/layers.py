@@ -107,6 +107,7 @@ class PackedLoRALinear(nn.Module):
         # the fused decode/SGMV kernel's read-modify-write of the output.  The base product is
         # then ours, not cuBLAS's (same math, different fp32 summation order).
         self.fused_gemm = bool(fused_gemm)
+        self._views = None                 # (bank storage key, (view_a, view_b)) of the fused path
 
     def _gemm_ok(self, x3: torch.Tensor) -> bool:
         w = self.base.weight
@@ -139,7 +140,10 @@ class PackedLoRALinear(nn.Module):
             assign = torch.zeros(bsz, dtype=torch.int32, device=x.device)
         ids = assign.to(device=x.device, dtype=torch.int32).contiguous()
         w = None if self.weights is None else self.weights.to(device=x.device, dtype=torch.float32).contiguous()
-        va, vb = self.bank.views(self.name, self.rows)
+        key = (self.bank.words.data_ptr(), self.bank.slot_stride)
+        if self._views is None or self._views[0] != key:
+            self._views = (key, self.bank.views(self.name, self.rows))
+        va, vb = self._views[1]
         h = torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device)
         b_dec = torch.empty(bsz, d_out, 16, dtype=torch.bfloat16, device=x.device)
         _launch.lora_prep_(x3, view_a=va, view_b=vb, n_slots=self.bank.n_slots, ids=ids, weights=w, d_out=d_out,
