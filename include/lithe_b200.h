@@ -244,6 +244,17 @@ LITHE_API int32_t lithe_pack_raw(const uint16_t* raw, int64_t n_raw, const lithe
                        int32_t n_segments, int32_t num_levels, uint64_t* words, int64_t n_words,
                        int32_t* err_flag, void* stream);
 
+/*
+ * lithe_pack_raw for n_payloads payloads in one launch (a bulk load of payloads already on the
+ * device): payload y at raw + y * raw_stride goes to bank slot slot_ids[y] (slot y when
+ * slot_ids is NULL), i.e. bank + slot * slot_stride words.  Slots outside [0, n_slots) set
+ * LITHE_DEVERR_SLOT and are skipped.  n_payloads <= 65535; raw_stride >= n_raw, a multiple of 8.
+ */
+LITHE_API int32_t lithe_pack_raw_batch(const uint16_t* raw, int64_t raw_stride, int32_t n_payloads, int64_t n_raw,
+                             const lithe_pack_segment* segments, int32_t n_segments, int32_t num_levels,
+                             uint64_t* bank, int64_t slot_stride, int64_t n_slots, const int32_t* slot_ids,
+                             int64_t n_words, int32_t* err_flag, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

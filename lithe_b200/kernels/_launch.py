@@ -282,3 +282,30 @@ def lora_prep_(x: torch.Tensor, *, view_a: _lib.IndexView, view_b: _lib.IndexVie
             weights.data_ptr() if weights is not None else None, bsz, m, d_in, int(d_out), 16, lut_array(lut),
             float(scaling), h.data_ptr(), b_dec.data_ptr(), err.data_ptr(), stream_handle(x.device))
     _lib.check(rc, "lithe_lora_prep")
+
+
+def pack_raw_batch_(raw: torch.Tensor, segments: torch.Tensor, levels: int, bank: torch.Tensor,
+                    slot_ids: Optional[torch.Tensor], n_words: int, err: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """lithe_pack_raw_batch: raw (n, payload) 16-bit rows -> bank rows slot_ids[i] (words [0, n_words))."""
+    _require_cuda(raw, "raw")
+    if raw.dtype not in (torch.int16, torch.uint16) or raw.dim() != 2 or raw.stride(1) != 1 or raw.stride(0) % 8:
+        raise ValueError("raw must be a (n, payload) 16-bit tensor with unit inner stride and an 8-aligned row stride")
+    if segments.dtype != torch.int64 or segments.dim() != 2 or segments.shape[1] != 3 \
+            or not segments.is_contiguous() or segments.device != raw.device:
+        raise ValueError("segments must be a contiguous (n, 3) int64 tensor on raw's device")
+    if bank.dim() != 2 or bank.dtype not in (torch.int64, torch.uint64) or not bank.is_contiguous() \
+            or bank.device != raw.device:
+        raise ValueError("bank must be a contiguous (n_slots, slot_stride) 64-bit tensor on raw's device")
+    if slot_ids is not None and (slot_ids.dtype != torch.int32 or slot_ids.numel() != raw.shape[0]
+                                 or not slot_ids.is_contiguous() or slot_ids.device != raw.device):
+        raise ValueError("slot_ids must be a contiguous (n,) int32 tensor on raw's device")
+    if err is None:
+        err = error_word(raw.device)
+    with device_ctx(raw.device):
+        rc = _lib.lib().lithe_pack_raw_batch(
+            raw.data_ptr(), raw.stride(0), raw.shape[0], raw.shape[1], segments.data_ptr(), segments.shape[0],
+            int(levels), bank.data_ptr(), bank.shape[1], bank.shape[0],
+            slot_ids.data_ptr() if slot_ids is not None else None, int(n_words), err.data_ptr(),
+            stream_handle(raw.device))
+    _lib.check(rc, "lithe_pack_raw_batch")
+    return bank

@@ -279,6 +279,15 @@ class PackedBank:
         _launch.pack_raw_(raw, self.layout.segments_on(self.device), self.layout.num_levels,
                           self.words[slot, : self.layout.num_words], err)
 
+    def load_raw_batch(self, slot_ids, raw: torch.Tensor, err: Optional[torch.Tensor] = None) -> None:
+        """Pack n raw payloads already on the device ((n, num_indices) int16 rows, the stream
+        order of the file) into slots ``slot_ids`` with one kernel launch."""
+        ids = torch.as_tensor(slot_ids, dtype=torch.int32).reshape(-1).to(self.device)
+        if raw.dim() != 2 or raw.shape[0] != ids.numel() or raw.shape[1] != self.layout.num_indices:
+            raise ValueError(f"raw must be ({ids.numel()}, {self.layout.num_indices}) for these slots")
+        _launch.pack_raw_batch_(raw, self.layout.segments_on(self.device), self.layout.num_levels, self.words, ids,
+                                self.layout.num_words, err)
+
     def fill_random(self, seed: int, slots: Optional[slice] = None) -> None:
         """Seeded uniform 9-bit indices in every slot: int64 random_() draws uniform words in
         [0, 2^63), i.e. 7 uniform 9-bit fields with the unused top bit clear."""

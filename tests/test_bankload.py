@@ -74,3 +74,17 @@ def test_pack_raw_argument_errors():
     assert lib.lithe_pack_raw(0x1000, 21, None, 2, 3, 0x3000, 3, None, None) == _lib.ERR_ARG
     assert lib.lithe_pack_raw(0x1000, 21, 0x2000, 0, 3, 0x3000, 3, None, None) == _lib.ERR_ARG
     assert lib.lithe_pack_raw(None, 0, None, 0, 3, None, 0, None, None) == _lib.OK                # empty
+
+
+def test_pack_raw_batch_argument_errors():
+    lib = _lib.lib()
+    seg = 0x2000
+    # raw_stride shorter than a payload, and not a multiple of 8
+    assert lib.lithe_pack_raw_batch(0x1000, 20, 2, 21, seg, 2, 3, 0x3000, 4, 2, None, 3, None, None) == _lib.ERR_ARG
+    assert lib.lithe_pack_raw_batch(0x1000, 25, 2, 21, seg, 2, 3, 0x3000, 4, 2, None, 3, None, None) == _lib.ERR_ARG
+    # slot stride shorter than a slot's words; more payloads than slots without slot_ids
+    assert lib.lithe_pack_raw_batch(0x1000, 24, 2, 21, seg, 2, 3, 0x3000, 2, 2, None, 3, None, None) == _lib.ERR_ARG
+    assert lib.lithe_pack_raw_batch(0x1000, 24, 3, 21, seg, 2, 3, 0x3000, 4, 2, None, 3, None, None) == _lib.ERR_ARG
+    assert lib.lithe_pack_raw_batch(0x1000, 24, 70000, 21, seg, 2, 3, 0x3000, 4, 2, 0x4000, 3, None, None) \
+        == _lib.ERR_UNSUPPORTED
+    assert lib.lithe_pack_raw_batch(0x1000, 24, 0, 21, seg, 2, 3, 0x3000, 4, 2, None, 3, None, None) == _lib.OK

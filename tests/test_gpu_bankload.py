@@ -145,3 +145,31 @@ def test_pack_raw_other_level_counts(levels):
     torch.cuda.synchronize()
     assert np.array_equal(words.cpu().numpy().view(np.uint64), decode_ref.pack_raw(raw, mods, levels=levels))
     assert device_errors() == 0
+
+
+def test_batched_pack_matches_single_launches():
+    mods = kohya.kohya_flux_modules(rank=16, double_blocks=2, single_blocks=2, hidden=256)
+    lay = PackedLayout.from_modules(mods)
+    n = 5
+    raws = [np.random.default_rng(40 + i).integers(0, 512, lay.num_indices).astype("<u2") for i in range(n)]
+    stride = (lay.num_indices + 7) // 8 * 8 + 8                       # padded rows: a strided batch
+    raw2 = torch.zeros(n, stride, dtype=torch.int16)
+    for i, r in enumerate(raws):
+        raw2[i, : lay.num_indices] = torch.from_numpy(r.view(np.int16))
+    raw2 = raw2.cuda()[:, : lay.num_indices]
+    bank = PackedBank(lay, 9, "cuda")
+    slots = [7, 0, 3, 8, 2]
+    bank.load_raw_batch(slots, raw2)
+    ref = PackedBank(lay, 9, "cuda")
+    for s, r in zip(slots, raws):
+        ref.load_raw(s, dev_raw(r))
+    torch.cuda.synchronize()
+    assert torch.equal(bank.words, ref.words)
+    for s, r in zip(slots, raws):
+        assert np.array_equal(slot_words(bank, s), decode_ref.pack_raw(r, mods))
+    assert device_errors() == 0
+    # an out-of-range slot is flagged and skipped
+    bank.load_raw_batch([1, 99], raw2[:2])
+    torch.cuda.synchronize()
+    assert device_errors() & 1                                         # LITHE_DEVERR_SLOT
+    assert np.array_equal(slot_words(bank, 1), decode_ref.pack_raw(raws[0], mods))
