@@ -59,3 +59,37 @@ def test_tiny_flux_lithe_matches_dense_comparator():
     assert rel_fro(outs["lithe"], outs["base"]) > 1e-3
     assert rel_fro(outs["lithe"], outs["dense"]) < 2e-2
     assert rel_fro(outs["lithe_loop"], outs["dense_loop"]) < 3e-2
+
+
+def test_tiny_flux_fused_gemm_path_matches_default_path():
+    """With 256-token streams every LoRA linear of the tiny model is eligible for the expand-in-
+    GEMM path (n % 256, k % 64, tokens % 128): the whole model's output must agree with the
+    cuBLAS + SGMV path to bf16 precision, and with the dense comparator."""
+    torch.manual_seed(1)
+    cfg = FluxConfig.tiny()
+    base_model = FluxShapedTransformer(cfg).cuda().bfloat16()
+    base_state = {k: v.clone() for k, v in base_model.state_dict().items()}
+    targets = lora_targets(base_model)
+    layout = PackedLayout.from_modules([{"name": n, "shape_a": [16, m.in_features], "shape_b": [m.out_features, 16]}
+                                        for n, m in targets])
+    bank = PackedBank(layout, 8, "cuda")
+    bank.fill_random(seed=4)
+    slots = [2, 7]
+    lat = torch.randn(2, 256, cfg.in_channels, device="cuda").bfloat16()
+    txt = torch.randn(2, 256, cfg.text_dim, device="cuda").bfloat16()
+    pooled = torch.randn(2, cfg.pooled_dim, device="cuda").bfloat16()
+    t = torch.full((2,), 0.5, device="cuda")
+    outs = {}
+    for mode in ("lithe", "fused", "dense"):
+        model = FluxShapedTransformer(cfg).cuda().bfloat16()
+        model.load_state_dict(base_state)
+        wrapped = _wire(model, "dense" if mode == "dense" else "lithe", bank, slots)
+        if mode == "fused":
+            for m in wrapped.values():
+                assert m._gemm_ok(torch.empty(2, 256, m.base.in_features, dtype=torch.bfloat16, device="cuda"))
+                m.fused_gemm = True
+        with torch.no_grad():
+            outs[mode] = model(lat, txt, pooled, t).float()
+    assert torch.isfinite(outs["fused"]).all()
+    assert rel_fro(outs["fused"], outs["lithe"]) < 2e-2
+    assert rel_fro(outs["fused"], outs["dense"]) < 2e-2
