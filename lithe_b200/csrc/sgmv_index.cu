@@ -300,7 +300,12 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
     const int grp = w / kGroupWarps;     // this warp's group: positions pos % kGroups == grp
     const int wr = w % kGroupWarps;      // row block within the tile
     const int g = lane >> 2, t4 = lane & 3;
-    const int r0 = 16 * wr + g;          // rows r0 and r0 + 8 of the 64-token tile
+    // Fragment row g holds token row gr = sigma(g): a quarter-warp (g = 2q, 2q+1) then reads
+    // token rows q and q + 4, whose 128-byte swizzles (16-byte unit ^= row & 7) differ in bit
+    // 2, so its eight 16-byte reads hit eight different bank groups (rows 2q, 2q+1 would share
+    // four and conflict 2-way).  Rank / logical-column indices stay on g.
+    const int gr = (g >> 1) | ((g & 1) << 2);
+    const int r0 = 16 * wr + gr;         // rows r0 and r0 + 8 of the 64-token tile
     uint32_t n_xchg = 0;                 // exchanges done (mbarrier phase parity)
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
     const bool accum = p.accumulate != 0;
@@ -337,8 +342,8 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
             const uint4 f1 = lds128(fa + (g + 8) * 32 + (t4 & 1) * 16);
 #pragma unroll
             for (int win = 0; win < 2; ++win) {
-                const uint4 xa = lds128(ra + (((4 * win + t4) ^ g) << 4));
-                const uint4 xb = lds128(rb + (((4 * win + t4) ^ g) << 4));
+                const uint4 xa = lds128(ra + (((4 * win + t4) ^ gr) << 4));
+                const uint4 xb = lds128(rb + (((4 * win + t4) ^ gr) << 4));
                 const uint32_t a0[4] = {xa.x, xb.x, xa.y, xb.y};
                 const uint32_t a1[4] = {xa.z, xb.z, xa.w, xb.w};
                 mma_bf16_16816(acc[0][win], a0, f0.x, f0.y, acc[0][win]);
@@ -421,7 +426,7 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
                 for (int q = 0; q < 2; ++q)
 #pragma unroll
                     for (int hr = 0; hr < 2; ++hr) {
-                        const uint4 o = accum ? lds128(tile + (r0 + 8 * hr) * 128 + ((((q << 2) + t4) ^ g) << 4))
+                        const uint4 o = accum ? lds128(tile + (r0 + 8 * hr) * 128 + ((((q << 2) + t4) ^ gr) << 4))
                                               : make_uint4(0, 0, 0, 0);
                         v[q][hr] = add_delta8<kRank>(o, d[q][2 * hr], d[q][2 * hr + 1]);
                     }
@@ -452,7 +457,7 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
                         for (int pp = 0; pp < 4; ++pp) {
                             const int col = base + pp * kPer;   // even: c0 at col, c1 at col + 1
                             const uint32_t o = accum ? *reinterpret_cast<const uint32_t*>(
-                                                           tile + (r0 + 8 * hr) * 128 + (((col >> 3) ^ g) << 4) +
+                                                           tile + (r0 + 8 * hr) * 128 + (((col >> 3) ^ gr) << 4) +
                                                            (col & 7) * 2)
                                                      : 0u;
                             v[q][hr][pp] = add_bf16x2(o, d[q][2 * hr], d[q][2 * hr + 1]);
