@@ -52,21 +52,21 @@ __global__ void __launch_bounds__(256) decode_packed_kernel(const __grid_constan
     view.level_stride = 0;
 
     const int64_t items = 2 * p.n_blocks;
-    const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
     constexpr int kBlockBytes = kF32 ? 256 : 128;
     char* out = static_cast<char*>(p.out) + sel * p.n_blocks * kBlockBytes;
-    for (int64_t item = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; item < items;
-         item += stride) {
-        const int64_t blk = item >> 1;
-        const uint32_t half = static_cast<uint32_t>(item & 1);
-        const int side = p.sides ? (p.sides[blk] != 0) : 0;
-        uint32_t k[LITHE_MAX_LEVELS];
-        fetch_indices<LITHE_MAX_LEVELS>(view, slot, blk, k, nullptr);
-        float v[8];
-        if (p.levels <= 3) decode_eight_fast(&tab, side, k, half, v);
-        else decode_eight<LITHE_MAX_LEVELS>(&lut_s[side][0][0], k, p.levels, half, v);
-        char* dst = out + blk * kBlockBytes;
-        if constexpr (kF32) {
+    if constexpr (kF32) {
+        const int64_t stride = static_cast<int64_t>(gridDim.x) * blockDim.x;
+        for (int64_t item = static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x; item < items;
+             item += stride) {
+            const int64_t blk = item >> 1;
+            const uint32_t half = static_cast<uint32_t>(item & 1);
+            const int side = p.sides ? (p.sides[blk] != 0) : 0;
+            uint32_t k[LITHE_MAX_LEVELS];
+            fetch_indices<LITHE_MAX_LEVELS>(view, slot, blk, k, nullptr);
+            float v[8];
+            if (p.levels <= 3) decode_eight_fast(&tab, side, k, half, v);
+            else decode_eight<LITHE_MAX_LEVELS>(&lut_s[side][0][0], k, p.levels, half, v);
+            char* dst = out + blk * kBlockBytes;
             const float4 lo = make_float4(v[0], v[1], v[2], v[3]);
             const float4 hi = make_float4(v[4], v[5], v[6], v[7]);
 #pragma unroll
@@ -75,11 +75,46 @@ __global__ void __launch_bounds__(256) decode_packed_kernel(const __grid_constan
                 d[0] = lo;
                 d[1] = hi;
             }
-        } else {
-            const uint4 q = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]),
-                                       pack_bf16x2(v[4], v[5]), pack_bf16x2(v[6], v[7]));
+        }
+    } else {
+        // bf16: a warp decodes 16 consecutive blocks (lane = one half block), then 4 shuffle
+        // rounds give every lane the 16-byte piece it stores, so each store instruction writes
+        // 4 whole blocks (512 contiguous bytes).  Piece q of a block holds values 8q .. 8q+7,
+        // i.e. half (q & 1) of the 16-value pattern.  Writing each half block to its 4 places
+        // from its own lane touched 16 blocks per store instruction and kept L1 saturated.
+        const int lane = threadIdx.x & 31;
+        const int64_t warp_id = (static_cast<int64_t>(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+        const int64_t n_warps = (static_cast<int64_t>(gridDim.x) * blockDim.x) >> 5;
+        for (int64_t base = warp_id * 32; base < items; base += n_warps * 32) {
+            const int64_t item = base + lane;
+            uint32_t q[4] = {0u, 0u, 0u, 0u};
+            if (item < items) {
+                const int64_t blk = item >> 1;
+                const uint32_t half = static_cast<uint32_t>(item & 1);
+                const int side = p.sides ? (p.sides[blk] != 0) : 0;
+                uint32_t k[LITHE_MAX_LEVELS];
+                fetch_indices<LITHE_MAX_LEVELS>(view, slot, blk, k, nullptr);
+                float v[8];
+                if (p.levels <= 3) decode_eight_fast(&tab, side, k, half, v);
+                else decode_eight<LITHE_MAX_LEVELS>(&lut_s[side][0][0], k, p.levels, half, v);
+                q[0] = pack_bf16x2(v[0], v[1]);
+                q[1] = pack_bf16x2(v[2], v[3]);
+                q[2] = pack_bf16x2(v[4], v[5]);
+                q[3] = pack_bf16x2(v[6], v[7]);
+            }
+            const int64_t blk0 = base >> 1;                 // first of the warp's 16 blocks
 #pragma unroll
-            for (int m = 0; m < 4; ++m) *reinterpret_cast<uint4*>(dst + half * 16 + m * 32) = q;
+            for (int j = 0; j < 4; ++j) {
+                const int b = 4 * j + (lane >> 3);          // block of this lane's piece
+                const int src = 2 * b + (lane & 1);         // lane that decoded its half
+                uint4 w;
+                w.x = __shfl_sync(0xffffffffu, q[0], src);
+                w.y = __shfl_sync(0xffffffffu, q[1], src);
+                w.z = __shfl_sync(0xffffffffu, q[2], src);
+                w.w = __shfl_sync(0xffffffffu, q[3], src);
+                if (blk0 + b < p.n_blocks)
+                    *reinterpret_cast<uint4*>(out + (blk0 + b) * kBlockBytes + (lane & 7) * 16) = w;
+            }
         }
     }
 }
