@@ -82,9 +82,19 @@ class Router:
 
 
 class MultiAdapterLinear(nn.Module):
-    def __init__(self, base: nn.Linear, router: Router, rank: int, pool_a: torch.Tensor, pool_b: torch.Tensor):
+    """``base(x)`` + the routed per-sample LoRA delta (``lithe/serve.py:47-97``).
+
+    ``fused_gemm``: when the route has one adapter column (no mixtures) and the shapes allow
+    it (rank 16, out_features % 256, in_features % 64, tokens per sample % 128), compute the
+    base linear with ``lithe_lora_gemm`` and apply the expand inside it; otherwise cuBLAS +
+    one fused decode/SGMV launch per route column.
+    """
+
+    def __init__(self, base: nn.Linear, router: Router, rank: int, pool_a: torch.Tensor, pool_b: torch.Tensor,
+                 fused_gemm: bool = False):
         super().__init__()
         self.base = base
+        self.fused_gemm = bool(fused_gemm)
         self.router = router
         self.rank = rank
         self.shape_a = (rank, base.in_features)
@@ -109,7 +119,37 @@ class MultiAdapterLinear(nn.Module):
         self.idx_b = torch.cat([self.idx_b, ib]).contiguous()
         self.scales.append(float(scale))
 
+    def _gemm_ok(self, x3: torch.Tensor) -> bool:
+        w, b = self.base.weight, self.base.bias
+        return (self.rank == 16 and x3.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.is_contiguous()
+                and (b is None or (b.dtype == torch.bfloat16 and b.is_contiguous()))
+                and w.shape[0] % 256 == 0 and w.shape[1] % 64 == 0 and x3.shape[1] % 128 == 0 and x3.shape[1] > 0)
+
+    def _forward_fused_gemm(self, x: torch.Tensor, xs: torch.Tensor, slot_ids: torch.Tensor,
+                            w: torch.Tensor) -> torch.Tensor:
+        bsz, m, d_in = xs.shape
+        d_out = self.base.out_features
+        va, vb = _launch.level_major_view(self.idx_a), _launch.level_major_view(self.idx_b)
+        h = torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device)
+        b_dec = torch.empty(bsz, d_out, 16, dtype=torch.bfloat16, device=x.device)
+        _launch.lora_prep_(xs, view_a=va, view_b=vb, n_slots=self.idx_a.shape[0], ids=slot_ids, weights=w,
+                           d_out=d_out, lut=self.lut, scaling=1.0, h=h, b_dec=b_dec)
+        out = torch.empty(bsz * m, d_out, dtype=torch.bfloat16, device=x.device)
+        _launch.lora_gemm_(xs.view(bsz * m, d_in), self.base.weight, self.base.bias, out, h=h, b_dec=b_dec,
+                           rows_per_sample=m)
+        return out.view(*x.shape[:-1], d_out)
+
     def forward(self, x: torch.Tensor) -> torch.Tensor:
+        if self.fused_gemm:
+            ids = self.router.ids
+            if ids is not None and not bool((ids < 0).all()) and ids.shape[0] == x.shape[0]:
+                bsz = ids.shape[0]
+                xs = x.reshape(bsz, -1, x.shape[-1]).contiguous()
+                cols = self.router.columns(x.device, tuple(self.scales))
+                if len(cols) == 1 and self._gemm_ok(xs):
+                    if torch.is_grad_enabled() and (x.requires_grad or self.base.weight.requires_grad):
+                        raise RuntimeError("lithe_b200 layers are inference-only (run under torch.no_grad())")
+                    return self._forward_fused_gemm(x, xs, *cols[0])
         out = self.base(x)
         ids = self.router.ids
         if ids is None or bool((ids < 0).all()):
@@ -127,9 +167,10 @@ class MultiAdapterLinear(nn.Module):
         return out
 
 
-def attach_adapters(model: nn.Module, adapters: List[LitheAdapter],
-                    router: Optional[Router] = None) -> Tuple[Router, Dict[str, MultiAdapterLinear]]:
-    """Wrap every linear named in the adapters' module list and load all index streams."""
+def attach_adapters(model: nn.Module, adapters: List[LitheAdapter], router: Optional[Router] = None,
+                    fused_gemm: bool = False) -> Tuple[Router, Dict[str, MultiAdapterLinear]]:
+    """Wrap every linear named in the adapters' module list and load all index streams
+    (``lithe/serve.py:100-127``); ``fused_gemm`` selects the expand-in-GEMM path where eligible."""
     if not adapters:
         raise ValueError("need at least one adapter")
     router = router or Router()
@@ -148,7 +189,7 @@ def attach_adapters(model: nn.Module, adapters: List[LitheAdapter],
             raise TypeError(f"{path} is not nn.Linear")
         parent_name, _, child = path.rpartition(".")
         parent = model.get_submodule(parent_name) if parent_name else model
-        layer = MultiAdapterLinear(base, router, ref.rank, pool_a, pool_b).to(base.weight.device)
+        layer = MultiAdapterLinear(base, router, ref.rank, pool_a, pool_b, fused_gemm=fused_gemm).to(base.weight.device)
         for ad in adapters:
             layer.add_adapter(ad.indices[name]["A"], ad.indices[name]["B"], float(ad.alpha) / ad.rank)
         setattr(parent, child, layer)

@@ -184,3 +184,60 @@ def test_fused_gemm_layer_serves_a_kohya_row_range():
     check(y0.view(-1, 256), ref.view(-1, 256))
     check(y1.view(-1, 256), ref.view(-1, 256))
     assert device_errors() == 0
+
+
+def test_serve_attach_adapters_fused_gemm_path():
+    """serve.attach_adapters(fused_gemm=True): single-adapter routes (with gains and an empty
+    route) take the expand-in-GEMM path and agree with the default path and the fp32 truth;
+    a mixture route falls back to the default path bit for bit."""
+    from lithe_b200 import serve
+
+    class Toy(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.up = torch.nn.Linear(512, 768)
+            self.down = torch.nn.Linear(768, 512)
+
+        def forward(self, x):
+            return self.down(torch.nn.functional.gelu(self.up(x)))
+
+    ads = [random_adapter([("up", 512, 768), ("down", 768, 512)], rank=16, seed=s) for s in range(3)]
+    torch.manual_seed(3)
+    base = Toy().cuda().bfloat16()
+    state = {k: v.clone() for k, v in base.state_dict().items()}
+    x = torch.randn(3, 256, 512, generator=torch.Generator().manual_seed(4)).bfloat16().cuda()
+    routes = [[(0, 1.0)], [(2, 0.5)], []]
+    outs = {}
+    for fused in (False, True):
+        model = Toy().cuda().bfloat16()
+        model.load_state_dict(state)
+        router, layers = serve.attach_adapters(model, ads, fused_gemm=fused)
+        router.set(routes)
+        with torch.no_grad():
+            outs[fused] = model(x).float()
+            if fused:
+                router.set([[(0, 0.6), (1, 0.4)], [(2, 1.0)], []])          # mixture: two columns
+                mix_fused = model(x)
+                for layer in layers.values():
+                    layer.fused_gemm = False
+                mix_default = model(x)
+                assert torch.equal(mix_fused, mix_default)
+    # fp32 truth of the two-layer model with the routed deltas on both layers
+    facs = [oracle_factors(a) for a in ads]
+
+    def layer_truth(inp, lin, name, route):
+        y = inp @ lin.weight.float().T + lin.bias.float()
+        for j, wj in route:
+            a_f, b_f = (torch.from_numpy(f).cuda() for f in facs[j][name])
+            y = y + wj * (inp @ a_f.T) @ b_f.T
+        return y
+
+    truth = []
+    for b, route in enumerate(routes):
+        z = torch.nn.functional.gelu(layer_truth(x[b].float(), base.up, "up", route).bfloat16().float())
+        truth.append(layer_truth(z.bfloat16().float(), base.down, "down", route))
+    truth = torch.stack(truth)
+    for fused in (False, True):
+        assert rel_fro(outs[fused].cpu(), truth.cpu()) < 2e-2, fused
+    assert rel_fro(outs[True].cpu(), outs[False].cpu()) < 2e-2
+    assert device_errors() == 0
