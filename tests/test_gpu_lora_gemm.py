@@ -233,9 +233,10 @@ def test_serve_attach_adapters_fused_gemm_path():
         return y
 
     truth = []
-    for b, route in enumerate(routes):
-        z = torch.nn.functional.gelu(layer_truth(x[b].float(), base.up, "up", route).bfloat16().float())
-        truth.append(layer_truth(z.bfloat16().float(), base.down, "down", route))
+    with torch.no_grad():
+        for b, route in enumerate(routes):
+            z = torch.nn.functional.gelu(layer_truth(x[b].float(), base.up, "up", route).bfloat16().float())
+            truth.append(layer_truth(z.bfloat16().float(), base.down, "down", route))
     truth = torch.stack(truth)
     for fused in (False, True):
         assert rel_fro(outs[fused].cpu(), truth.cpu()) < 2e-2, fused
