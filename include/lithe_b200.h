@@ -255,6 +255,15 @@ LITHE_API int32_t lithe_pack_raw_batch(const uint16_t* raw, int64_t raw_stride, 
                              uint64_t* bank, int64_t slot_stride, int64_t n_slots, const int32_t* slot_ids,
                              int64_t n_words, int32_t* err_flag, void* stream);
 
+/*
+ * Self-test of the bounded pipeline wait (no counterpart in the reference): one warp waits on
+ * an mbarrier that nothing arrives at.  After the wait's time limit (4 s) it ORs
+ * LITHE_DEVERR_TIMEOUT into *err_flag, writes 0 to *waited_ok (device int32, may be NULL) and
+ * returns; the context stays usable.  This is the path every kernel's waits take when a
+ * pipeline stalls, exercised without any fault.
+ */
+LITHE_API int32_t lithe_selftest_wait_timeout(int32_t* err_flag, int32_t* waited_ok, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -85,6 +85,7 @@ _SIGNATURES.update({
     "lithe_pack_raw_batch": (_c.c_int32, [
         _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_int64, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_void_p,
         _c.c_int64, _c.c_int64, _c.c_void_p, _c.c_int64, _c.c_void_p, _c.c_void_p]),
+    "lithe_selftest_wait_timeout": (_c.c_int32, [_c.c_void_p, _c.c_void_p, _c.c_void_p]),
     "lithe_decode_packed": (_c.c_int32, [
         _c.c_void_p, _c.c_int64, _c.c_int32, _c.c_void_p, _c.POINTER(_c.c_float), _c.c_void_p,
         _c.c_int32, _c.c_void_p]),

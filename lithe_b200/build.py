@@ -19,7 +19,7 @@ CSRC = PKG / "csrc"
 INCLUDE = ROOT / "include"
 LIB_DIR = PKG / "_lib"
 LIB_PATH = LIB_DIR / "liblithe_b200.so"
-SOURCES = ["host_common.cu", "decode_packed.cu", "sgmv_index.cu", "pack_raw.cu", "lora_gemm.cu"]
+SOURCES = ["host_common.cu", "decode_packed.cu", "sgmv_index.cu", "pack_raw.cu", "lora_gemm.cu", "selftest.cu"]
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 
