@@ -44,7 +44,6 @@ constexpr int kConsumerWarps = kGroupWarps * kGroups;
 constexpr int kDecodeWarps = 4;
 constexpr int kProducerWarp = kConsumerWarps;
 constexpr int kFirstDecodeWarp = kConsumerWarps + 1;
-constexpr int kThreads = 32 * (kConsumerWarps + 1 + kDecodeWarps);     // fused mode
 constexpr int kThreadsStaged = 32 * (kConsumerWarps + 1);                // staged mode: no decoder warps
 constexpr int kStages = 16;
 constexpr int kTileBytes = kBM * kChunk * 2;      // 8192

@@ -17,7 +17,7 @@ import os
 import socket
 import traceback
 from dataclasses import dataclass
-from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple
+from typing import Any, Callable, Dict, List, Sequence, Tuple
 
 import torch.multiprocessing as mp
 

@@ -1,7 +1,6 @@
 """.lithe -> resident slot on the device (lithe_pack_raw, PackedBank.load_raw, SlotLoader):
 every packed word bit-identical to the oracle's restatement of the reference's
 load_lithe -> flat_indices -> pack_indices chain, at golden, small and full FLUX sizes."""
-import json
 from pathlib import Path
 
 import numpy as np

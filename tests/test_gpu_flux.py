@@ -1,7 +1,6 @@
 """Index-resident LoRA in a (tiny) FLUX-shaped transformer: the 342-target wiring by module
 path, packed-bank routing per sample, and agreement with the dense decoded-factor comparator
 (the counterpart of the reference's multi-adapter FLUX test, which needs diffusers)."""
-import numpy as np
 import pytest
 import torch
 
