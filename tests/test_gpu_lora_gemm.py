@@ -2,12 +2,15 @@
 torch fp32 reference of the same op: out = x W^T + bias + h Bdec_sample^T, rounded to bf16.
 Tolerance (bf16 inputs, fp32 accumulation in a different order, one bf16 rounding of the
 output): max |got - ref| <= 1e-2 * max |ref| and relative Frobenius error < 5e-3."""
+import numpy as np
 import pytest
 import torch
 
-from lithe_b200 import device_errors
-from lithe_b200.kernels import _launch
-from tests.helpers import rel_fro
+from lithe_b200 import device_errors, kohya, serve
+from lithe_b200.fileio import LitheAdapter
+from lithe_b200.kernels import PackedBank, PackedLoRALinear, _launch
+from oracle import decode_ref
+from tests.helpers import max_abs_rel, oracle_factors, oracle_pools, random_adapter, rel_fro
 
 pytestmark = pytest.mark.gpu
 
@@ -84,9 +87,6 @@ def test_unsupported_shapes_are_rejected():
 
 
 # ------------------------------------------------------------------ prep + the fused layer path
-from lithe_b200 import kohya  # noqa: E402
-from lithe_b200.kernels import PackedBank, PackedLoRALinear  # noqa: E402
-from tests.helpers import max_abs_rel, oracle_factors, random_adapter  # noqa: E402
 
 
 def _prep(bank, name, x, ids, weights, scaling, rows=None):
@@ -153,8 +153,6 @@ def test_fused_gemm_layer_matches_truth_and_default_path(m):
 
 def test_fused_gemm_layer_serves_a_kohya_row_range():
     mods = kohya.kohya_flux_modules(rank=16, double_blocks=1, single_blocks=1, hidden=256, mlp_ratio=4)
-    from lithe_b200.fileio import LitheAdapter
-    import numpy as np
     ads = []
     for s in range(2):
         rng = np.random.default_rng(s)
@@ -175,8 +173,6 @@ def test_fused_gemm_layer_serves_a_kohya_row_range():
     ref = x.float() @ base.weight.float().T + base.bias.float()
     for b, j in enumerate([1, 0]):
         ia, ib, sa, sb = kohya.split_indices(ads[j])["transformer_blocks.0.attn.to_k"]
-        from oracle import decode_ref
-        from tests.helpers import oracle_pools
         pa, pb = oracle_pools()
         a_f = torch.from_numpy(decode_ref.decode_factor(ia, sa, pa)).cuda()
         b_f = torch.from_numpy(decode_ref.decode_factor(ib, sb, pb)).cuda()
@@ -190,7 +186,6 @@ def test_serve_attach_adapters_fused_gemm_path():
     """serve.attach_adapters(fused_gemm=True): single-adapter routes (with gains and an empty
     route) take the expand-in-GEMM path and agree with the default path and the fp32 truth;
     a mixture route falls back to the default path bit for bit."""
-    from lithe_b200 import serve
 
     class Toy(torch.nn.Module):
         def __init__(self):
