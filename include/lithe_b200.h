@@ -195,7 +195,8 @@ LITHE_API int32_t lithe_decode_packed_batch(const uint64_t* bank, int64_t slot_s
  *   b_dec  device bf16 (batch, d_out, 16): B_j of every sample, decoded and rounded to bf16
  *          (zero for unrouted samples)
  * Two launches on `stream`: the B decode and the fused kernel in shrink-only form (x is read
- * once, no output tiles).
+ * once, no output tiles).  Either output may be NULL to skip its half (not both): split targets
+ * of one fused Kohya module share A, so one h serves all of them.
  */
 LITHE_API int32_t lithe_lora_prep(const void* x, const lithe_index_view* idx_a, const lithe_index_view* idx_b,
                         int64_t n_slots, const int32_t* ids, const float* weights, int32_t batch, int32_t m,

@@ -698,7 +698,7 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
                         const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids, const float* weights,
                         int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank, const float* lut,
                         float scaling, int32_t* err_flag, void* ws, int64_t ws_bytes, void* stream,
-                        void* h_out = nullptr, void* bdec_out = nullptr) {
+                        void* h_out = nullptr, void* bdec_out = nullptr, bool prep = false) {
     if (batch < 0 || m < 0) return fail_arg("batch (%d) and m (%d) must be >= 0", batch, m);
     if (rank != 1 && rank != 2 && rank != 4 && rank != 8 && rank != 16)
         return fail_unsupported("rank must be one of 1, 2, 4, 8, 16; got %d", rank);
@@ -720,13 +720,12 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     if (!lut) return fail_arg("lut is NULL");
     if (n_slots < 0) return fail_arg("n_slots must be >= 0");
     if (batch == 0 || m == 0) return LITHE_OK;
-    const bool prep = h_out != nullptr;
     if (prep) {
         if (rank != 16) return fail_unsupported("lithe_lora_prep supports rank 16, got %d", rank);
-        if (!bdec_out) return fail_arg("b_dec is NULL");
+        if (!h_out && !bdec_out) return fail_arg("h and b_dec are both NULL");
         if (reinterpret_cast<uintptr_t>(h_out) % 16 || reinterpret_cast<uintptr_t>(bdec_out) % 16)
             return fail_arg("h and b_dec must be 16-byte aligned");
-        out = h_out;                  // only used for the alignment check and an unused tensor map below
+        out = h_out ? h_out : bdec_out;   // only used for the alignment check and an unused tensor map below
     }
     if (!x || !out || !ids) return fail_arg("x, out and ids must be non-NULL");
     if (reinterpret_cast<uintptr_t>(x) % 16 || reinterpret_cast<uintptr_t>(out) % 16)
@@ -780,12 +779,16 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     if (prep) {
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         // B side first: every sample's decoded factor, (batch, d_out, 16)
-        const int64_t warps_needed = static_cast<int64_t>(batch) * p.n_ochunks;
-        int64_t blocks = (warps_needed + 7) / 8;
-        if (blocks > 2LL * sms) blocks = 2LL * sms;
-        decode_bdec_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(bdec_out), batch);
-        cudaError_t e = cudaGetLastError();
-        if (e != cudaSuccess) return fail_cuda(e, "decode_bdec_kernel launch");
+        if (bdec_out) {
+            const int64_t warps_needed = static_cast<int64_t>(batch) * p.n_ochunks;
+            int64_t blocks = (warps_needed + 7) / 8;
+            if (blocks > 2LL * sms) blocks = 2LL * sms;
+            decode_bdec_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(bdec_out),
+                                                                              batch);
+            cudaError_t e = cudaGetLastError();
+            if (e != cudaSuccess) return fail_cuda(e, "decode_bdec_kernel launch");
+        }
+        if (!h_out) return LITHE_OK;
         // A side: the fused kernel in shrink-only form (x tiles only, h stored after the shrink)
         p.h_out = static_cast<__nv_bfloat16*>(h_out);
         p.n_ochunks = 0;
@@ -836,9 +839,9 @@ extern "C" int32_t lithe_lora_prep(const void* x, const lithe_index_view* idx_a,
                                    int32_t d_in, int32_t d_out, int32_t rank, const float* lut, float scaling, void* h,
                                    void* b_dec, int32_t* err_flag, void* stream) {
     lithe::clear_error();
-    if (batch > 0 && m > 0 && (!h || !b_dec)) return lithe::fail_arg("h and b_dec must be non-NULL");
-    return lithe::sgmv_index_impl(x, h, 1, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out, rank, lut,
-                                  scaling, err_flag, nullptr, 0, stream, h, b_dec);
+    if (batch > 0 && m > 0 && !h && !b_dec) return lithe::fail_arg("h and b_dec are both NULL");
+    return lithe::sgmv_index_impl(x, h ? h : b_dec, 1, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
+                                  rank, lut, scaling, err_flag, nullptr, 0, stream, h, b_dec, true);
 }
 
 extern "C" int64_t lithe_sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out) {

@@ -260,17 +260,21 @@ def lora_gemm_(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tenso
 
 
 def lora_prep_(x: torch.Tensor, *, view_a: _lib.IndexView, view_b: _lib.IndexView, n_slots: int, ids: torch.Tensor,
-               weights: Optional[torch.Tensor], d_out: int, lut: np.ndarray, scaling: float, h: torch.Tensor,
-               b_dec: torch.Tensor, err: Optional[torch.Tensor] = None) -> None:
-    """lithe_lora_prep: h (B*M, 16) and b_dec (B, d_out, 16), bf16, for lithe_lora_gemm's fused expand."""
+               weights: Optional[torch.Tensor], d_out: int, lut: np.ndarray, scaling: float,
+               h: Optional[torch.Tensor], b_dec: Optional[torch.Tensor], err: Optional[torch.Tensor] = None) -> None:
+    """lithe_lora_prep: h (B*M, 16) and b_dec (B, d_out, 16), bf16, for lithe_lora_gemm's fused expand.
+    Either may be None to skip its half (not both)."""
     _require_cuda(x, "x")
     if x.dtype != torch.bfloat16 or x.dim() != 3 or not x.is_contiguous():
         raise ValueError("x must be a contiguous (B, M, d_in) bfloat16 tensor")
     bsz, m, d_in = x.shape
-    if h.dtype != torch.bfloat16 or h.numel() != bsz * m * 16 or not h.is_contiguous() or h.device != x.device:
+    if h is None and b_dec is None:
+        raise ValueError("h and b_dec are both None")
+    if h is not None and (h.dtype != torch.bfloat16 or h.numel() != bsz * m * 16 or not h.is_contiguous()
+                          or h.device != x.device):
         raise ValueError("h must be a contiguous (B*M, 16) bfloat16 tensor on x's device")
-    if b_dec.dtype != torch.bfloat16 or b_dec.numel() != bsz * d_out * 16 or not b_dec.is_contiguous() \
-            or b_dec.device != x.device:
+    if b_dec is not None and (b_dec.dtype != torch.bfloat16 or b_dec.numel() != bsz * d_out * 16
+                              or not b_dec.is_contiguous() or b_dec.device != x.device):
         raise ValueError("b_dec must be a contiguous (B, d_out, 16) bfloat16 tensor on x's device")
     if ids.dtype != torch.int32 or ids.numel() != bsz or ids.device != x.device or not ids.is_contiguous():
         raise ValueError("ids must be a contiguous (B,) int32 tensor on x's device")
@@ -280,7 +284,8 @@ def lora_prep_(x: torch.Tensor, *, view_a: _lib.IndexView, view_b: _lib.IndexVie
         rc = _lib.lib().lithe_lora_prep(
             x.data_ptr(), ctypes.byref(view_a), ctypes.byref(view_b), int(n_slots), ids.data_ptr(),
             weights.data_ptr() if weights is not None else None, bsz, m, d_in, int(d_out), 16, lut_array(lut),
-            float(scaling), h.data_ptr(), b_dec.data_ptr(), err.data_ptr(), stream_handle(x.device))
+            float(scaling), h.data_ptr() if h is not None else None, b_dec.data_ptr() if b_dec is not None else None,
+            err.data_ptr(), stream_handle(x.device))
     _lib.check(rc, "lithe_lora_prep")
 
 

@@ -132,6 +132,27 @@ class PackedLoRALinear(nn.Module):
                                     weights=self.weights, rows=self.rows)
         return out
 
+    def _h_key(self, x3, ids, w):
+        """(tensors compared by identity, values compared by equality)."""
+        return (x3, ids, w), (x3._version, ids._version, None if w is None else w._version, self.scaling)
+
+    def _shared_h(self, x3, ids, w) -> Optional[torch.Tensor]:
+        """The h a sibling split target computed for the same input, routing and scale, if any.
+        The entry holds the tensors themselves, so a hit needs the very same (unmodified) objects."""
+        entry = getattr(self.bank, "_shared_h", {}).get(self.name)
+        if entry is None:
+            return None
+        (objs, vals), h = entry
+        mine_objs, mine_vals = self._h_key(x3, ids, w)
+        if all(a is b for a, b in zip(objs, mine_objs)) and vals == mine_vals:
+            return h
+        return None
+
+    def _store_h(self, x3, ids, w, h) -> None:
+        if not hasattr(self.bank, "_shared_h"):
+            self.bank._shared_h = {}
+        self.bank._shared_h[self.name] = (self._h_key(x3, ids, w), h)      # one entry per fused module
+
     def _forward_fused_gemm(self, x: torch.Tensor, x3: torch.Tensor) -> torch.Tensor:
         bsz, m, d_in = x3.shape
         d_out = self.base.out_features
@@ -144,10 +165,17 @@ class PackedLoRALinear(nn.Module):
         if self._views is None or self._views[0] != key:
             self._views = (key, self.bank.views(self.name, self.rows))
         va, vb = self._views[1]
-        h = torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device)
+        # Split targets of one fused module (Kohya q/k/v, q/k/v/proj_mlp) share its A factor and are
+        # called with the same input, so h = x . A^T is computed once and reused by the others.
+        h = self._shared_h(x3, ids, w) if self.rows is not None else None
+        fresh = h is None
+        if fresh:
+            h = torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device)
         b_dec = torch.empty(bsz, d_out, 16, dtype=torch.bfloat16, device=x.device)
         _launch.lora_prep_(x3, view_a=va, view_b=vb, n_slots=self.bank.n_slots, ids=ids, weights=w, d_out=d_out,
-                           lut=self.bank.lut, scaling=self.scaling, h=h, b_dec=b_dec)
+                           lut=self.bank.lut, scaling=self.scaling, h=h if fresh else None, b_dec=b_dec)
+        if fresh and self.rows is not None:
+            self._store_h(x3, ids, w, h)
         out = torch.empty(bsz * m, d_out, dtype=torch.bfloat16, device=x.device)
         _launch.lora_gemm_(x3.view(bsz * m, d_in), self.base.weight, self.base.bias, out, h=h, b_dec=b_dec,
                            rows_per_sample=m)

@@ -237,3 +237,51 @@ def test_serve_attach_adapters_fused_gemm_path():
         assert rel_fro(outs[fused].cpu(), truth.cpu()) < 2e-2, fused
     assert rel_fro(outs[True].cpu(), outs[False].cpu()) < 2e-2
     assert device_errors() == 0
+
+
+def test_kohya_split_targets_share_h():
+    """q, k, v of one fused Kohya module share A: called with the same input, the fused-GEMM path
+    computes h once (the first call) and the others reuse it, with bit-identical outputs; an
+    in-place change of the input invalidates the shared h."""
+    mods = kohya.kohya_flux_modules(rank=16, double_blocks=1, single_blocks=1, hidden=256, mlp_ratio=4)
+    ads = [random_adapter([(m["name"], m["shape_a"][1], m["shape_b"][0]) for m in mods], rank=16, seed=s)
+           for s in range(2)]
+    for ad in ads:
+        ad.key_format = "kohya"
+    name = "lora_unet_double_blocks_0_img_attn_qkv"
+    torch.manual_seed(5)
+    bases = [torch.nn.Linear(256, 256).cuda().bfloat16() for _ in range(3)]
+    ids = torch.tensor([1, 0], dtype=torch.int32, device="cuda")
+    x = torch.randn(2, 256, 256, generator=torch.Generator().manual_seed(6)).bfloat16().cuda()
+
+    def run(bank):
+        layers = [PackedLoRALinear(bases[i], bank, name, 16, 1.0, rows=(256 * i, 256 * (i + 1)), fused_gemm=True)
+                  for i in range(3)]
+        for layer in layers:
+            layer.assign = ids
+        with torch.no_grad():
+            return [layer(x) for layer in layers], layers
+
+    shared_bank = PackedBank.from_adapters(ads, "cuda")
+    outs_shared, layers = run(shared_bank)
+    assert set(shared_bank._shared_h) == {name}
+    h0 = shared_bank._shared_h[name][1]
+    assert layers[1]._shared_h(x, ids, None) is h0 and layers[2]._shared_h(x, ids, None) is h0
+    # the same three calls, each computing its own h (no sibling to share with)
+    separate = []
+    for i in range(3):
+        bank = PackedBank.from_adapters(ads, "cuda")
+        layer = PackedLoRALinear(bases[i], bank, name, 16, 1.0, rows=(256 * i, 256 * (i + 1)), fused_gemm=True)
+        layer.assign = ids
+        with torch.no_grad():
+            separate.append(layer(x))
+    for a, b in zip(outs_shared, separate):
+        assert torch.equal(a, b)
+    # an in-place change of x must not reuse the stale h
+    with torch.no_grad():
+        x.mul_(0.5)
+        y = layers[1](x)
+    assert shared_bank._shared_h[name][1] is not h0
+    # everything but the bias is linear in x: y(x / 2) = (y(x) - b) / 2 + b
+    check(y.view(-1, 256), (0.5 * outs_shared[1].float()).view(-1, 256) + 0.5 * bases[1].bias.float())
+    assert device_errors() == 0
