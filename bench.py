@@ -530,10 +530,13 @@ def run_decode(args):
 
 
 # --------------------------------------------------------------------------------------- denoise workloads
-DENOISE = {  # workload -> (image tokens, text tokens, batch, steps)
-    "denoise_512": (1024, 512, 14, 16),        # config 3: 512^2, B=14, 16 steps
-    "denoise_256_b96": (256, 512, 96, 4),      # config 4: 256^2, B=96 distinct adapters, 4 steps
-    "denoise_1024": (4096, 512, 14, 28),       # config 5: 1024^2, B=14, 28 steps
+DENOISE = {  # workload -> (image tokens, text tokens, batch, steps, adapter key format)
+    "denoise_512": (1024, 512, 14, 16, "diffusers"),        # config 3: 512^2, B=14, 16 steps
+    "denoise_256_b96": (256, 512, 96, 4, "diffusers"),      # config 4: 256^2, B=96 distinct adapters, 4 steps
+    "denoise_1024": (4096, 512, 14, 28, "diffusers"),       # config 5: 1024^2, B=14, 28 steps
+    # the released adapters' layout: Kohya-304, served on all 494 diffusers linears
+    "denoise_512_kohya": (1024, 512, 14, 16, "kohya"),
+    "denoise_1024_kohya": (4096, 512, 14, 28, "kohya"),
 }
 
 
@@ -547,7 +550,7 @@ def run_denoise(args):
                                     wrap_linears)
     from lithe_b200.shard import shard_bounds
 
-    img_tok, txt_tok, batch, steps = DENOISE[args.workload]
+    img_tok, txt_tok, batch, steps, key_format = DENOISE[args.workload]
     world, rank, local = dist_env()
     if args.impl == "reference":
         if rank == 0:
@@ -559,9 +562,15 @@ def run_denoise(args):
     dev = torch.device("cuda", local)
     torch.manual_seed(0)
     model = FluxShapedTransformer().to(device=dev, dtype=torch.bfloat16).eval()
-    targets = lora_targets(model)
-    layout = PackedLayout.from_modules([{"name": n, "shape_a": [RANK, m.in_features], "shape_b": [m.out_features, RANK]}
-                                        for n, m in targets])
+    if key_format == "kohya":
+        from lithe_b200 import kohya
+        layout = PackedLayout.from_modules(kohya.kohya_flux_modules(rank=RANK))
+        split = kohya.split_targets(layout.names, layout.shapes_a, layout.shapes_b, "kohya")
+        targets = [(path, model.get_submodule(path)) for path in split]
+    else:
+        targets = lora_targets(model)
+        layout = PackedLayout.from_modules([{"name": n, "shape_a": [RANK, m.in_features],
+                                             "shape_b": [m.out_features, RANK]} for n, m in targets])
     bank = PackedBank(layout, BANK_SLOTS, dev)
     bank.fill_random(seed=1234)
     lo, hi = shard_bounds(batch, world, rank) if args.shard_batch else (0, batch)
@@ -574,12 +583,21 @@ def run_denoise(args):
     pooled = torch.randn(batch, 768, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous()
     names = [n for n, _ in targets]
     bases = {n: m for n, m in targets}
-    packed = {n: PackedLoRALinear(bases[n], bank, n, RANK, 1.0) for n in names}
+    if key_format == "kohya":
+        def _packed(path):
+            name, r0, r1 = split[path]
+            full = r0 == 0 and r1 == layout.shapes_b[layout.index(name)][0]
+            return PackedLoRALinear(bases[path], bank, name, RANK, 1.0, rows=None if full else (r0, r1))
+        packed = {n: _packed(n) for n in names}
+    else:
+        packed = {n: PackedLoRALinear(bases[n], bank, n, RANK, 1.0) for n in names}
     ids = slots.to(torch.int32).to(dev)
     for m in packed.values():
         m.assign = ids
     dec = bank.decode(ids, dtype=torch.bfloat16)                   # the dense comparator's resident factors
     per = [split_decoded(dec[i], layout) for i in range(nb)]
+    if key_format == "kohya":
+        per = [kohya.split_factors(p_) for p_ in per]
     dense = {}
     for n in names:
         d = PerSampleLoRALinear(bases[n], "sgmv")
@@ -629,6 +647,8 @@ def run_denoise(args):
             "data": "synthetic: random-init FLUX.1-dev-shaped transformer, seeded uniform 9-bit packed adapters",
             "config": {"workload": args.workload, "image_tokens": img_tok, "text_tokens": txt_tok, "batch": batch,
                        "rank_batch": nb, "lora_linears": len(names), "bank_slots": BANK_SLOTS,
+                       "adapter_format": key_format + ("-304 (all 494 linears; fused q/k/v share h)"
+                                                       if key_format == "kohya" else "-342"),
                        "parallelism": (f"B={batch} split by sample over {world} ranks" if args.shard_batch
                                        else f"dp{world}: every rank its own B={batch}") + ", bank replicated"},
             "base_only_s": t_base, "lithe_s": t_lithe, "dense_resident_lora_s": t_dense,
@@ -895,6 +915,8 @@ LORA_GEMM_SHAPES = [  # (tag, tokens per sample, d_in, d_out, linears per forwar
     ("img_sq", 4096, 3072, 3072, 76), ("img_up", 4096, 3072, 12288, 19), ("img_dn", 4096, 12288, 3072, 19),
     ("txt_sq", 512, 3072, 3072, 76), ("txt_up", 512, 3072, 12288, 19), ("txt_dn", 512, 12288, 3072, 19),
     ("single_sq", 4608, 3072, 3072, 114)]
+# the extra targets of the Kohya-304 layout (single blocks' proj_mlp and proj_out); run only when named by --shapes
+LORA_GEMM_KOHYA_SHAPES = [("single_mlp", 4608, 3072, 12288, 38), ("single_out", 4608, 15360, 3072, 38)]
 
 
 def run_lora_gemm(args):
@@ -921,8 +943,9 @@ def run_lora_gemm(args):
     gen = torch.Generator(device=dev)
     gen.manual_seed(11 + rank)
     err = _lk.error_word(dev)
-    for tag, m, d_in, d_out, count in LORA_GEMM_SHAPES:
-        if args.shapes and tag not in args.shapes.split(","):
+    named = args.shapes.split(",") if args.shapes else None
+    for tag, m, d_in, d_out, count in LORA_GEMM_SHAPES + LORA_GEMM_KOHYA_SHAPES:
+        if (named is None and (tag, m, d_in, d_out, count) in LORA_GEMM_KOHYA_SHAPES) or (named and tag not in named):
             continue
         mm = m if not rows_override else max(256, rows_override // batch // 256 * 256)
         lay = PackedLayout.from_modules([{"name": "l", "shape_a": [RANK, d_in], "shape_b": [d_out, RANK]}])
@@ -1010,8 +1033,8 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["lithe", "reference"], default="lithe")
     ap.add_argument("--workload", choices=["flux_sweep_b14", "decode_flux342", "decode_kohya304", "denoise_512",
-                                           "denoise_256_b96", "denoise_1024", "hotswap_kohya304",
-                                           "lora_gemm_flux"],
+                                           "denoise_256_b96", "denoise_1024", "denoise_512_kohya",
+                                           "denoise_1024_kohya", "hotswap_kohya304", "lora_gemm_flux"],
                     default="flux_sweep_b14", help="flux_sweep_b14: fused decode+SGMV (default); decode_*: "
                     "standalone packed decode of 14 resident adapters per launch")
     ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")

@@ -658,6 +658,169 @@ static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, co
     return LITHE_OK;
 }
 
+// ---------------------------------------------------------------------------------------
+// Small-m form: at most kSmallM token rows per sample (one decode step of a serving batch,
+// or the per-sample modulation linears of a diffusion transformer).  A 64-token work unit
+// of the persistent kernel would stream 64-row tiles for one live row and keep one CTA per
+// sample busy through every chunk, so here the output columns are split over CTAs instead:
+//   grid (n_split, batch); CTA (s, b) first forms h[i][r] = sum_k x[b,i,k] A[r,k] for all
+//   rows of its sample (the A side is tiny and L2-resident, so every CTA of the sample
+//   recomputes it), then adds scale * h . B^T to its share of the B blocks.
+// Shrink: thread t owns rank row r = t % kRank and the 64-column chunks c = t / kRank + j *
+// (256 / kRank); since A[r, 64c + u + 16q] = a_{r,c}[u], it folds the four 16-column quarters
+// of each x chunk before the 16-term dot.  The partial sums are added in a fixed order
+// (deterministic).  Decoded values are rounded to bf16 and h * scale to bf16, as in the
+// tensor-core form; the expand and the add to out run in fp32.
+// Expand: thread t owns B block G (64 values = 64/kRank output rows o, B[o, r] =
+// v[(kRank*(o % (64/kRank)) + r) & 15]) and writes its rows for every token row of the sample.
+// ---------------------------------------------------------------------------------------
+constexpr int kSmallM = 8;
+constexpr int kSmallThreads = 256;
+
+__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+
+__device__ __forceinline__ void decode_block16(const float* lut_side, const uint32_t* k, int levels, float v[16]) {
+    decode_eight<LITHE_MAX_LEVELS>(lut_side, k, levels, 0, v);
+    decode_eight<LITHE_MAX_LEVELS>(lut_side, k, levels, 1, v + 8);
+#pragma unroll
+    for (int u = 0; u < 16; ++u) v[u] = bf16_round(v[u]);
+}
+
+template <int kRank, int kM>
+__global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const __nv_bfloat16* __restrict__ x,
+                                                                   const __grid_constant__ SgmvParams p) {
+    constexpr int kCols = kSmallThreads / kRank;   // chunk stride of the shrink
+    constexpr int kRowsPerBlock = 64 / kRank;      // output rows of one B block
+    __shared__ float lut_s[kLutFloats];
+    __shared__ float part_s[kM][kSmallThreads];
+    __shared__ float h_s[kM][kRank];
+    const int tid = threadIdx.x;
+    const int b = blockIdx.y;
+    const int m = p.m;
+    const int32_t sid = __ldg(p.ids + b);
+    const bool active = sid >= 0 && static_cast<int64_t>(sid) < p.n_slots;
+    if (!active) {
+        if (sid >= 0 && blockIdx.x == 0 && tid == 0 && p.err) atomicOr(p.err, LITHE_DEVERR_SLOT);
+        if (p.accumulate) return;               // unrouted sample: out unchanged
+    }
+    for (int i = tid; i < kLutFloats; i += kSmallThreads) lut_s[i] = (&p.lut[0][0][0])[i];
+    __syncthreads();
+
+    // ---- shrink
+    float acc[kM];
+#pragma unroll
+    for (int i = 0; i < kM; ++i) acc[i] = 0.f;
+    const int r = tid % kRank;
+    if (active) {
+        for (int c = tid / kRank; c < p.n_xchunks; c += kCols) {
+            uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
+            fetch_indices<LITHE_MAX_LEVELS>(p.ia, sid, static_cast<int64_t>(r) * p.a_blocks_per_row + c, k, p.err);
+            float a[16];
+            decode_block16(lut_s, k, p.ia.levels, a);
+#pragma unroll
+            for (int i = 0; i < kM; ++i) {
+                if (i < m) {
+                    const uint4* xr = reinterpret_cast<const uint4*>(x + (static_cast<int64_t>(b) * m + i) * p.d_in +
+                                                                     static_cast<int64_t>(kChunk) * c);
+                    float f[16];
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) f[u] = 0.f;
+#pragma unroll
+                    for (int q = 0; q < 8; ++q) {        // 8 bf16 at columns 8q .. 8q + 7, u = 8 (q & 1) + j
+                        const uint4 w = __ldg(xr + q);
+                        const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
+#pragma unroll
+                        for (int j = 0; j < 4; ++j) {
+                            f[8 * (q & 1) + 2 * j] += bf16lo_to_f32(ww[j]);
+                            f[8 * (q & 1) + 2 * j + 1] += bf16hi_to_f32(ww[j]);
+                        }
+                    }
+                    float s = 0.f;
+#pragma unroll
+                    for (int u = 0; u < 16; ++u) s = fmaf(a[u], f[u], s);
+                    acc[i] += s;
+                }
+            }
+        }
+    }
+#pragma unroll
+    for (int i = 0; i < kM; ++i) part_s[i][tid] = acc[i];
+    __syncthreads();
+    if (tid < kM * kRank) {
+        const int i = tid / kRank, rr = tid % kRank;
+        float s = 0.f;
+        for (int c0 = 0; c0 < kCols; ++c0) s += part_s[i][rr + kRank * c0];
+        const float sc = p.scaling * (p.weights ? __ldg(p.weights + b) : 1.0f);
+        h_s[i][rr] = active ? bf16_round(s * sc) : 0.f;
+    }
+    __syncthreads();
+
+    // ---- expand
+    const float* lut_b = lut_s + LITHE_MAX_LEVELS * 16;
+    for (int64_t G = static_cast<int64_t>(blockIdx.x) * kSmallThreads + tid; G < p.b_blocks;
+         G += static_cast<int64_t>(gridDim.x) * kSmallThreads) {
+        float v[16];
+        if (active) {
+            uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
+            fetch_indices<LITHE_MAX_LEVELS>(p.ib, sid, G, k, p.err);
+            decode_block16(lut_b, k, p.ia.levels, v);
+        } else {
+#pragma unroll
+            for (int u = 0; u < 16; ++u) v[u] = 0.f;
+        }
+#pragma unroll
+        for (int i = 0; i < kM; ++i) {
+            if (i < m) {
+                __nv_bfloat16* orow = p.out + (static_cast<int64_t>(b) * m + i) * p.d_out + G * kRowsPerBlock;
+#pragma unroll
+                for (int q0 = 0; q0 < kRowsPerBlock; q0 += 4) {   // 4 output rows = one 8-byte access
+                    float d[4];
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        float s = 0.f;
+#pragma unroll
+                        for (int rr = 0; rr < kRank; ++rr) s = fmaf(h_s[i][rr], v[(kRank * (q0 + e) + rr) & 15], s);
+                        d[e] = s;
+                    }
+                    uint2* dst = reinterpret_cast<uint2*>(orow + q0);
+                    uint2 o = make_uint2(0u, 0u);
+                    if (p.accumulate) o = *dst;
+                    *dst = make_uint2(add_bf16x2(o.x, d[0], d[1]), add_bf16x2(o.y, d[2], d[3]));
+                }
+            }
+        }
+    }
+}
+
+template <int kRank>
+static int32_t launch_small_rank(const __nv_bfloat16* x, const SgmvParams& p, int32_t batch, int sms,
+                                 cudaStream_t stream) {
+    // one B block per thread, but no more CTAs per sample than fill ~2 waves of the SMs
+    const int64_t per_sample = (static_cast<int64_t>(p.b_blocks) + kSmallThreads - 1) / kSmallThreads;
+    const int64_t fill = (2LL * sms + batch - 1) / batch;
+    const int64_t split = per_sample < fill ? per_sample : (fill < 1 ? 1 : fill);
+    const dim3 grid(static_cast<unsigned>(split), static_cast<unsigned>(batch));
+    if (p.m <= 1) sgmv_small_kernel<kRank, 1><<<grid, kSmallThreads, 0, stream>>>(x, p);
+    else if (p.m <= 2) sgmv_small_kernel<kRank, 2><<<grid, kSmallThreads, 0, stream>>>(x, p);
+    else if (p.m <= 4) sgmv_small_kernel<kRank, 4><<<grid, kSmallThreads, 0, stream>>>(x, p);
+    else sgmv_small_kernel<kRank, kSmallM><<<grid, kSmallThreads, 0, stream>>>(x, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "sgmv_small_kernel launch");
+    return LITHE_OK;
+}
+
+static int32_t launch_small(const __nv_bfloat16* x, const SgmvParams& p, int32_t rank, int32_t batch, int sms,
+                            cudaStream_t stream) {
+    if (batch > 65535) return fail_unsupported("the small-m form takes at most 65535 samples, got %d", batch);
+    switch (rank) {
+        case 16: return launch_small_rank<16>(x, p, batch, sms, stream);
+        case 8: return launch_small_rank<8>(x, p, batch, sms, stream);
+        case 4: return launch_small_rank<4>(x, p, batch, sms, stream);
+        case 2: return launch_small_rank<2>(x, p, batch, sms, stream);
+        default: return launch_small_rank<1>(x, p, batch, sms, stream);
+    }
+}
+
 static int32_t check_view(const lithe_index_view* v, const char* name) {
     if (!v) return fail_arg("%s is NULL", name);
     if (!v->base) return fail_arg("%s.base is NULL", name);
@@ -738,20 +901,6 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     rc = current_device_sms(&device, &sms);
     if (rc != LITHE_OK) return rc;
 
-    CUtensorMap tmx, tmo_ld;
-    // Tensor maps over the flattened (batch * m) rows: measured on B200, a (d, m, batch) map
-    // with a (64, 64, 1) box streams about 15% slower than a 2-D map over the same rows.  The
-    // last tile of a sample may then read the next sample's first rows; those rows are never
-    // stored (stores are bounded by the sample's own m), and rows past the tensor read zeros.
-    rc = encode_bf16_3d(&tmx, x, d_in, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
-    if (rc != LITHE_OK) return rc;
-    if (prep) {
-        tmo_ld = tmx;                 // no out tiles in shrink-only mode
-    } else {
-        rc = encode_bf16_3d(&tmo_ld, out, d_out, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
-        if (rc != LITHE_OK) return rc;
-    }
-
     SgmvParams p{};
     p.ia = to_view(idx_a);
     p.ib = to_view(idx_b);
@@ -776,6 +925,31 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     p.n_chunks = p.n_xchunks + p.n_ochunks;
     p.ws = static_cast<const uint8_t*>(ws);
     p.h_out = nullptr;
+    if (ws && !prep) {
+        if (reinterpret_cast<uintptr_t>(ws) % 16) return fail_arg("workspace must be 16-byte aligned");
+        const int64_t need = sgmv_workspace_bytes(batch, d_in, d_out);
+        if (ws_bytes < need)
+            return fail_arg("workspace holds %lld bytes, this call needs %lld", (long long)ws_bytes, (long long)need);
+    }
+    // A few token rows per sample (decode-time serving, modulation linears): the small-m form,
+    // in every entry point (it needs no workspace, so the staged and fused modes agree).
+    if (!prep && m <= kSmallM) return launch_small(static_cast<const __nv_bfloat16*>(x), p, rank, batch, sms,
+                                                          static_cast<cudaStream_t>(stream));
+
+    CUtensorMap tmx, tmo_ld;
+    // Tensor maps over the flattened (batch * m) rows: measured on B200, a (d, m, batch) map
+    // with a (64, 64, 1) box streams about 15% slower than a 2-D map over the same rows.  The
+    // last tile of a sample may then read the next sample's first rows; those rows are never
+    // stored (stores are bounded by the sample's own m), and rows past the tensor read zeros.
+    rc = encode_bf16_3d(&tmx, x, d_in, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
+    if (rc != LITHE_OK) return rc;
+    if (prep) {
+        tmo_ld = tmx;                 // no out tiles in shrink-only mode
+    } else {
+        rc = encode_bf16_3d(&tmo_ld, out, d_out, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
+        if (rc != LITHE_OK) return rc;
+    }
+
     if (prep) {
         cudaStream_t s = static_cast<cudaStream_t>(stream);
         // B side first: every sample's decoded factor, (batch, d_out, 16)
@@ -796,12 +970,6 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
         p.n_chunks = p.n_xchunks;
         p.out = nullptr;
         ws = nullptr;
-    }
-    if (ws) {
-        if (reinterpret_cast<uintptr_t>(ws) % 16) return fail_arg("workspace must be 16-byte aligned");
-        const int64_t need = sgmv_workspace_bytes(batch, d_in, d_out);
-        if (ws_bytes < need)
-            return fail_arg("workspace holds %lld bytes, this call needs %lld", (long long)ws_bytes, (long long)need);
     }
 
     const int grid = static_cast<int>(p.total_units < sms ? p.total_units : sms);

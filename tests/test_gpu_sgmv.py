@@ -340,3 +340,66 @@ def test_staged_mode_workspace_checks():
                                         ids.data_ptr(), None, 2, 8, 256, 256, 16, _launch.lut_array(cb.kernel_lut(*cb.twin_pools())),
                                         1.0, None, small.data_ptr(), small.numel(), None)
     assert rc == _lib.ERR_ARG and b"workspace" in _lib.lib().lithe_last_error()
+
+
+# m <= 8 token rows per sample run the small-m form (output columns split over CTAs, h formed
+# per CTA); the same tolerance and exact properties as the tensor-core form.
+SMALL_CASES = [(1, 3072, 18432, 16), (1, 3072, 9216, 16), (1, 256, 384, 4), (2, 512, 640, 8), (3, 192, 256, 2),
+               (5, 256, 128, 1), (8, 1024, 4096, 16), (7, 15360, 3072, 16)]
+
+
+@pytest.mark.parametrize("seq,d_in,d_out,r", SMALL_CASES)
+@pytest.mark.parametrize("fmt", ["packed", "i16", "i32"])
+def test_small_m_form_matches_truth(seq, d_in, d_out, r, fmt):
+    ads = [random_adapter([("l", d_in, d_out)], rank=r, seed=s + 40) for s in range(3)]
+    x = (torch.randn(14, seq, d_in, generator=torch.Generator().manual_seed(seq * 7 + d_in)) * 0.5).bfloat16().cuda()
+    assign = [i % 3 for i in range(14)]
+    got = run_fused(x, ads, assign, fmt).float().cpu()
+    want = truth_delta(x, ads, assign)
+    assert max_abs_rel(got, want) <= MAX_ABS_REL and rel_fro(got, want) < REL_FRO
+    assert device_errors() == 0
+
+
+def test_small_m_routing_accumulate_and_exact_properties():
+    ads = [random_adapter([("l", 512, 768)], rank=16, seed=s + 50) for s in range(2)]
+    x = torch.randn(6, 3, 512, generator=torch.Generator().manual_seed(51)).bfloat16().cuda()
+    base = (torch.randn(6, 3, 768, generator=torch.Generator().manual_seed(52)) * 0.05).bfloat16().cuda()
+    assign = [0, -1, 5, 1, 1, 0]
+    weights = [1.0, 1.0, 1.0, 0.5, 0.0, 2.0]
+    device_errors()
+    acc = run_fused(x, ads, assign, accumulate=True, out=base.clone(), weights=weights, scaling=0.75)
+    assert device_errors() == 1                                    # slot 5 >= n_slots reported
+    for b in (1, 2, 4):                                            # unrouted, invalid, weight 0: untouched
+        assert torch.equal(acc[b], base[b])
+    routed = [0, -1, -1, 1, 1, 0]
+    truth = truth_delta(x, ads, routed, weights=weights, scaling=0.75)
+    want = base.float().cpu() + truth
+    tol = 2 ** -8 * want.abs() + MAX_ABS_REL * truth.abs().max()
+    assert bool(((acc.float().cpu() - want).abs() <= tol).all())
+    delta = run_fused(x, ads, assign, weights=weights, scaling=0.75)
+    device_errors()
+    assert bool((delta[1] == 0).all()) and bool((delta[2] == 0).all()) and bool((delta[4] == 0).all())
+    assert max_abs_rel(delta.float().cpu(), truth) <= MAX_ABS_REL
+    # exact: doubling, batch independence, index formats, staged == fused
+    d1 = run_fused(x, ads, routed)
+    assert torch.equal(run_fused(x * 2, ads, routed), d1 * 2)
+    assert torch.equal(run_fused(x[3:4].contiguous(), ads, [routed[3]])[0], d1[3])
+    assert torch.equal(run_fused(x, ads, routed, fmt="i16"), d1)
+    assert torch.equal(run_fused(x, ads, routed, mode="staged"), d1)
+    assert device_errors() == 0
+
+
+def test_small_m_layers_and_serve():
+    """One decode token per request through IndexLoRALinear-style packed layers and the router."""
+    ads = [random_adapter([("l", 1024, 3072)], rank=16, seed=s + 60) for s in range(4)]
+    bank = PackedBank.from_adapters(ads, "cuda")
+    base = torch.nn.Linear(1024, 3072).cuda().bfloat16()
+    layer = PackedLoRALinear(base, bank, "l", 16, 1.0)
+    layer.assign = torch.tensor([3, 1, 0, 2, 1], dtype=torch.int32, device="cuda")
+    x = torch.randn(5, 1024, generator=torch.Generator().manual_seed(61)).bfloat16().cuda()   # (batch, d_in)
+    with torch.no_grad():
+        y = layer(x).float().cpu()
+    truth = truth_delta(x.unsqueeze(1), ads, [3, 1, 0, 2, 1])[:, 0]
+    want = x.float().cpu() @ base.weight.float().cpu().T + base.bias.float().cpu() + truth
+    assert max_abs_rel(y, want) <= MAX_ABS_REL
+    assert device_errors() == 0
