@@ -541,11 +541,15 @@ DENOISE = {  # workload -> (image tokens, text tokens, batch, steps, adapter key
 
 
 def run_denoise(args):
-    """Full denoise loop on a random-init FLUX.1-dev-shaped transformer (bf16), three ways:
-    base only, index-resident LoRA (fused kernel on every one of the 342 target linears, 9-bit
-    packed 10,000-slot bank), and a dense resident-LoRA comparator (decoded bf16 factors of the
-    batch's adapters resident in HBM, two cuBLAS bmm + in-place add per linear)."""
+    """Full denoise loop on a random-init FLUX.1-dev-shaped transformer (bf16), five ways: base
+    only (cuBLAS), the base on lithe_lora_gemm without LoRA (diagnostic), index-resident LoRA
+    on every target linear from a 9-bit packed 10,000-slot bank -- cuBLAS + the fused
+    decode/SGMV kernel, and lithe_lora_prep + lithe_lora_gemm with the expand inside the GEMM --
+    and a dense resident-LoRA comparator (decoded bf16 factors of the batch's adapters resident
+    in HBM, cuBLAS bmm + in-place baddbmm per linear).  Targets: the 342 diffusers linears, or
+    the 494 linears a Kohya-304 adapter covers (its fused q/k/v modules served in place)."""
     from lithe_b200.flux_model import FluxShapedTransformer, denoise, lora_targets
+    from lithe_b200.kernels.layers import FUSED_GEMM_MAX_K
     from lithe_b200.kernels import (PackedBank, PackedLayout, PackedLoRALinear, PerSampleLoRALinear, split_decoded,
                                     wrap_linears)
     from lithe_b200.shard import shard_bounds
@@ -606,17 +610,40 @@ def run_denoise(args):
         dense[n] = d
     del dec, per
 
+    class _PlainGemm(torch.nn.Module):
+        """The base linear on lithe_lora_gemm without a LoRA term, on the linears where the fused
+        path uses it (the rest stay on cuBLAS): separates the GEMM's own cost from the LoRA work."""
+
+        def __init__(self, lin, gate):
+            super().__init__()
+            self.lin, self.gate = lin, gate
+
+        def forward(self, x):
+            x3 = x.unsqueeze(1) if x.dim() == 2 else x
+            if not self.gate._gemm_ok(x3):
+                return self.lin(x)
+            x2 = x3.contiguous().view(-1, x3.shape[-1])
+            out = torch.empty(x2.shape[0], self.lin.out_features, dtype=x.dtype, device=x.device)
+            _launch_k.lora_gemm_(x2, self.lin.weight, self.lin.bias, out)
+            return out.view(*x.shape[:-1], self.lin.out_features)
+
+    from lithe_b200.kernels import _launch as _launch_k
+    plain = {n: _PlainGemm(bases[n], packed[n]) for n in names}
+
     def install(kind):
-        table = {"base": bases, "lithe": packed, "lithe_fused": packed, "dense": dense}[kind]
+        table = {"base": bases, "plain_gemm": plain, "lithe": packed, "lithe_fused": packed, "lithe_fused_all": packed,
+                 "dense": dense}[kind]
         for m in packed.values():
-            m.fused_gemm = kind == "lithe_fused"
+            m.fused_gemm = kind.startswith("lithe_fused")
+            # lithe_fused: the default policy (in_features <= FUSED_GEMM_MAX_K); _all: every eligible linear
+            m.fused_gemm_max_k = None if kind in ("lithe_fused_all", "plain_gemm") else FUSED_GEMM_MAX_K
         wrap_linears_any(model, names, table)
 
     stream = torch.cuda.current_stream(dev)
     # ABBA order: the GPU runs under its power cap and its clocks drift as it heats up, so each
     # variant is timed once on the way out and once on the way back and the two are averaged
     # (a linear drift cancels); both passes are reported.
-    kinds = ("base", "lithe", "lithe_fused", "dense")
+    kinds = ("base", "plain_gemm", "lithe", "lithe_fused", "lithe_fused_all", "dense")
     runs = {k: [] for k in kinds}
     clock_log = {k: [] for k in kinds}
     with torch.no_grad():
@@ -642,7 +669,8 @@ def run_denoise(args):
             "metric": f"{steps}-step denoise wall time", "value": t_fused, "unit": "s", "n_gpus": world, "steps": steps,
             "warmup": 1, "ms_per_step": 1000.0 * t_fused / steps, "higher_is_better": False,
             "lora_path": "PackedLoRALinear(fused_gemm=True): lithe_lora_prep + lithe_lora_gemm (expand inside the "
-                         "tcgen05 base GEMM); lithe_s is the cuBLAS + fused decode/SGMV path",
+                         "tcgen05 base GEMM) on linears with in_features <= 4096, cuBLAS + the fused decode/SGMV "
+                         "kernel on the rest; lithe_s is cuBLAS + decode/SGMV everywhere",
             "scaling": "strong" if args.shard_batch else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: random-init FLUX.1-dev-shaped transformer, seeded uniform 9-bit packed adapters",
             "config": {"workload": args.workload, "image_tokens": img_tok, "text_tokens": txt_tok, "batch": batch,
@@ -657,6 +685,10 @@ def run_denoise(args):
             "lithe_fused_gemm_s": t_fused, "lithe_fused_gemm_lora_overhead_s": t_fused - t_base,
             "overhead_ratio_fused_gemm_vs_dense": (t_fused - t_base) / max(1e-9, t_dense - t_base),
             "clocks_fused_gemm": results["lithe_fused"][1],
+            "plain_gemm_base_s": results["plain_gemm"][0],
+            "lithe_fused_all_s": results["lithe_fused_all"][0],
+            "overhead_ratio_fused_all_vs_dense": (results["lithe_fused_all"][0] - t_base) / max(1e-9, t_dense - t_base),
+            "fused_all_lora_cost_over_plain_gemm_s": results["lithe_fused_all"][0] - results["plain_gemm"][0],
             "passes_s": runs, "order": "ABBA: " + " ".join(kinds + tuple(reversed(kinds))),
             "clocks": results["lithe"][1], "gpu_launches": steps * len(names)}), flush=True)
     if world > 1:

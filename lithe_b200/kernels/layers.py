@@ -73,6 +73,16 @@ class IndexLoRALinear(nn.Module):
         return out
 
 
+# The fused-GEMM path saves the output's read-modify-write (4 bytes per output element) but
+# runs the base product on lithe_lora_gemm instead of cuBLAS.  Measured in a sustained 28-step
+# 1024^2 B=14 FLUX denoise on B200 (power-capped), that GEMM costs more energy per FLOP than
+# cuBLAS's, so the trade pays where in_features is small relative to the output: with the
+# fused path limited to in_features <= 4096, the 494-linear Kohya-304 run took 38.36 s against
+# 39.38 s with it on every eligible linear (the ff.net.2 / proj_out linears, in_features 12288
+# and 15360, back on cuBLAS + the decode/SGMV kernel).
+FUSED_GEMM_MAX_K = 4096
+
+
 class PackedLoRALinear(nn.Module):
     """y = W x + per-sample delta from module ``name`` of a shared packed bank.
 
@@ -107,6 +117,9 @@ class PackedLoRALinear(nn.Module):
         # the fused decode/SGMV kernel's read-modify-write of the output.  The base product is
         # then ours, not cuBLAS's (same math, different fp32 summation order).
         self.fused_gemm = bool(fused_gemm)
+        # largest in_features the fused path takes (None: any); larger linears stay on cuBLAS +
+        # the fused decode/SGMV kernel (FUSED_GEMM_MAX_K gives the measured reason)
+        self.fused_gemm_max_k: Optional[int] = FUSED_GEMM_MAX_K
         self._views = None                 # (bank storage key, (view_a, view_b)) of the fused path
 
     def _gemm_ok(self, x3: torch.Tensor) -> bool:
@@ -114,7 +127,8 @@ class PackedLoRALinear(nn.Module):
         b = self.base.bias
         return (self.rank == 16 and w.dtype == torch.bfloat16 and w.is_contiguous() and x3.dtype == torch.bfloat16
                 and (b is None or (b.dtype == torch.bfloat16 and b.is_contiguous()))
-                and w.shape[0] % 256 == 0 and w.shape[1] % 64 == 0 and x3.shape[1] % 128 == 0 and x3.shape[0] > 0)
+                and w.shape[0] % 256 == 0 and w.shape[1] % 64 == 0 and x3.shape[1] % 128 == 0 and x3.shape[0] > 0
+                and (self.fused_gemm_max_k is None or w.shape[1] <= self.fused_gemm_max_k))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         x3 = x.unsqueeze(1) if x.dim() == 2 else x

@@ -22,7 +22,7 @@ from . import codebook as cb
 from . import quant
 from .fileio import LitheAdapter
 from .kernels import _launch
-from .kernels.layers import _inference_only
+from .kernels.layers import FUSED_GEMM_MAX_K, _inference_only
 
 Route = Sequence[Tuple[int, float]]
 
@@ -95,6 +95,7 @@ class MultiAdapterLinear(nn.Module):
         super().__init__()
         self.base = base
         self.fused_gemm = bool(fused_gemm)
+        self.fused_gemm_max_k: Optional[int] = FUSED_GEMM_MAX_K   # larger in_features: cuBLAS + decode/SGMV
         self.router = router
         self.rank = rank
         self.shape_a = (rank, base.in_features)
@@ -123,7 +124,8 @@ class MultiAdapterLinear(nn.Module):
         w, b = self.base.weight, self.base.bias
         return (self.rank == 16 and x3.dtype == torch.bfloat16 and w.dtype == torch.bfloat16 and w.is_contiguous()
                 and (b is None or (b.dtype == torch.bfloat16 and b.is_contiguous()))
-                and w.shape[0] % 256 == 0 and w.shape[1] % 64 == 0 and x3.shape[1] % 128 == 0 and x3.shape[1] > 0)
+                and w.shape[0] % 256 == 0 and w.shape[1] % 64 == 0 and x3.shape[1] % 128 == 0 and x3.shape[1] > 0
+                and (self.fused_gemm_max_k is None or w.shape[1] <= self.fused_gemm_max_k))
 
     def _forward_fused_gemm(self, x: torch.Tensor, xs: torch.Tensor, slot_ids: torch.Tensor,
                             w: torch.Tensor) -> torch.Tensor:
