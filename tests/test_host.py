@@ -178,3 +178,19 @@ def test_flux_shaped_model_targets_342_linears():
     shapes = sorted({(m.in_features, m.out_features) for _, m in targets})
     assert shapes == [(3072, 3072), (3072, 12288), (12288, 3072)]
     assert 11.5e9 < sum(p.numel() for p in model.parameters()) < 12.5e9
+
+
+def test_fused_gemm_in_features_limit():
+    """The fused-GEMM path is taken only up to FUSED_GEMM_MAX_K input features (host-side gate)."""
+    from lithe_b200.kernels import PackedBank, PackedLayout, PackedLoRALinear
+    from lithe_b200.kernels.layers import FUSED_GEMM_MAX_K
+    assert FUSED_GEMM_MAX_K == 4096
+    for d_in, want in ((3072, True), (4096, True), (12288, False)):
+        lay = PackedLayout.from_modules([{"name": "l", "shape_a": [16, d_in], "shape_b": [512, 16]}])
+        bank = PackedBank(lay, 1, "cpu")
+        layer = PackedLoRALinear(torch.nn.Linear(d_in, 512).bfloat16(), bank, "l", 16, 1.0, fused_gemm=True)
+        x3 = torch.zeros(2, 128, d_in, dtype=torch.bfloat16)
+        assert layer._gemm_ok(x3) is want
+        layer.fused_gemm_max_k = None
+        assert layer._gemm_ok(x3)
+        assert not layer._gemm_ok(torch.zeros(2, 100, d_in, dtype=torch.bfloat16))   # tokens per sample % 128
