@@ -99,6 +99,8 @@ LITHE_API const char* lithe_last_error(void);
  *   err_flag device int32 (may be NULL)
  * Requirements: rank in {1,2,4,8,16}; d_in % 64 == 0; d_out % 8 == 0; (d_out*rank) % 64 == 0;
  * x, out 16-byte aligned; idx_a and idx_b with the same num_levels.
+ * m <= 8 (one decode step, per-sample modulation rows) runs a small-m kernel that splits the
+ * output columns over CTAs; same formula and rounding steps, in every sgmv entry point.
  */
 LITHE_API int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate,
                          const lithe_index_view* idx_a, const lithe_index_view* idx_b,
