@@ -3,7 +3,8 @@
 // Replaces the two Triton launches of lithe/kernels/shared.py:36-157 (shrink decodes A
 // tiles and writes y_lo; expand decodes B tiles per M-tile and writes a fresh delta),
 // the separate "delta * scaling" pass (shared.py:261-262) and the caller's "out + delta"
-// pass (lithe/kernels/layers.py:131, lithe/serve.py:97).  One persistent launch per linear:
+// pass (lithe/kernels/layers.py:131, lithe/serve.py:97).  One persistent launch per linear
+// (calls with at most kSmallM token rows per sample take sgmv_small_kernel further down):
 //
 //   work unit  = (sample b, 64-token tile); CTA i owns a contiguous range of units.
 //   per unit   = d_in/64 "x chunks" (64x64 bf16 activation tiles, TMA, 128B swizzle)
