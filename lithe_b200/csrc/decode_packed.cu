@@ -112,8 +112,8 @@ __global__ void __launch_bounds__(256) decode_packed_kernel(const __grid_constan
                 w.y = __shfl_sync(0xffffffffu, q[1], src);
                 w.z = __shfl_sync(0xffffffffu, q[2], src);
                 w.w = __shfl_sync(0xffffffffu, q[3], src);
-                if (blk0 + b < p.n_blocks)
-                    *reinterpret_cast<uint4*>(out + (blk0 + b) * kBlockBytes + (lane & 7) * 16) = w;
+                if (blk0 + b < p.n_blocks)   // streaming store: the output is larger than L2 and not re-read here
+                    __stcs(reinterpret_cast<uint4*>(out + (blk0 + b) * kBlockBytes + (lane & 7) * 16), w);
             }
         }
     }

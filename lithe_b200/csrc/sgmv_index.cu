@@ -439,8 +439,9 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
 #pragma unroll
                         for (int q = 0; q < 2; ++q) {
                             const int col = col0 + 32 * q + 8 * t4;
-                            if (col < p.d_out)
-                                *reinterpret_cast<uint4*>(out_b + static_cast<int64_t>(row) * p.d_out + col) = v[q][hr];
+                            if (col < p.d_out)   // streaming store: out is not re-read by this launch
+                                __stcs(reinterpret_cast<uint4*>(out_b + static_cast<int64_t>(row) * p.d_out + col),
+                                       v[q][hr]);
                         }
                     }
                 }
