@@ -610,6 +610,8 @@ def run_denoise(args):
         dense[n] = d
     del dec, per
 
+    from lithe_b200.kernels import _launch as _launch_k
+
     class _PlainGemm(torch.nn.Module):
         """The base linear on lithe_lora_gemm without a LoRA term, on the linears where the fused
         path uses it (the rest stay on cuBLAS): separates the GEMM's own cost from the LoRA work."""
@@ -627,7 +629,6 @@ def run_denoise(args):
             _launch_k.lora_gemm_(x2, self.lin.weight, self.lin.bias, out)
             return out.view(*x.shape[:-1], self.lin.out_features)
 
-    from lithe_b200.kernels import _launch as _launch_k
     plain = {n: _PlainGemm(bases[n], packed[n]) for n in names}
 
     def install(kind):
