@@ -298,19 +298,40 @@ def run_lithe(args):
     max_in = max(a for a, _ in SHAPES)
     max_out = max(b for _, b in SHAPES)
     if not args.no_e2e:
+        # x is only read from the host, so the shapes share one buffer; each shape's output has
+        # its own, written back every step and read again as the next step's base output
         x_host = torch.empty(nb * TOKENS * max_in, dtype=torch.bfloat16, pin_memory=True)
-        o_host = torch.empty(nb * TOKENS * max_out, dtype=torch.bfloat16, pin_memory=True)
         x_host.normal_()
-        o_host.normal_().mul_(0.05)
+        o_hosts = [torch.empty(nb * TOKENS * b, dtype=torch.bfloat16, pin_memory=True) for _, b in SHAPES]
+        for o in o_hosts:
+            o.normal_().mul_(0.05)
     h2d = sum(nb * TOKENS * (a + b) * 2 for a, b in SHAPES)
     d2h = sum(nb * TOKENS * b * 2 for _, b in SHAPES)
+    # Copies in on one stream, the call on the current stream, copies out on a third: PCIe is
+    # full duplex, so one shape's output read-back overlaps the next shape's input upload.
+    copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
+    done_call = [None] * len(SHAPES)     # per shape: its last call (xs[i] / outs[i] free to refill)
+    done_back = [None] * len(SHAPES)     # per shape: its last read-back (o_hosts[i] written)
 
     def e2e_step():
         for i, (a, b) in enumerate(SHAPES):
-            xs[i].copy_(x_host[: nb * TOKENS * a].view(nb, TOKENS, a), non_blocking=True)
-            outs[i].copy_(o_host[: nb * TOKENS * b].view(nb, TOKENS, b), non_blocking=True)
+            with torch.cuda.stream(copy_in):
+                for ev in (done_call[i], done_back[i]):
+                    if ev is not None:
+                        copy_in.wait_event(ev)
+                xs[i].copy_(x_host[: nb * TOKENS * a].view(nb, TOKENS, a), non_blocking=True)
+                outs[i].copy_(o_hosts[i].view(nb, TOKENS, b), non_blocking=True)
+                uploaded = torch.cuda.Event()
+                uploaded.record(copy_in)
+            stream.wait_event(uploaded)
             packed_codebook_lora_delta_(outs[i], xs[i], bank, names[i], ids, scaling=1.0)
-            o_host[: nb * TOKENS * b].view(nb, TOKENS, b).copy_(outs[i], non_blocking=True)
+            done_call[i] = torch.cuda.Event()
+            done_call[i].record(stream)
+            with torch.cuda.stream(copy_out):
+                copy_out.wait_event(done_call[i])
+                o_hosts[i].view(nb, TOKENS, b).copy_(outs[i], non_blocking=True)
+                done_back[i] = torch.cuda.Event()
+                done_back[i].record(copy_out)
 
     e2e_ms = None
     if not args.no_e2e:
@@ -320,8 +341,12 @@ def run_lithe(args):
         barrier(world)
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         e0.record(stream)
+        copy_in.wait_event(e0)                      # no copy starts before the timed region
+        copy_out.wait_event(e0)
         for _ in range(e2e_steps):
             e2e_step()
+        for ev in done_back:                        # ...and the region ends after the last read-back
+            stream.wait_event(ev)
         e1.record(stream)
         torch.cuda.synchronize(dev)
         barrier(world)
@@ -373,7 +398,8 @@ def run_lithe(args):
             "e2e": None if e2e_ms is None else {
                 "value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                "api": "lithe_b200.kernels.packed_codebook_lora_delta_ (C ABI lithe_sgmv_index), pinned host buffers"},
+                "api": "lithe_b200.kernels.packed_codebook_lora_delta_ (C ABI lithe_sgmv_index), pinned host buffers; "
+                       "uploads, calls and read-backs on three streams (one shape's read-back overlaps the next upload)"},
             "clocks": clocks.summary(),
             "gpu_launches": launches,
             "per_shape": shapes_out,
