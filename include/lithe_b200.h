@@ -143,7 +143,8 @@ LITHE_API int32_t lithe_sgmv_index_ws(const void* x, void* out, int32_t accumula
  * only allocator is cudaMalloc (which synchronises the device and can fail under memory
  * pressure in the middle of serving), or a serving loop that runs under a fixed memory budget.
  * The decoded factors go to a static device array of LITHE_NOALLOC_WS_BYTES that is part of the
- * library's image on each device; results equal lithe_sgmv_index's bit for bit.
+ * library's image on each device; results equal lithe_sgmv_index's bit for bit.  Calls with
+ * m <= 8 take the small-m form, which needs no workspace and leaves the array untouched.
  *   - Limit: lithe_sgmv_workspace_bytes(batch, d_in, d_out) must be <= LITHE_NOALLOC_WS_BYTES
  *     (e.g. batch 34 at d_in 3072, d_out 12288); a larger call returns LITHE_ERR_UNSUPPORTED
  *     and launches nothing.  Use lithe_sgmv_index or lithe_sgmv_index_ws for it.
