@@ -148,8 +148,13 @@ LITHE_API int32_t lithe_sgmv_index_ws(const void* x, void* out, int32_t accumula
  *   - Limit: lithe_sgmv_workspace_bytes(batch, d_in, d_out) must be <= LITHE_NOALLOC_WS_BYTES
  *     (e.g. batch 34 at d_in 3072, d_out 12288); a larger call returns LITHE_ERR_UNSUPPORTED
  *     and launches nothing.  Use lithe_sgmv_index or lithe_sgmv_index_ws for it.
- *   - Set-up: the first call on each device looks up the array's device address with that
- *     device current (a runtime call); make that first call before any stream capture starts.
+ *   - Set-up: the first call in each CUDA context (in practice: on each device, whose primary
+ *     context the runtime uses) looks up the array's device address with that context current
+ *     (runtime calls, one of which initialises the context if needed); make that first call
+ *     before any stream capture starts.  The address is cached per context handle.  After
+ *     cudaDeviceReset() the device's next primary context may be given the old handle while the
+ *     array sits at a new address, so do not call this entry point again in a process that has
+ *     reset the device.
  *   - Nothing has to start at zero: every workspace byte the SGMV kernel reads is written by
  *     the same call's decode kernel.
  *   - Races: all calls on one device share the one array.  Two calls in flight at the same

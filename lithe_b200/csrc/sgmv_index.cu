@@ -1037,23 +1037,46 @@ namespace lithe {
 // so calls never allocate.  256-byte alignment covers the 16-byte bulk-copy rule.
 static __device__ __align__(256) uint8_t g_noalloc_ws[LITHE_NOALLOC_WS_BYTES];
 
-// Device address of g_noalloc_ws on the current device, looked up on the first call per device.
+// Device address of g_noalloc_ws in the current CUDA context.  The address belongs to the
+// module image loaded into a context, so it is cached per context (keyed on the handle that
+// cuCtxGetCurrent returns, looked up through the runtime's driver entry point) rather than per
+// device ordinal: a context created after a reset of the device gets its own lookup.
 static int32_t noalloc_workspace(void** ptr) {
+    using CtxGetCurrent = CUresult (*)(CUcontext*);
     static std::mutex mu;
-    static void* addr[64] = {};
-    int device = 0;
-    cudaError_t e = cudaGetDevice(&device);
-    if (e != cudaSuccess) return fail_cuda(e, "cudaGetDevice");
-    if (device < 0 || device >= 64) return fail_unsupported("device ordinal %d", device);
+    static CtxGetCurrent get_ctx = nullptr;
+    constexpr int kSlots = 64;
+    static CUcontext ctx_of[kSlots] = {};
+    static void* addr_of[kSlots] = {};
+    static int used = 0;
     std::lock_guard<std::mutex> lock(mu);
-    if (!addr[device]) {
-        void* a = nullptr;
-        e = cudaGetSymbolAddress(&a, g_noalloc_ws);
-        if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(noalloc workspace)");
-        if (!a) return fail_arg("cudaGetSymbolAddress returned NULL for the noalloc workspace");
-        addr[device] = a;
+    cudaError_t e = cudaSuccess;
+    if (!get_ctx) {
+        void* fn = nullptr;
+        cudaDriverEntryPointQueryResult q = cudaDriverEntryPointSymbolNotFound;
+        e = cudaGetDriverEntryPoint("cuCtxGetCurrent", &fn, cudaEnableDefault, &q);
+        if (e != cudaSuccess) return fail_cuda(e, "cudaGetDriverEntryPoint(cuCtxGetCurrent)");
+        if (q != cudaDriverEntryPointSuccess || !fn) return fail_unsupported("driver does not export cuCtxGetCurrent");
+        get_ctx = reinterpret_cast<CtxGetCurrent>(fn);
     }
-    *ptr = addr[device];
+    CUcontext ctx = nullptr;
+    if (get_ctx(&ctx) != CUDA_SUCCESS) return fail_arg("cuCtxGetCurrent failed");
+    for (int i = 0; ctx && i < used; ++i) {
+        if (ctx_of[i] == ctx) {
+            *ptr = addr_of[i];
+            return LITHE_OK;
+        }
+    }
+    // also makes the device's primary context current when no context was current yet
+    void* a = nullptr;
+    e = cudaGetSymbolAddress(&a, g_noalloc_ws);
+    if (e != cudaSuccess) return fail_cuda(e, "cudaGetSymbolAddress(noalloc workspace)");
+    if (!a) return fail_arg("cudaGetSymbolAddress returned NULL for the noalloc workspace");
+    if (!ctx && (get_ctx(&ctx) != CUDA_SUCCESS || !ctx)) return fail_arg("no current CUDA context");
+    const int slot = used < kSlots ? used++ : static_cast<int>(reinterpret_cast<uintptr_t>(ctx) % kSlots);
+    ctx_of[slot] = ctx;
+    addr_of[slot] = a;
+    *ptr = a;
     return LITHE_OK;
 }
 

@@ -32,10 +32,21 @@ LZMA_PRESET = 9 | lzma.PRESET_EXTREME
 
 @dataclass
 class LitheAdapter:
-    """Index streams of one adapter plus everything needed to decode them."""
+    """One adapter as it sits in a ``.lithe`` file, held in host memory.
 
-    modules: List[Dict[str, Any]]                  # [{"name", "shape_a", "shape_b"}] in stream order
-    indices: Dict[str, Dict[str, np.ndarray]]      # name -> {"A": (L, nA) uint16, "B": (L, nB) uint16}
+    The field names and defaults are those of the reference's ``LitheAdapter``, so an object
+    from either package carries the same information.  ``modules`` lists the wrapped linears
+    in the order their indices appear in the payload; each entry is a dict with ``name`` and
+    the two factor shapes ``shape_a`` = (rank, in_features) and ``shape_b`` =
+    (out_features, rank).  ``indices[name]["A"]`` / ``["B"]`` are the codebook indices of the
+    two factors, one row per residual level and one column per 64-value block.  The remaining
+    fields describe the codebook the indices point into (block size, index width, number of
+    levels, the per-level scales of the A and B pools) and the adapter's naming scheme
+    ("diffusers" or "kohya" module names), its alpha and free-form metadata.
+    """
+
+    modules: List[Dict[str, Any]]
+    indices: Dict[str, Dict[str, np.ndarray]]
     rank: int
     alpha: float
     key_format: str = "diffusers"
@@ -49,16 +60,26 @@ class LitheAdapter:
 
     @property
     def num_indices(self) -> int:
-        return sum(int(v["A"].size) + int(v["B"].size) for v in self.indices.values())
+        """Total index count over both factors of every module."""
+        total = 0
+        for sides in self.indices.values():
+            total += int(np.size(sides["A"])) + int(np.size(sides["B"]))
+        return total
 
     @property
     def scaling(self) -> float:
+        """The factor the LoRA product is multiplied by: alpha / rank."""
         return float(self.alpha) / self.rank
 
     def raw_stream(self) -> bytes:
-        names = [m["name"] for m in self.modules]
-        sides = [self.indices[n]["A"] for n in names] + [self.indices[n]["B"] for n in names]
-        return b"".join(np.ascontiguousarray(a, dtype="<u2").tobytes() for a in sides)
+        """The uncompressed payload: every module's A matrix, then every module's B matrix,
+        each as little-endian uint16 in (level, block) row-major order."""
+        order = [m["name"] for m in self.modules]
+        chunks = []
+        for side in ("A", "B"):
+            for name in order:
+                chunks.append(np.ascontiguousarray(self.indices[name][side], dtype="<u2").tobytes())
+        return b"".join(chunks)
 
 
 def _header(ad: LitheAdapter, raw: bytes) -> Dict[str, Any]:

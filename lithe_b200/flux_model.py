@@ -222,5 +222,6 @@ def denoise(model: FluxShapedTransformer, latents, text, pooled, steps: int) -> 
 
 def lora_targets(model: nn.Module):
     """(path, linear) of the 342 attention + FFN linears LoRA adapters target."""
-    from .module import FLUX_TARGET_MODULES, _match
-    return [(n, m) for n, m in model.named_modules() if isinstance(m, nn.Linear) and _match(n, FLUX_TARGET_MODULES)]
+    from . import _modtree
+    from .module import FLUX_TARGET_MODULES
+    return list(_modtree.linears_matching(model, FLUX_TARGET_MODULES))

@@ -15,6 +15,9 @@ import torch
 
 from .. import _lib
 
+# Activation dtypes the sgmv kernels compute in.
+ACTIVATION_DTYPES = (torch.bfloat16,)
+
 _err_words: dict = {}
 _err_lock = threading.Lock()
 

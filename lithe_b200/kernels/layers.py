@@ -19,6 +19,7 @@ from typing import Callable, Dict, Iterable, Optional, Tuple
 import torch
 from torch import nn
 
+from .. import _modtree
 from .. import codebook as cb
 from . import _launch
 from .packed import PackedBank
@@ -262,18 +263,9 @@ class PerSampleLoRALinear(nn.Module):
 
 def wrap_linears(model: nn.Module, paths: Iterable[str],
                  factory: Callable[[str, nn.Linear], nn.Module]) -> Dict[str, nn.Module]:
-    """Replace ``model.<path>`` (an ``nn.Linear``) by ``factory(path, linear)`` for every path."""
-    wrapped = {}
-    for path in paths:
-        base = model.get_submodule(path)
-        if not isinstance(base, nn.Linear):
-            raise TypeError(f"{path} is not nn.Linear")
-        parent_name, _, child = path.rpartition(".")
-        parent = model.get_submodule(parent_name) if parent_name else model
-        module = factory(path, base)
-        setattr(parent, child, module)
-        wrapped[path] = module
-    return wrapped
+    """Put ``factory(path, linear)`` in place of the ``nn.Linear`` at every dotted ``path``
+    of ``model`` (TypeError if a path names something else); returns {path: wrapper}."""
+    return _modtree.replace_linears(model, paths, factory)
 
 
 def wrap_packed(model: nn.Module, bank: PackedBank, key_format: str = "diffusers",

@@ -3,20 +3,22 @@
 Inference form of ``LitheLinear`` (lithe/module.py:63-156): after ``load_indices`` the layer
 computes  y = W x + (B_hat A_hat x) * alpha / r  with A_hat, B_hat decoded from its index
 streams.  The indices stay resident on the GPU in packed form and the fused sm_100a kernel
-decodes them inside the shrink/expand tiles, accumulating into the base output; shapes the
-fused kernel does not take (d_in not a multiple of 64, other ranks) use factors decoded once
-by the decode kernel and two cuBLAS products.  Training (straight-through re-quantisation of
+decodes them inside the shrink/expand tiles, accumulating into the base output.  There is
+no second path: shapes the kernel does not take (in_features not a multiple of 64, ranks
+other than 1/2/4/8/16) and activation dtypes it does not compute in raise instead of falling
+back to decoded factors and eager products.  Training (straight-through re-quantisation of
 fp32 proxies) is not part of this package.
 """
 from __future__ import annotations
 
 import math
-from typing import Dict, Iterable, List, Optional, Sequence
+from typing import Dict, List, Optional, Sequence
 
 import numpy as np
 import torch
 from torch import nn
 
+from . import _modtree
 from . import codebook as cb
 from . import quant
 from .kernels import _launch
@@ -43,25 +45,34 @@ _FUSED_RANKS = (1, 2, 4, 8, 16)
 
 
 class TwinCodebook(nn.Module):
-    """Holds the deterministic pools as non-persistent buffers (never saved)."""
+    """The fixed twin codebook of a LITHE adapter, as a module every ``LitheLinear`` shares.
+
+    It is derived from four numbers (block size, index width and the per-level scales of the
+    A and B pools), so nothing of it is ever written to a state dict: the pools are
+    non-persistent buffers that follow ``.to(device)``.  ``lut`` is the ten-values-per-level
+    table the CUDA kernels take in place of the pools; a decode through it equals a decode
+    through the pools bit for bit (``codebook.level_lut`` checks that when it builds it).
+    """
 
     def __init__(self, block_size: int = cb.BLOCK_SIZE, n_bits: int = cb.N_BITS,
                  sigma_a: Sequence[float] = cb.SIGMA_A, sigma_b: Sequence[float] = cb.SIGMA_B):
         super().__init__()
-        pool_a, pool_b = cb.twin_pools(block_size, n_bits, sigma_a, sigma_b)
-        self.block_size = block_size
-        self.n_bits = n_bits
-        self.sigma_a = tuple(float(s) for s in sigma_a)
-        self.sigma_b = tuple(float(s) for s in sigma_b)
-        self.register_buffer("pool_a", pool_a, persistent=False)
-        self.register_buffer("pool_b", pool_b, persistent=False)
-        self.register_buffer("proj", cb.projection_matrix(block_size, n_bits), persistent=False)
-        self.lut = cb.kernel_lut(pool_a, pool_b)
+        self.block_size, self.n_bits = int(block_size), int(n_bits)
+        self.sigma_a = tuple(map(float, sigma_a))
+        self.sigma_b = tuple(map(float, sigma_b))
+        pools = dict(zip(("pool_a", "pool_b"), cb.twin_pools(block_size, n_bits, self.sigma_a, self.sigma_b)))
+        # proj: the generator matrix of the lattice, kept for callers that inspect it
+        pools["proj"] = cb.projection_matrix(block_size, n_bits)
+        for name, tensor in pools.items():
+            self.register_buffer(name, tensor, persistent=False)
+        self.lut = cb.kernel_lut(self.pool_a, self.pool_b)
 
     def decode(self, indices: torch.Tensor, shape, side: str, device=None) -> torch.Tensor:
-        """fp32 factor decoded on a CUDA device (bit-identical to the reference decode)."""
-        pool = self.pool_a if side == "A" else self.pool_b
-        return quant.decode(indices, shape, pool, device=device)
+        """The fp32 factor named by ``indices`` (L, n_blocks), decoded on a CUDA device;
+        bit-identical to the reference's decode."""
+        if side not in ("A", "B"):
+            raise ValueError(f"side must be 'A' or 'B', got {side!r}")
+        return quant.decode(indices, shape, self.pool_a if side == "A" else self.pool_b, device=device)
 
 
 class LitheLinear(nn.Module):
@@ -133,48 +144,50 @@ class LitheLinear(nn.Module):
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if not self._frozen:
             raise RuntimeError("LitheLinear has no indices loaded (training is not part of lithe_b200)")
+        if not self.fused:
+            raise ValueError(f"LitheLinear {self.in_features}->{self.out_features}, rank {self.rank}: the sm_100a "
+                             "kernel needs rank in (1, 2, 4, 8, 16), in_features % 64 == 0, out_features % 8 == 0 "
+                             "and out_features * rank % 64 == 0 (decoded_factors() still decodes any shape)")
+        if x.dtype not in _launch.ACTIVATION_DTYPES:
+            raise TypeError(f"LitheLinear runs the sm_100a kernel on {_launch.ACTIVATION_DTYPES} activations, "
+                            f"got {x.dtype}")
         out = self.base(x)
         _inference_only(out)
-        if self.fused and x.dtype == torch.bfloat16 and x.is_cuda:
-            x3 = x.reshape(1, -1, self.in_features).contiguous()
-            out3 = out.view(1, -1, self.out_features)
-            L = self._levels
-            va = _launch.index_view(self._words, 0, L, 0, 0)
-            vb = _launch.index_view(self._words, 0, L, 0, L * self._na)
-            _launch.sgmv_index_(x3, out3, accumulate=True, view_a=va, view_b=vb, n_slots=1, ids=self._ids,
-                                weights=None, rank=self.rank, lut=self.codebook.lut, scaling=self.scaling)
-            return out
-        a_hat, b_hat = self.decoded_factors()
-        delta = nn.functional.linear(nn.functional.linear(x, a_hat.to(x.dtype)), b_hat.to(x.dtype))
-        return out + delta * self.scaling
-
-
-def _match(path: str, targets: Iterable[str]) -> bool:
-    return any(path == t or path.endswith("." + t) for t in targets)
+        x3 = x.reshape(1, -1, self.in_features).contiguous()
+        out3 = out.view(1, -1, self.out_features)
+        L = self._levels
+        va = _launch.index_view(self._words, 0, L, 0, 0)
+        vb = _launch.index_view(self._words, 0, L, 0, L * self._na)
+        _launch.sgmv_index_(x3, out3, accumulate=True, view_a=va, view_b=vb, n_slots=1, ids=self._ids,
+                            weights=None, rank=self.rank, lut=self.codebook.lut, scaling=self.scaling)
+        return out
 
 
 def inject_lithe(model: nn.Module, target_modules: Sequence[str] = FLUX_TARGET_MODULES, rank: int = 16,
                  alpha: Optional[float] = None, requantize_every: int = 10, drift_tau: Optional[float] = None,
                  codebook: Optional[TwinCodebook] = None) -> Dict[str, LitheLinear]:
-    """Replace every nn.Linear whose path ends with a target suffix by a LitheLinear.
+    """Wrap every ``nn.Linear`` of ``model`` whose dotted path ends in one of
+    ``target_modules`` (whole path components) in a ``LitheLinear`` sharing one codebook.
 
-    Returns an ordered {module_path: LitheLinear}; this order defines the index-stream layout.
+    The returned dict follows ``model.named_modules()`` order, which is the order of the
+    modules in an adapter's index stream.  ValueError if nothing matches.
     """
-    codebook = codebook if codebook is not None else TwinCodebook()
-    targets = [(name, mod) for name, mod in model.named_modules()
-               if isinstance(mod, nn.Linear) and _match(name, target_modules)]
-    if not targets:
+    shared = TwinCodebook() if codebook is None else codebook
+    paths = [path for path, _ in _modtree.linears_matching(model, target_modules)]
+    if not paths:
         raise ValueError("no target linear found; check target_modules")
-    wrapped: Dict[str, LitheLinear] = {}
-    for name, mod in targets:
-        parent_name, _, child = name.rpartition(".")
-        parent = model.get_submodule(parent_name) if parent_name else model
-        layer = LitheLinear(mod, codebook, rank=rank, alpha=alpha, requantize_every=requantize_every,
-                            drift_tau=drift_tau)
-        setattr(parent, child, layer)
-        wrapped[name] = layer
-    return wrapped
+
+    def make(_path: str, lin: nn.Linear) -> LitheLinear:
+        return LitheLinear(lin, shared, rank=rank, alpha=alpha, requantize_every=requantize_every,
+                           drift_tau=drift_tau)
+
+    return _modtree.replace_linears(model, paths, make)
 
 
 def lithe_layers(model: nn.Module) -> Dict[str, LitheLinear]:
-    return {n: m for n, m in model.named_modules() if isinstance(m, LitheLinear)}
+    """Every ``LitheLinear`` in ``model``, by dotted path."""
+    found: Dict[str, LitheLinear] = {}
+    for path, mod in model.named_modules():
+        if isinstance(mod, LitheLinear):
+            found[path] = mod
+    return found

@@ -18,6 +18,7 @@ import numpy as np
 import torch
 from torch import nn
 
+from . import _modtree
 from . import codebook as cb
 from . import quant
 from .fileio import LitheAdapter
@@ -28,25 +29,34 @@ Route = Sequence[Tuple[int, float]]
 
 
 class Router:
-    """Per-batch routing table shared by all MultiAdapterLinear layers."""
+    """The routing of the current batch, shared by every ``MultiAdapterLinear`` of a model.
+
+    ``set(routes)`` takes one route per sample, a route being a list of (adapter id, weight)
+    pairs (empty: the sample gets no adapter).  It stores them as two (batch, width) tables,
+    width being the longest route (at least 1): ``ids`` int64 with -1 in unused places and
+    ``weights`` float32 with 0 there.  Weights must be >= 0 (ValueError otherwise).
+    """
 
     def __init__(self):
-        self.ids: Optional[torch.Tensor] = None      # (b, m) int64, -1 = padding
-        self.weights: Optional[torch.Tensor] = None  # (b, m) float32
+        self.ids: Optional[torch.Tensor] = None
+        self.weights: Optional[torch.Tensor] = None
         self._tables: Dict[tuple, List[Tuple[torch.Tensor, torch.Tensor]]] = {}
         self._key = None
         self._serial = 0
 
     def set(self, routes: Sequence[Route]) -> None:
-        m = max(1, max((len(r) for r in routes), default=1))
-        ids = torch.full((len(routes), m), -1, dtype=torch.int64)
-        w = torch.zeros(len(routes), m, dtype=torch.float32)
-        for i, r in enumerate(routes):
-            for j, (a, wt) in enumerate(r):
-                if wt < 0:
+        routes = [list(r) for r in routes]
+        width = max([1] + [len(r) for r in routes])
+        id_rows = np.full((len(routes), width), -1, dtype=np.int64)
+        w_rows = np.zeros((len(routes), width), dtype=np.float32)
+        for i, route in enumerate(routes):
+            for j, (adapter, weight) in enumerate(route):
+                if weight < 0:
                     raise ValueError("mixture weights must be non-negative")
-                ids[i, j], w[i, j] = int(a), float(wt)
-        self.ids, self.weights = ids, w
+                id_rows[i, j] = int(adapter)
+                w_rows[i, j] = float(weight)
+        self.ids = torch.from_numpy(id_rows)
+        self.weights = torch.from_numpy(w_rows)
         self._serial += 1
 
     def columns(self, device: torch.device, scales: Tuple[float, ...]) -> List[Tuple[torch.Tensor, torch.Tensor]]:
@@ -169,42 +179,59 @@ class MultiAdapterLinear(nn.Module):
         return out
 
 
-def attach_adapters(model: nn.Module, adapters: List[LitheAdapter], router: Optional[Router] = None,
-                    fused_gemm: bool = False) -> Tuple[Router, Dict[str, MultiAdapterLinear]]:
-    """Wrap every linear named in the adapters' module list and load all index streams
-    (``lithe/serve.py:100-127``); ``fused_gemm`` selects the expand-in-GEMM path where eligible."""
+def _shared_module_names(adapters: List[LitheAdapter]) -> List[str]:
+    """Module names of the first adapter, after checking that every adapter covers the same
+    set of modules (in any order) with the same rank."""
     if not adapters:
         raise ValueError("need at least one adapter")
-    router = router or Router()
-    ref = adapters[0]
-    names = [mm["name"] for mm in ref.modules]
-    for ad in adapters[1:]:
-        if {mm["name"] for mm in ad.modules} != set(names) or ad.rank != ref.rank:
+    first = adapters[0]
+    names = [entry["name"] for entry in first.modules]
+    expected = set(names)
+    for other in adapters[1:]:
+        if other.rank != first.rank or {entry["name"] for entry in other.modules} != expected:
             raise ValueError("all adapters must cover the same modules with the same rank")
-    pool_a = cb.build_pools(ref.sigma_a, ref.block_size, ref.n_bits)
-    pool_b = cb.build_pools(ref.sigma_b, ref.block_size, ref.n_bits)
+    return names
+
+
+def attach_adapters(model: nn.Module, adapters: List[LitheAdapter], router: Optional[Router] = None,
+                    fused_gemm: bool = False) -> Tuple[Router, Dict[str, MultiAdapterLinear]]:
+    """Serve ``adapters`` from ``model``: every linear an adapter names becomes a
+    ``MultiAdapterLinear`` holding the int16 index banks of all of them, in list order (adapter
+    id = position in ``adapters``), all sharing one ``Router``.
+
+    Module names may carry a leading "transformer." (the diffusers pipeline attribute); it is
+    dropped to find the linear inside ``model``.  ``fused_gemm`` selects the expand-in-GEMM
+    path where it is eligible.  Returns (router, {module name: layer}).
+    """
+    names = _shared_module_names(adapters)
+    router = Router() if router is None else router
+    first = adapters[0]
+    pool_a = cb.build_pools(first.sigma_a, first.block_size, first.n_bits)
+    pool_b = cb.build_pools(first.sigma_b, first.block_size, first.n_bits)
+    scales = [float(ad.alpha) / ad.rank for ad in adapters]
+    prefix = "transformer."
     layers: Dict[str, MultiAdapterLinear] = {}
     for name in names:
-        path = name[len("transformer."):] if name.startswith("transformer.") else name
-        base = model.get_submodule(path)
-        if not isinstance(base, nn.Linear):
-            raise TypeError(f"{path} is not nn.Linear")
-        parent_name, _, child = path.rpartition(".")
-        parent = model.get_submodule(parent_name) if parent_name else model
-        layer = MultiAdapterLinear(base, router, ref.rank, pool_a, pool_b, fused_gemm=fused_gemm).to(base.weight.device)
-        for ad in adapters:
-            layer.add_adapter(ad.indices[name]["A"], ad.indices[name]["B"], float(ad.alpha) / ad.rank)
-        setattr(parent, child, layer)
-        layers[name] = layer
+        path = name[len(prefix):] if name.startswith(prefix) else name
+        base = _modtree.linear_at(model, path)
+        layer = MultiAdapterLinear(base, router, first.rank, pool_a, pool_b, fused_gemm=fused_gemm)
+        layer = layer.to(base.weight.device)
+        for ad, scale in zip(adapters, scales):
+            layer.add_adapter(ad.indices[name]["A"], ad.indices[name]["B"], scale)
+        layers[name] = _modtree.swap(model, path, layer)
     return router, layers
 
 
+_NO_ROUTE = frozenset({"", "none", "-"})
+
+
 def parse_route(spec: str) -> List[Tuple[int, float]]:
-    """'0' -> [(0, 1.0)];  '0:0.6,2:0.4' -> [(0, 0.6), (2, 0.4)];  'none' -> []."""
-    if spec.strip().lower() in ("", "none", "-"):
+    """Route text -> route.  "3" is adapter 3 at weight 1; "0:0.6,2:0.4" mixes adapters 0
+    and 2; "", "none" and "-" (any case) mean no adapter."""
+    if spec.strip().lower() in _NO_ROUTE:
         return []
-    route = []
-    for part in spec.split(","):
-        a, _, wt = part.partition(":")
-        route.append((int(a), float(wt) if wt else 1.0))
+    route: List[Tuple[int, float]] = []
+    for item in spec.split(","):
+        adapter, sep, weight = item.partition(":")
+        route.append((int(adapter), float(weight) if sep and weight else 1.0))
     return route

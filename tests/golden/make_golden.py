@@ -1,7 +1,9 @@
 """Generate the golden fixtures of tests/golden/ by running the REFERENCE implementation.
 
-Run where the reference package (JianJiang1995/LITHE, ``import lithe``) is importable:
+Run it with the root of a checkout of the reference package (JianJiang1995/LITHE, the
+folder that holds ``lithe/``), given either as the first argument or as LITHE_REF:
 
+    python tests/golden/make_golden.py /path/to/LITHE
     LITHE_REF=/path/to/LITHE python tests/golden/make_golden.py
 
 Every fixture holds seeded inputs and the reference's outputs for them; the tests use the
@@ -38,7 +40,18 @@ import numpy as np
 import torch
 
 HERE = Path(__file__).resolve().parent
-REF = os.environ.get("LITHE_REF", "/root/reference")
+
+
+def _reference_root() -> str:
+    """The reference checkout to import: argv[1], else $LITHE_REF; there is no default."""
+    ref = sys.argv[1] if len(sys.argv) > 1 else os.environ.get("LITHE_REF", "")
+    if not ref or not (Path(ref) / "lithe" / "__init__.py").exists():
+        raise SystemExit("make_golden.py needs the reference checkout: pass its root as the first argument "
+                         "or set LITHE_REF (the folder that contains lithe/__init__.py)")
+    return ref
+
+
+REF = _reference_root()
 sys.path.insert(0, REF)
 
 from lithe import codebook as cb  # noqa: E402

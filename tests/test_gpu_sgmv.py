@@ -247,10 +247,12 @@ def test_index_layer_matches_truth():
             assert rel_fro(player(x).float(), truth) < REL_FRO
 
 
-def test_lithe_linear_fused_and_decoded_paths():
+def test_lithe_linear_kernel_path_and_unsupported_shapes():
+    """LitheLinear runs the fused kernel; a shape the kernel does not take raises (there is no
+    eager second path), while decoded_factors() still decodes it bit-exactly."""
     import lithe_b200 as lb
     torch.manual_seed(0)
-    for d_in, d_out, rank in ((256, 384, 16), (96, 160, 8)):
+    for d_in, d_out, rank in ((256, 384, 16), (192, 160, 8), (96, 160, 8)):
         base = torch.nn.Linear(d_in, d_out).cuda().bfloat16()
         net = torch.nn.Sequential(base)
         layers = lb.inject_lithe(net, ["0"], rank=rank, alpha=2 * rank)
@@ -263,11 +265,17 @@ def test_lithe_linear_fused_and_decoded_paths():
         fa, fb = layer.decoded_factors()
         assert torch.equal(fa.cpu(), a) and torch.equal(fb.cpu(), bm)
         x = torch.randn(2, 40, d_in, device="cuda").bfloat16()
+        if not layer.fused:
+            with torch.no_grad(), pytest.raises(ValueError):
+                net(x)
+            continue
         with torch.no_grad():
             y = net(x).float()
         truth = torch.nn.functional.linear(x.float(), base.weight.float(), base.bias.float()) + \
             (x.float() @ a.cuda().T @ bm.cuda().T) * 2.0
         assert rel_fro(y, truth) < REL_FRO
+        with torch.no_grad(), pytest.raises(TypeError):
+            net(x.float())            # fp32 activations: not a kernel dtype
 
 
 @pytest.mark.parametrize("d_in,d_out", FLUX_SHAPES)

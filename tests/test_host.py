@@ -6,7 +6,8 @@ import torch
 from lithe_b200 import codebook as cb
 from lithe_b200 import fileio, quant, serve
 from lithe_b200.kernels import packed
-from lithe_b200.module import FLUX_TARGET_MODULES, _match
+from lithe_b200 import _modtree
+from lithe_b200.module import FLUX_TARGET_MODULES
 from oracle import codebook_ref, decode_ref
 from tests.helpers import GOLDEN, SMALL, golden_modules, load_golden, random_adapter
 
@@ -145,6 +146,14 @@ def test_router_and_parse_route():
     assert serve.parse_route("1") == [(1, 1.0)]
     assert serve.parse_route("0:0.6,2:0.4") == [(0, 0.6), (2, 0.4)]
     assert serve.parse_route("none") == []
+    for empty in ("", "  ", "-", "NONE", " None "):
+        assert serve.parse_route(empty) == []
+    assert serve.parse_route("4:") == [(4, 1.0)]
+    assert serve.parse_route(" 1 : 0.25, 3") == [(1, 0.25), (3, 1.0)]
+    with pytest.raises(ValueError):
+        serve.parse_route("a:1")
+    r.set([])
+    assert tuple(r.ids.shape) == (0, 1) and r.ids.dtype == torch.int64 and r.weights.dtype == torch.float32
 
 
 def test_router_columns_fold_weights_and_scales():
@@ -166,7 +175,7 @@ def test_flux_target_count():
     for i in range(38):
         names += [f"single_transformer_blocks.{i}.attn.{t}" for t in ("to_q", "to_k", "to_v")]
         names += [f"single_transformer_blocks.{i}.{t}" for t in ("proj_mlp", "proj_out", "norm.linear")]
-    assert sum(_match(n, FLUX_TARGET_MODULES) for n in names) == 342
+    assert sum(_modtree.suffix_match(n, FLUX_TARGET_MODULES) for n in names) == 342
 
 
 def test_flux_shaped_model_targets_342_linears():
@@ -194,3 +203,80 @@ def test_fused_gemm_in_features_limit():
         layer.fused_gemm_max_k = None
         assert layer._gemm_ok(x3)
         assert not layer._gemm_ok(torch.zeros(2, 100, d_in, dtype=torch.bfloat16))   # tokens per sample % 128
+
+
+def test_module_tree_helpers():
+    """Suffix matching works on whole path components; swaps keep the tree's order; a bad
+    path leaves the model untouched."""
+    from torch import nn
+    assert _modtree.suffix_match("blocks.0.attn.to_q", ["attn.to_q"])
+    assert _modtree.suffix_match("attn.to_q", ["attn.to_q"])
+    assert not _modtree.suffix_match("blocks.0.xattn.to_q", ["attn.to_q"])
+    assert not _modtree.suffix_match("blocks.0.attn.to_q2", ["attn.to_q"])
+    model = nn.Sequential(nn.Linear(4, 4), nn.ReLU(), nn.Sequential(nn.Linear(4, 8), nn.Linear(8, 4)))
+    got = _modtree.replace_linears(model, ["2.1", "0"], lambda p, lin: nn.Sequential(lin))
+    assert list(got) == ["2.1", "0"]
+    assert isinstance(model[0], nn.Sequential) and isinstance(model[2][1], nn.Sequential)
+    assert isinstance(model[2][0], nn.Linear)
+    with pytest.raises(TypeError):
+        _modtree.replace_linears(model, ["2.0", "1"], lambda p, lin: nn.Sequential(lin))
+    assert isinstance(model[2][0], nn.Linear)          # nothing swapped
+    assert [p for p, _ in _modtree.linears_matching(model, ["0"])] == ["0.0", "2.0", "2.1.0"]
+
+
+def test_inject_lithe_and_lithe_layers_on_cpu():
+    from torch import nn
+    from lithe_b200.module import LitheLinear, inject_lithe, lithe_layers
+
+    class Block(nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.attn = nn.Module()
+            self.attn.to_q = nn.Linear(64, 64)
+            self.attn.to_k = nn.Linear(64, 64)
+            self.xattn = nn.Module()
+            self.xattn.to_q = nn.Linear(64, 64)
+            self.norm = nn.LayerNorm(64)
+
+    model = nn.Module()
+    model.blocks = nn.ModuleList([Block(), Block()])
+    wrapped = inject_lithe(model, ["attn.to_q", "attn.to_k"], rank=4)
+    assert list(wrapped) == ["blocks.0.attn.to_q", "blocks.0.attn.to_k", "blocks.1.attn.to_q", "blocks.1.attn.to_k"]
+    assert all(isinstance(m, LitheLinear) for m in wrapped.values())
+    assert isinstance(model.blocks[0].xattn.to_q, nn.Linear)
+    assert len({id(m.codebook) for m in wrapped.values()}) == 1
+    assert list(lithe_layers(model)) == list(wrapped)
+    with pytest.raises(ValueError):
+        inject_lithe(model, ["no.such"], rank=4)
+
+
+def test_attach_adapters_checks_on_cpu():
+    """attach_adapters' argument checks and wrapping (host side; the forward needs a GPU)."""
+    from torch import nn
+    ads = [random_adapter(SMALL[:3], 8, seed=s, alpha=4 * s) for s in (1, 2)]
+    names = [m["name"] for m in ads[0].modules]
+    with pytest.raises(ValueError):
+        serve.attach_adapters(nn.Module(), [])
+
+    def model_for(mods):
+        root = nn.Module()
+        for m in mods:
+            holder = root
+            parts = m["name"].split(".")
+            for part in parts[:-1]:
+                if not hasattr(holder, part):
+                    holder.add_module(part, nn.Module())
+                holder = getattr(holder, part)
+            holder.add_module(parts[-1], nn.Linear(m["shape_a"][1], m["shape_b"][0]))
+        return root
+
+    model = model_for(ads[0].modules)
+    router, layers = serve.attach_adapters(model, ads)
+    assert list(layers) == names
+    for n, layer in layers.items():
+        assert isinstance(layer, serve.MultiAdapterLinear) and layer.idx_a.shape[0] == 2
+        assert model.get_submodule(n) is layer
+        assert layer.scales == [ads[0].alpha / ads[0].rank, ads[1].alpha / ads[1].rank]
+    other = random_adapter(SMALL[:1], 8, seed=3)
+    with pytest.raises(ValueError):
+        serve.attach_adapters(model_for(ads[0].modules), [ads[0], other])

@@ -58,6 +58,36 @@ def test_noalloc_matches_existing_entry_on_two_calls(d_in, d_out, r):
         assert torch.equal(got, want)
 
 
+@pytest.mark.gpu
+def test_noalloc_at_full_capacity_and_small_m():
+    """A call whose factors fill the built-in workspace to its limit (batch 34 at 3072 -> 12288:
+    4,177,920 of 4,194,304 bytes, the last chunk near the array's end), then a call with m <= 8
+    (the small-m form, which uses no workspace), then the full call again: each equal to
+    lithe_sgmv_index bit for bit."""
+    d_in, d_out, r = 3072, 12288, 16
+    ads = [random_adapter([("l", d_in, d_out)], rank=r, seed=10 + s) for s in range(5)]
+    bank = PackedBank.from_adapters(ads, "cuda")
+    va, vb = bank.views("l")
+    lut = cb.kernel_lut(*cb.twin_pools())
+    err = torch.zeros(1, dtype=torch.int32, device="cuda")
+    g = torch.Generator().manual_seed(5)
+    full = 34
+    assert _launch.workspace_bytes(full, d_in, d_out) == 4177920
+    assert _launch.workspace_bytes(full + 1, d_in, d_out) > _lib.NOALLOC_WS_BYTES
+    for batch, seq in ((full, 72), (9, 5), (full, 16)):
+        assign = [(7 * b + batch) % 5 for b in range(batch)]
+        x = (torch.randn(batch, seq, d_in, generator=g) * 0.5).bfloat16().cuda()
+        base = torch.randn(batch, seq, d_out, generator=g).bfloat16().cuda()
+        ids = torch.tensor(assign, dtype=torch.int32, device="cuda")
+        want = _call("lithe_sgmv_index", x, base.clone(), True, va, vb, len(ads), ids, r, lut, 1.0, err)
+        got = _call("lithe_sgmv_index_noalloc", x, base.clone(), True, va, vb, len(ads), ids, r, lut, 1.0, err)
+        torch.cuda.synchronize()
+        assert int(err.item()) == 0
+        g_d, w_d = got.float().cpu() - base.float().cpu(), want.float().cpu() - base.float().cpu()
+        assert max_abs_rel(g_d, w_d) <= MAX_ABS_REL and rel_fro(g_d, w_d) < REL_FRO
+        assert torch.equal(got, want)
+
+
 def test_noalloc_rejects_calls_beyond_the_builtin_workspace():
     # Rejected on the host before any CUDA call, so no device memory is touched.
     lib = _lib.lib()
