@@ -96,6 +96,28 @@ int32_t encode_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t
     return LITHE_OK;
 }
 
+int32_t encode_bf16_chunked(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
+                            uint32_t chunks_per_box) {
+    if (inner % 64 != 0) return fail_arg("chunked tensor map: row length %llu is not a multiple of 64",
+                                         (unsigned long long)inner);
+    PFN_cuTensorMapEncodeTiled_v12000 enc;
+    int32_t rc = get_encoder(&enc);
+    if (rc != LITHE_OK) return rc;
+    // element (c0, r, k) = base[r * inner + 64 * k + c0]: the chunk index is the outer dimension,
+    // with a stride (128 B) smaller than the row stride; the three extents cover the array exactly
+    const cuuint64_t dims[3] = {64, rows, inner / 64};
+    const cuuint64_t strides[2] = {inner * 2, 128};
+    const cuuint32_t box[3] = {64, box_rows, chunks_per_box};
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, const_cast<void*>(base), dims, strides, box, estr,
+                     CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                     CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS)
+        return fail_arg("cuTensorMapEncodeTiled failed (CUresult %d) for a chunked map: row length %llu, rows %llu",
+                        static_cast<int>(r), (unsigned long long)inner, (unsigned long long)rows);
+    return LITHE_OK;
+}
+
 int32_t encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner,
                        uint32_t box_rows, int swizzle_bytes) {
     PFN_cuTensorMapEncodeTiled_v12000 enc;

@@ -27,6 +27,12 @@ int32_t current_device_sms(int* device, int* sms);
 // (b0, b1, 1) and 128-byte swizzle.  Returns LITHE_OK or an error code.
 int32_t encode_bf16_3d(CUtensorMap* map, const void* base, uint64_t d0, uint64_t d1, uint64_t d2,
                        uint32_t b0, uint32_t b1);
+// "Chunked" view of a row-major (rows, inner) bf16 array, inner a multiple of 64: dimensions
+// (64 columns, rows, inner / 64 chunks) with the chunk stride (128 B) as the outer one, so one
+// box (64, box_rows, chunks_per_box) fetches chunks_per_box adjacent 64-column chunks of
+// box_rows rows, each laid out as its own 128-byte-swizzled tile, in one TMA operation.
+int32_t encode_bf16_chunked(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_rows,
+                            uint32_t chunks_per_box);
 // 2-D bf16 tensor map (rows of `inner` elements), box (box_inner, box_rows), swizzle 0/32/64/128 B.
 int32_t encode_bf16_2d(CUtensorMap* map, const void* base, uint64_t inner, uint64_t rows, uint32_t box_inner,
                        uint32_t box_rows, int swizzle_bytes);

@@ -7,15 +7,22 @@
 // (calls with at most kSmallM token rows per sample take sgmv_small_kernel further down):
 //
 //   work unit  = (sample b, 64-token tile); CTA i owns a contiguous range of units.
-//   per unit   = d_in/64 "x chunks" (64x64 bf16 activation tiles, TMA, 128B swizzle)
-//              + d_out/64 "out chunks" (64x64 bf16 base-output tiles, TMA load; the updated
-//                values go back with coalesced 16-byte stores straight from registers).
+//   per unit   = d_in/64 "x chunks" (64x64 bf16 activation tiles, 128B swizzle)
+//              + d_out/64 "out chunks" (64x64 bf16 base-output tiles; the updated values go
+//                back with coalesced 16-byte stores straight from registers).
+//   stage      = two adjacent chunks of one unit, fetched by ONE TMA operation through a
+//                "chunked" 3-D view of the array (64 columns, rows, chunks; the chunk stride,
+//                128 B, is the outer dimension), so each op moves 16 KB.  On B200 the op count
+//                matters: streaming 8 KB boxes from one CTA per SM topped out near 33-37 GB/s
+//                per SM, 16 KB boxes reach ~42 GB/s (6.2 TB/s over 148 SMs).
 //   warps      = 8 consumer warps in 2 groups that take alternate pipeline positions (each
 //                group has 4 warps of 16 tokens; the groups add their partial x.A^T sums
-//                through shared memory before the expand), 1 TMA producer warp, 4 decoder warps.
-//   pipeline   = kStages shared-memory stages; each stage holds one 8 KB tile and the
-//                512 B decoded factor chunk that goes with it; full barrier = TMA bytes +
-//                one decoder arrival, empty barrier = one arrival per warp of the group.
+//                through shared memory before the expand), and kFeed feeder warps that take
+//                every kFeed-th position: each issues its positions' TMA loads (one lane) and
+//                decodes their factor chunks (the whole warp) while the loads are in flight.
+//   pipeline   = kStages shared-memory stages; each stage holds two 8 KB chunk tiles and the
+//                two 512 B decoded factor chunks that go with them; full barrier = TMA bytes +
+//                the feeder's arrival, empty barrier = one arrival per warp of the group.
 //
 // Decoded factors.  The codeword c_k has period 16 (device_common.cuh), so
 //   A_j[r, 64c + t] = a_{r,c}[t & 15]     (16 values per (rank row, 64-column chunk))
@@ -42,18 +49,17 @@ constexpr int kChunk = 64;              // columns per chunk
 constexpr int kGroupWarps = 4;                    // consumer warps per group (16 token rows each)
 constexpr int kGroups = 2;                        // consumer groups; group g takes positions pos % 2 == g
 constexpr int kConsumerWarps = kGroupWarps * kGroups;
-constexpr int kDecodeWarps = 4;
-constexpr int kProducerWarp = kConsumerWarps;
-constexpr int kFirstDecodeWarp = kConsumerWarps + 1;
-constexpr int kThreadsStaged = 32 * (kConsumerWarps + 1);                // staged mode: no decoder warps
-constexpr int kStages = 16;
-constexpr int kTileBytes = kBM * kChunk * 2;      // 8192
-constexpr int kFactBytes = 16 * 16 * 2;           // 512
+constexpr int kDecodeWarps = 4;                   // feeder warps of the fused form (they also decode)
+constexpr int kFeedStaged = 4;                    // feeder warps of the staged form (loads only)
+constexpr int kFirstFeedWarp = kConsumerWarps;
+constexpr int kStageChunks = 2;                   // 64-column chunks per stage (one TMA operation)
+constexpr int kStages = 8;
+constexpr int kTileBytes = kBM * kChunk * 2;      // 8192, one chunk
+constexpr int kFactBytes = 16 * 16 * 2;           // 512, one chunk's decoded factor
+constexpr int kStageBytes = kStageChunks * kTileBytes;
+constexpr int kStageFactBytes = kStageChunks * kFactBytes;
 constexpr int kLutFloats = 2 * LITHE_MAX_LEVELS * 16;
-constexpr int kXchgFloats = kConsumerWarps * 32 * 8;   // partial h of every consumer thread
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * (kTileBytes + kFactBytes) + sizeof(DecodeTables) +
-                              kXchgFloats * sizeof(float) + (2 * kStages + 2) * sizeof(uint64_t) +
-                              kLutFloats * sizeof(float) + 16;
+constexpr int kXchgFloats = kConsumerWarps * 32 * 8;   // partial h of every consumer thread (one buffer)
 
 struct SgmvParams {
     IndexView ia, ib;
@@ -64,6 +70,7 @@ struct SgmvParams {
     int32_t m, d_in, d_out;
     int32_t n_mtiles, n_xchunks, n_ochunks, total_units;
     int32_t accumulate;
+    int32_t out_pairs;          // 1: out tiles come as chunk pairs from a chunked map (d_out % 64 == 0)
     int32_t a_blocks_per_row;   // d_in / 64
     int32_t b_blocks;           // d_out * rank / 64
     float scaling;
@@ -78,19 +85,58 @@ struct Unit {
     int b, mt;
     int64_t slot;
     bool active;
-    int nx, no;
+    int nx, no;     // x chunks, out chunks
+    int sx, so;     // stages they take: ceil(nx / 2), ceil(no / 2)
 };
 
-__device__ __forceinline__ Unit unit_at(const SgmvParams& p, int u) {
+// The slot ids and weights of the samples a CTA's unit range touches, read once into shared
+// memory at kernel start, so that no role waits on a global load when it moves to its next
+// unit (those dependent loads stalled the pipeline at every unit boundary).  Samples beyond
+// the first kUnitCache of the range (only when units are tiny) are read from global memory.
+constexpr int kUnitCache = 128;
+struct UnitCache {
+    int32_t b0, n;
+    int32_t slot[kUnitCache];
+    float weight[kUnitCache];
+};
+
+__device__ __forceinline__ void fill_unit_cache(UnitCache* uc, const SgmvParams& p, int u_begin, int u_end, int tid,
+                                                int nthreads) {
+    const int b0 = u_begin / p.n_mtiles;
+    const int nb = u_end > u_begin ? (u_end - 1) / p.n_mtiles - b0 + 1 : 0;
+    const int n = nb < kUnitCache ? nb : kUnitCache;
+    if (tid == 0) {
+        uc->b0 = b0;
+        uc->n = n;
+    }
+    for (int i = tid; i < n; i += nthreads) {
+        uc->slot[i] = __ldg(p.ids + b0 + i);
+        uc->weight[i] = p.weights ? __ldg(p.weights + b0 + i) : 1.0f;
+    }
+}
+
+__device__ __forceinline__ Unit unit_at(const SgmvParams& p, const UnitCache* uc, int u) {
     Unit r;
     r.b = u / p.n_mtiles;
     r.mt = u - r.b * p.n_mtiles;
-    const int32_t sid = __ldg(p.ids + r.b);
+    const int i = r.b - uc->b0;
+    const int32_t sid = i < uc->n ? uc->slot[i] : __ldg(p.ids + r.b);
     r.slot = sid;
     r.active = sid >= 0 && static_cast<int64_t>(sid) < p.n_slots;
     r.nx = r.active ? p.n_xchunks : 0;
     r.no = (r.active || !p.accumulate) ? p.n_ochunks : 0;
+    r.sx = (r.nx + kStageChunks - 1) / kStageChunks;
+    r.so = (r.no + kStageChunks - 1) / kStageChunks;
     return r;
+}
+
+constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * (kStageBytes + kStageFactBytes) + sizeof(DecodeTables) +
+                              2 * kXchgFloats * sizeof(float) + (2 * kStages + 2) * sizeof(uint64_t) +
+                              kLutFloats * sizeof(float) + sizeof(UnitCache) + 16;
+
+__device__ __forceinline__ float unit_weight(const SgmvParams& p, const UnitCache* uc, int b) {
+    const int i = b - uc->b0;
+    return i < uc->n ? uc->weight[i] : (p.weights ? __ldg(p.weights + b) : 1.0f);
 }
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* a) { return *reinterpret_cast<const uint4*>(a); }
@@ -102,7 +148,7 @@ __device__ __forceinline__ uint32_t add_bf16x2(uint32_t w, float dlo, float dhi)
 }
 
 // ---------------------------------------------------------------------------------------
-// Decoder warps
+// Factor chunks (decoded by the feeder warps)
 // ---------------------------------------------------------------------------------------
 // Issue the index loads of the block this lane decodes in chunk c of a unit (A chunk
 // c < nx, else B chunk c - nx).  Returns false when the lane's values are structurally zero
@@ -177,99 +223,153 @@ __device__ __forceinline__ void decode_chunk(const SgmvParams& p, const DecodeTa
     for (int i = 0; i < 8; i += 2) dst[(i >> 1) * 2 + half] = pack_bf16x2(val[i], val[i + 1]);
 }
 
-// Decoder warp d fills the factor chunk of every pipeline position pos with
-// pos % kDecodeWarps == d.  The indices of its next chunk are fetched before it waits for
-// and decodes the current one, so the index-load latency overlaps the decode.
-template <int kRank, int kDec>
-__device__ void run_decoder(int d, int lane, const SgmvParams& p, uint8_t* facts, const DecodeTables* tab,
-                            const float* lut_s, uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin,
-                            int u_end) {
-    int u = u_begin, c = 0;          // cursor: unit, chunk within the unit
-    uint32_t pos = 0;                // pipeline position of (u, c)
+// The chunks of stage q of a unit, in the unit's chunk numbering (x chunks 0 .. nx-1, then
+// out chunks nx .. nx+no-1): the first one and how many (1 or 2).
+__device__ __forceinline__ void stage_chunks(const Unit& un, int q, int& c0, int& n) {
+    if (q < un.sx) {
+        c0 = kStageChunks * q;
+        n = un.nx - c0 < kStageChunks ? un.nx - c0 : kStageChunks;
+    } else {
+        const int j0 = kStageChunks * (q - un.sx);
+        c0 = un.nx + j0;
+        n = un.no - j0 < kStageChunks ? un.no - j0 : kStageChunks;
+    }
+}
+
+// Lane 0 of a feeder: the TMA load(s) of stage q's tiles into dst.  x chunks and, when
+// d_out % 64 == 0, out chunks come as one 16 KB op from the chunked maps (a missing second
+// chunk past the end reads as zeros); ragged out chunks come one 8 KB op each from a
+// per-chunk map.  Returns the bytes the loads deliver.
+__device__ __forceinline__ uint32_t load_stage_tiles(const SgmvParams& p, const CUtensorMap* tmx,
+                                                     const CUtensorMap* tmo, const Unit& un, int q, uint8_t* dst,
+                                                     uint64_t* bar, bool expect) {
+    int c0, n;
+    stage_chunks(un, q, c0, n);
+    const int row = un.b * p.m + un.mt * kBM;
+    const bool pair = q < un.sx || p.out_pairs;
+    const uint32_t bytes = pair ? static_cast<uint32_t>(kStageBytes) : static_cast<uint32_t>(n * kTileBytes);
+    if (expect) mbar_expect_tx(bar, bytes);
+    if (q < un.sx) {
+        tma_load_3d(dst, tmx, bar, 0, row, c0);
+    } else if (pair) {
+        tma_load_3d(dst, tmo, bar, 0, row, c0 - un.nx);
+    } else {
+        for (int k = 0; k < n; ++k) tma_load_3d(dst + k * kTileBytes, tmo, bar, (c0 - un.nx + k) * kChunk, row, 0);
+    }
+    return bytes;
+}
+
+// Feeder warp d (of kFeed) owns every pipeline position pos with pos % kFeed == d.  For each
+// one it waits until the stage is free, issues the stage's TMA load from lane 0 (the x tiles
+// of x chunks; the base-output tiles of out chunks when accumulating) and then, in the fused
+// form, decodes the stage's factor chunks while the load is in flight and arrives on the
+// stage's full barrier.  The staged form bulk-copies the chunks decode_chunks_kernel wrote
+// instead.  The index words of a warp's next stage are fetched before it waits for the
+// current one, so their load latency overlaps the wait and the decode.
+// Why several feeder warps: on B200 a CTA whose TMA loads all come from one thread streams
+// 8 KB boxes at about 20-25 GB/s per SM however deep its pipeline is; with the loads issued by
+// four to eight warps the same stream reaches 33-37 GB/s per SM (measured with a streaming
+// probe, 57344 x 3072 bf16, one CTA per SM).
+// Returns one past the last position this warp issued (all of them have arrived).
+template <int kRank, bool kStaged, int kFeed>
+__device__ uint32_t run_feeder(int d, int lane, const SgmvParams& p, const UnitCache* uc, const CUtensorMap* tmx,
+                               const CUtensorMap* tmo, uint8_t* tiles, uint8_t* facts, const DecodeTables* tab,
+                               const float* lut_s, uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin,
+                               int u_end) {
+    int u = u_begin, q = 0;          // cursor: unit, stage within the unit
+    uint32_t pos = 0;                // pipeline position of (u, q)
     Unit un;
     // Move to the next position owned by this warp (the current one when first == true).
     auto seek = [&](bool first) {
         if (!first) {
-            ++c;
+            ++q;
             ++pos;
         }
         while (u < u_end) {
-            if (first || c == 0) un = unit_at(p, u);
+            if (first || q == 0) un = unit_at(p, uc, u);
             first = false;
-            const int n = un.nx + un.no;
-            if (c < n) {
-                const int skip = (d - static_cast<int>(pos % kDec) + kDec) % kDec;
-                if (c + skip < n) {
-                    c += skip;
+            const int n = un.sx + un.so;
+            if (q < n) {
+                const int skip = (d - static_cast<int>(pos % kFeed) + kFeed) % kFeed;
+                if (q + skip < n) {
+                    q += skip;
                     pos += skip;
                     return true;
                 }
-                pos += n - c;
+                pos += n - q;
             }
             ++u;
-            c = 0;
+            q = 0;
         }
         return false;
     };
+    uint32_t issued = 0;
     bool have = seek(true);
-    RawIndices<LITHE_MAX_LEVELS> raw_next;
-    bool live_next = have && un.active && chunk_fetch<kRank>(p, un, c, lane, raw_next);
+    RawIndices<LITHE_MAX_LEVELS> raw_next[kStageChunks];
+    bool live_next[kStageChunks];
+    auto fetch_next = [&]() {
+        int c0 = 0, n = 0;
+        if (have && un.active) stage_chunks(un, q, c0, n);
+#pragma unroll
+        for (int k = 0; k < kStageChunks; ++k)
+            live_next[k] = k < n && chunk_fetch<kRank>(p, un, c0 + k, lane, raw_next[k]);
+    };
+    if constexpr (!kStaged) fetch_next();
     while (have) {
         const Unit cur = un;
-        const int cc = c;
+        const int cq = q;
         const uint32_t cpos = pos;
-        const RawIndices<LITHE_MAX_LEVELS> raw = raw_next;
-        const bool live = live_next;
-        // loads of the next chunk go out now and are unpacked only one iteration later
+        RawIndices<LITHE_MAX_LEVELS> raw[kStageChunks];
+        bool live[kStageChunks];
+#pragma unroll
+        for (int k = 0; k < kStageChunks; ++k) {
+            raw[k] = raw_next[k];
+            live[k] = live_next[k];
+        }
         have = seek(false);
-        live_next = have && un.active && chunk_fetch<kRank>(p, un, c, lane, raw_next);
+        // loads of the next stage go out now and are unpacked only one iteration later
+        if constexpr (!kStaged) fetch_next();
 
         const uint32_t s = cpos % kStages, ph = (cpos / kStages) & 1u;
-        if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return;
-        if (cur.active) {
-            uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
-            if (live) finish_raw<LITHE_MAX_LEVELS>(cc < cur.nx ? p.ia : p.ib, raw, k, p.err);
-            decode_chunk<kRank>(p, tab, lut_s, cur, cc, live, k, facts + s * kFactBytes, lane);
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&full[s]);
-    }
-}
-
-// ---------------------------------------------------------------------------------------
-// Producer (one lane)
-// ---------------------------------------------------------------------------------------
-// Staged mode: the producer also bulk-copies the unit's decoded factor chunk (512 B, written
-// by decode_chunks_kernel) into the stage, so one arrival + the TMA bytes complete a stage.
-template <bool kStaged>
-__device__ uint32_t run_producer(const SgmvParams& p, const CUtensorMap* tmx, const CUtensorMap* tmo,
-                                 uint8_t* tiles, uint8_t* facts, uint64_t* full, uint64_t* empty, volatile int* abort,
-                                 int u_begin, int u_end) {
-    uint32_t pos = 0;
-    for (int u = u_begin; u < u_end; ++u) {
-        const Unit un = unit_at(p, u);
-        if (!un.active && un.slot >= p.n_slots && p.err) atomicOr(p.err, LITHE_DEVERR_SLOT);
-        const int n = un.nx + un.no;
-        for (int c = 0; c < n; ++c, ++pos) {
-            const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
-            if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return pos;
-            uint8_t* dst = tiles + s * kTileBytes;
-            const bool tile = c < un.nx || p.accumulate;
-            const bool fact = kStaged && un.active;
-            const uint32_t bytes = (tile ? kTileBytes : 0u) + (fact ? static_cast<uint32_t>(kFactBytes) : 0u);
-            if (bytes == 0) {
-                mbar_arrive(&full[s]);
-                continue;
+        if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return issued;
+        const bool tile = cq < cur.sx || p.accumulate;
+        uint8_t* dst = tiles + s * kStageBytes;
+        uint8_t* fdst = facts + s * kStageFactBytes;
+        int c0, n;
+        stage_chunks(cur, cq, c0, n);
+        if constexpr (kStaged) {
+            if (lane == 0) {
+                const uint32_t fbytes = cur.active ? static_cast<uint32_t>(n * kFactBytes) : 0u;
+                if (!tile && fbytes == 0) {
+                    mbar_arrive(&full[s]);
+                } else {
+                    if (tile) load_stage_tiles(p, tmx, tmo, cur, cq, dst, &full[s], true);
+                    if (fbytes) {
+                        mbar_expect_tx(&full[s], fbytes);
+                        bulk_load_1d(fdst, p.ws + (static_cast<int64_t>(cur.b) * p.n_chunks + c0) * kFactBytes,
+                                     fbytes, &full[s]);
+                    }
+                    mbar_arrive(&full[s]);
+                }
             }
-            mbar_arrive_expect_tx(&full[s], bytes);
-            if (c < un.nx) tma_load_3d(dst, tmx, &full[s], c * kChunk, un.b * p.m + un.mt * kBM, 0);
-            else if (p.accumulate) tma_load_3d(dst, tmo, &full[s], (c - un.nx) * kChunk, un.b * p.m + un.mt * kBM, 0);
-            if (fact)
-                bulk_load_1d(facts + s * kFactBytes,
-                             p.ws + (static_cast<int64_t>(un.b) * p.n_chunks + c) * kFactBytes, kFactBytes, &full[s]);
+        } else {
+            if (lane == 0 && tile) load_stage_tiles(p, tmx, tmo, cur, cq, dst, &full[s], true);
+            if (cur.active) {
+#pragma unroll
+                for (int k = 0; k < kStageChunks; ++k) {
+                    if (k < n) {
+                        uint32_t kk[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
+                        if (live[k]) finish_raw<LITHE_MAX_LEVELS>(c0 + k < cur.nx ? p.ia : p.ib, raw[k], kk, p.err);
+                        decode_chunk<kRank>(p, tab, lut_s, cur, c0 + k, live[k], kk, fdst + k * kFactBytes, lane);
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&full[s]);
         }
+        issued = cpos + 1;
     }
-    return pos;
+    return issued;
 }
 
 // ---------------------------------------------------------------------------------------
@@ -294,9 +394,9 @@ __device__ __forceinline__ uint4 add_delta8(uint4 v, float c0, float c1) {
 }
 
 template <int kRank>
-__device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tiles, const uint8_t* facts,
-                             uint64_t* full, uint64_t* empty, float* xchg, uint64_t* xbar, volatile int* abort,
-                             int u_begin, int u_end) {
+__device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCache* uc, uint8_t* tiles,
+                             const uint8_t* facts, uint64_t* full, uint64_t* empty, float* xchg, uint64_t* xbar,
+                             volatile int* abort, int u_begin, int u_end) {
     const int grp = w / kGroupWarps;     // this warp's group: positions pos % kGroups == grp
     const int wr = w % kGroupWarps;      // row block within the tile
     const int g = lane >> 2, t4 = lane & 3;
@@ -306,12 +406,13 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
     // four and conflict 2-way).  Rank / logical-column indices stay on g.
     const int gr = (g >> 1) | ((g & 1) << 2);
     const int r0 = 16 * wr + gr;         // rows r0 and r0 + 8 of the 64-token tile
-    uint32_t n_xchg = 0;                 // exchanges done (mbarrier phase parity)
+    uint32_t n_xchg = 0;                 // exchanges done (buffer = n_xchg & 1, phase = (n_xchg >> 1) & 1)
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
     const bool accum = p.accumulate != 0;
     uint32_t pos = 0;
     for (int u = u_begin; u < u_end; ++u) {
-        const Unit un = unit_at(p, u);
+        const Unit un = unit_at(p, uc, u);
+        if (w == 0 && lane == 0 && !un.active && un.slot >= p.n_slots && p.err) atomicOr(p.err, LITHE_DEVERR_SLOT);
         if (un.nx + un.no == 0) {
             if (p.h_out && grp == 0) {              // unrouted sample: its h rows are zero
 #pragma unroll
@@ -330,33 +431,40 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
         float acc[2][2][4];
 #pragma unroll
         for (int i = 0; i < 16; ++i) (&acc[0][0][0])[i] = 0.f;
-        for (int c = 0; c < un.nx; ++c, ++pos) {
+        for (int q = 0; q < un.sx; ++q, ++pos) {
             if (static_cast<int>(pos % kGroups) != grp) continue;
             const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
             if (!mbar_wait(&full[s], ph, abort, p.err)) return;
-            const uint8_t* tile = tiles + s * kTileBytes;
-            const uint8_t* fa = facts + s * kFactBytes;
-            const uint8_t* ra = tile + r0 * 128;
-            const uint8_t* rb = ra + 8 * 128;
-            const uint4 f0 = lds128(fa + g * 32 + (t4 & 1) * 16);
-            const uint4 f1 = lds128(fa + (g + 8) * 32 + (t4 & 1) * 16);
 #pragma unroll
-            for (int win = 0; win < 2; ++win) {
-                const uint4 xa = lds128(ra + (((4 * win + t4) ^ gr) << 4));
-                const uint4 xb = lds128(rb + (((4 * win + t4) ^ gr) << 4));
-                const uint32_t a0[4] = {xa.x, xb.x, xa.y, xb.y};
-                const uint32_t a1[4] = {xa.z, xb.z, xa.w, xb.w};
-                mma_bf16_16816(acc[0][win], a0, f0.x, f0.y, acc[0][win]);
-                mma_bf16_16816(acc[1][win], a0, f1.x, f1.y, acc[1][win]);
-                mma_bf16_16816(acc[0][win], a1, f0.z, f0.w, acc[0][win]);
-                mma_bf16_16816(acc[1][win], a1, f1.z, f1.w, acc[1][win]);
+            for (int k = 0; k < kStageChunks; ++k) {
+                if (kStageChunks * q + k >= un.nx) break;
+                const uint8_t* tile = tiles + s * kStageBytes + k * kTileBytes;
+                const uint8_t* fa = facts + s * kStageFactBytes + k * kFactBytes;
+                const uint8_t* ra = tile + r0 * 128;
+                const uint8_t* rb = ra + 8 * 128;
+                const uint4 f0 = lds128(fa + g * 32 + (t4 & 1) * 16);
+                const uint4 f1 = lds128(fa + (g + 8) * 32 + (t4 & 1) * 16);
+#pragma unroll
+                for (int win = 0; win < 2; ++win) {
+                    const uint4 xa = lds128(ra + (((4 * win + t4) ^ gr) << 4));
+                    const uint4 xb = lds128(rb + (((4 * win + t4) ^ gr) << 4));
+                    const uint32_t a0[4] = {xa.x, xb.x, xa.y, xb.y};
+                    const uint32_t a1[4] = {xa.z, xb.z, xa.w, xb.w};
+                    mma_bf16_16816(acc[0][win], a0, f0.x, f0.y, acc[0][win]);
+                    mma_bf16_16816(acc[1][win], a0, f1.x, f1.y, acc[1][win]);
+                    mma_bf16_16816(acc[0][win], a1, f0.z, f0.w, acc[0][win]);
+                    mma_bf16_16816(acc[1][win], a1, f1.z, f1.w, acc[1][win]);
+                }
             }
             __syncwarp();
             if (lane == 0) mbar_arrive(&empty[s]);
         }
         // The two groups each saw half of the x chunks: add the partner warp's partial h
-        // (same rows, other group) through shared memory.  xbar[0] = partials written,
-        // xbar[1] = partials read; both count one arrival per consumer warp.
+        // (same rows, other group) through shared memory.  The exchange buffer and its
+        // mbarrier alternate between two copies by unit, so one barrier per unit suffices: a
+        // warp rewrites copy k only at exchange k + 2, after every warp has arrived at
+        // exchange k + 1, which each does only after reading its partner's values of
+        // exchange k.  (fp32 addition commutes, so both partners form the same sum.)
         float part[8];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -364,23 +472,22 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
             part[4 + i] = acc[1][0][i] + acc[1][1][i];
         }
         {
-            float4* mine = reinterpret_cast<float4*>(xchg + (w * 32 + lane) * 8);
+            float* buf = xchg + (n_xchg & 1u) * kXchgFloats;
+            uint64_t* bar = &xbar[n_xchg & 1u];
+            float4* mine = reinterpret_cast<float4*>(buf + (w * 32 + lane) * 8);
             mine[0] = make_float4(part[0], part[1], part[2], part[3]);
             mine[1] = make_float4(part[4], part[5], part[6], part[7]);
             __syncwarp();
-            if (lane == 0) mbar_arrive(&xbar[0]);
-            if (!mbar_wait(&xbar[0], n_xchg & 1u, abort, p.err)) return;
+            if (lane == 0) mbar_arrive(bar);
+            if (!mbar_wait(bar, (n_xchg >> 1) & 1u, abort, p.err)) return;
             const int partner = (w + kGroupWarps) % kConsumerWarps;
-            const float4* other = reinterpret_cast<const float4*>(xchg + (partner * 32 + lane) * 8);
+            const float4* other = reinterpret_cast<const float4*>(buf + (partner * 32 + lane) * 8);
             const float4 o0 = other[0], o1 = other[1];
             part[0] += o0.x; part[1] += o0.y; part[2] += o0.z; part[3] += o0.w;
             part[4] += o1.x; part[5] += o1.y; part[6] += o1.z; part[7] += o1.w;
-            __syncwarp();
-            if (lane == 0) mbar_arrive(&xbar[1]);
-            if (!mbar_wait(&xbar[1], n_xchg & 1u, abort, p.err)) return;
             ++n_xchg;
         }
-        const float sc = p.scaling * (p.weights ? __ldg(p.weights + un.b) : 1.0f);
+        const float sc = p.scaling * unit_weight(p, uc, un.b);
         float h0[4], h1[4];
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
@@ -406,80 +513,91 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
             continue;
         }
         __nv_bfloat16* out_b = p.out + static_cast<int64_t>(un.b) * p.m * p.d_out;
-        for (int j = 0; j < un.no; ++j, ++pos) {
+        for (int q = 0; q < un.so; ++q, ++pos) {
             if (static_cast<int>(pos % kGroups) != grp) continue;
             const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
             if (!mbar_wait(&full[s], ph, abort, p.err)) return;
-            const uint8_t* tile = tiles + s * kTileBytes;
-            float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
-            if (un.active) {
-                const uint8_t* fb = facts + s * kFactBytes;
-                const uint2 b0 = *reinterpret_cast<const uint2*>(fb + g * 32 + t4 * 8);
-                const uint2 b1 = *reinterpret_cast<const uint2*>(fb + (g + 8) * 32 + t4 * 8);
-                mma_bf16_16816(d[0], ha, b0.x, b0.y, zero);
-                mma_bf16_16816(d[1], ha, b1.x, b1.y, zero);
-            }
-            const int col0 = j * kChunk;
-            if constexpr (kRank >= 8) {
-                uint4 v[2][2];          // [n8 tile q][row half]
+            const int n = un.no - kStageChunks * q < kStageChunks ? un.no - kStageChunks * q : kStageChunks;
 #pragma unroll
-                for (int q = 0; q < 2; ++q)
+            for (int k = 0; k < kStageChunks; ++k) {
+                if (k >= n) break;
+                const bool release = k == n - 1;      // the stage is free once its last tile is in registers
+                const int j = kStageChunks * q + k;
+                const uint8_t* tile = tiles + s * kStageBytes + k * kTileBytes;
+                float d[2][4] = {{0.f, 0.f, 0.f, 0.f}, {0.f, 0.f, 0.f, 0.f}};
+                if (un.active) {
+                    const uint8_t* fb = facts + s * kStageFactBytes + k * kFactBytes;
+                    const uint2 b0 = *reinterpret_cast<const uint2*>(fb + g * 32 + t4 * 8);
+                    const uint2 b1 = *reinterpret_cast<const uint2*>(fb + (g + 8) * 32 + t4 * 8);
+                    mma_bf16_16816(d[0], ha, b0.x, b0.y, zero);
+                    mma_bf16_16816(d[1], ha, b1.x, b1.y, zero);
+                }
+                const int col0 = j * kChunk;
+                if constexpr (kRank >= 8) {
+                    uint4 v[2][2];          // [n8 tile q][row half]
+#pragma unroll
+                    for (int qq = 0; qq < 2; ++qq)
+#pragma unroll
+                        for (int hr = 0; hr < 2; ++hr) {
+                            const uint4 o = accum ? lds128(tile + (r0 + 8 * hr) * 128 + ((((qq << 2) + t4) ^ gr) << 4))
+                                                  : make_uint4(0, 0, 0, 0);
+                            v[qq][hr] = add_delta8<kRank>(o, d[qq][2 * hr], d[qq][2 * hr + 1]);
+                        }
+                    if (release) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[s]);
+                    }
 #pragma unroll
                     for (int hr = 0; hr < 2; ++hr) {
-                        const uint4 o = accum ? lds128(tile + (r0 + 8 * hr) * 128 + ((((q << 2) + t4) ^ gr) << 4))
-                                              : make_uint4(0, 0, 0, 0);
-                        v[q][hr] = add_delta8<kRank>(o, d[q][2 * hr], d[q][2 * hr + 1]);
-                    }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
+                        const int row = row0 + 8 * hr;
+                        if (row < p.m) {
 #pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                    const int row = row0 + 8 * hr;
-                    if (row < p.m) {
-#pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const int col = col0 + 32 * q + 8 * t4;
-                            if (col < p.d_out)   // streaming store: out is not re-read by this launch
-                                __stcs(reinterpret_cast<uint4*>(out_b + static_cast<int64_t>(row) * p.d_out + col),
-                                       v[q][hr]);
+                            for (int qq = 0; qq < 2; ++qq) {
+                                const int col = col0 + 32 * qq + 8 * t4;
+                                if (col < p.d_out)   // streaming store: out is not re-read by this launch
+                                    __stcs(reinterpret_cast<uint4*>(out_b + static_cast<int64_t>(row) * p.d_out + col),
+                                           v[qq][hr]);
+                            }
                         }
                     }
-                }
-            } else {
-                constexpr int kPer = 16 / kRank;        // logical columns per block
-                uint32_t v[2][2][4];                    // [q][row half][pp]
+                } else {
+                    constexpr int kPer = 16 / kRank;        // logical columns per block
+                    uint32_t v[2][2][4];                    // [qq][row half][pp]
 #pragma unroll
-                for (int q = 0; q < 2; ++q) {
-                    const int nl = 8 * q + 2 * t4;      // local logical column of c0
-                    const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
+                    for (int qq = 0; qq < 2; ++qq) {
+                        const int nl = 8 * qq + 2 * t4;     // local logical column of c0
+                        const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
 #pragma unroll
-                    for (int hr = 0; hr < 2; ++hr)
-#pragma unroll
-                        for (int pp = 0; pp < 4; ++pp) {
-                            const int col = base + pp * kPer;   // even: c0 at col, c1 at col + 1
-                            const uint32_t o = accum ? *reinterpret_cast<const uint32_t*>(
-                                                           tile + (r0 + 8 * hr) * 128 + (((col >> 3) ^ gr) << 4) +
-                                                           (col & 7) * 2)
-                                                     : 0u;
-                            v[q][hr][pp] = add_bf16x2(o, d[q][2 * hr], d[q][2 * hr + 1]);
-                        }
-                }
-                __syncwarp();
-                if (lane == 0) mbar_arrive(&empty[s]);
-#pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                    const int row = row0 + 8 * hr;
-                    if (row < p.m) {
-#pragma unroll
-                        for (int q = 0; q < 2; ++q) {
-                            const int nl = 8 * q + 2 * t4;
-                            const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
+                        for (int hr = 0; hr < 2; ++hr)
 #pragma unroll
                             for (int pp = 0; pp < 4; ++pp) {
-                                const int col = col0 + base + pp * kPer;
-                                if (col < p.d_out)
-                                    *reinterpret_cast<uint32_t*>(out_b + static_cast<int64_t>(row) * p.d_out + col) =
-                                        v[q][hr][pp];
+                                const int col = base + pp * kPer;   // even: c0 at col, c1 at col + 1
+                                const uint32_t o = accum ? *reinterpret_cast<const uint32_t*>(
+                                                               tile + (r0 + 8 * hr) * 128 + (((col >> 3) ^ gr) << 4) +
+                                                               (col & 7) * 2)
+                                                         : 0u;
+                                v[qq][hr][pp] = add_bf16x2(o, d[qq][2 * hr], d[qq][2 * hr + 1]);
+                            }
+                    }
+                    if (release) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[s]);
+                    }
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
+                        const int row = row0 + 8 * hr;
+                        if (row < p.m) {
+#pragma unroll
+                            for (int qq = 0; qq < 2; ++qq) {
+                                const int nl = 8 * qq + 2 * t4;
+                                const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
+#pragma unroll
+                                for (int pp = 0; pp < 4; ++pp) {
+                                    const int col = col0 + base + pp * kPer;
+                                    if (col < p.d_out)
+                                        *reinterpret_cast<uint32_t*>(out_b + static_cast<int64_t>(row) * p.d_out + col) =
+                                            v[qq][hr][pp];
+                                }
                             }
                         }
                     }
@@ -489,26 +607,33 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, uint8_t* tile
     }
 }
 
-template <int kRank, bool kStaged, int kDec>
-__global__ void __launch_bounds__(kStaged ? kThreadsStaged : 32 * (kConsumerWarps + 1 + kDec), 1)
+template <int kRank, bool kStaged, int kFeed>
+__global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
     sgmv_index_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmo_ld,
                       const __grid_constant__ SgmvParams p) {
+    // Every pipeline wait is a parity wait, which is only correct when the waiter is at most
+    // one phase ahead of the barrier.  That holds when the warp (or group) waiting for position
+    // pos also owned position pos - kStages on the same stage, i.e. when the owners' counts
+    // divide kStages; otherwise two feeders could share a stage in different phases.
+    static_assert(kStages % kFeed == 0, "each feeder warp must own whole stages");
+    static_assert(kStages % kGroups == 0, "each consumer group must own whole stages");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* tiles = base;
-    uint8_t* facts = tiles + kStages * kTileBytes;
-    DecodeTables* tab = reinterpret_cast<DecodeTables*>(facts + kStages * kFactBytes);
-    float* xchg = reinterpret_cast<float*>(tab + 1);
-    uint64_t* full = reinterpret_cast<uint64_t*>(xchg + kXchgFloats);
+    uint8_t* facts = tiles + kStages * kStageBytes;
+    DecodeTables* tab = reinterpret_cast<DecodeTables*>(facts + kStages * kStageFactBytes);
+    float* xchg = reinterpret_cast<float*>(tab + 1);                       // 2 x kXchgFloats
+    uint64_t* full = reinterpret_cast<uint64_t*>(xchg + 2 * kXchgFloats);
     uint64_t* empty = full + kStages;
     uint64_t* xbar = empty + kStages;
     float* lut_s = reinterpret_cast<float*>(xbar + 2);
-    volatile int* abort = reinterpret_cast<volatile int*>(lut_s + kLutFloats);
+    UnitCache* uc = reinterpret_cast<UnitCache*>(lut_s + kLutFloats);
+    volatile int* abort = reinterpret_cast<volatile int*>(uc + 1);
 
     const int tid = threadIdx.x;
     if (tid == 0) {
         for (int s = 0; s < kStages; ++s) {
-            mbar_init(&full[s], kStaged ? 1 : 2);   // producer (+ one decoder warp in fused mode)
+            mbar_init(&full[s], 1);                 // the owning feeder's arrival (+ the TMA bytes)
             mbar_init(&empty[s], kGroupWarps);      // one arrival per warp of the consuming group
         }
         mbar_init(&xbar[0], kConsumerWarps);
@@ -516,36 +641,37 @@ __global__ void __launch_bounds__(kStaged ? kThreadsStaged : 32 * (kConsumerWarp
         *abort = 0;
         fence_mbar_init();
     }
+    const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_units / gridDim.x);
+    const int u_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.total_units / gridDim.x);
+    fill_unit_cache(uc, p, u_begin, u_end, tid, blockDim.x);
     if constexpr (!kStaged) {
         for (int i = tid; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
         build_decode_tables(tab, &p.lut[0][0][0], p.ia.levels, tid, blockDim.x);
     }
     __syncthreads();
-
-    const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_units / gridDim.x);
-    const int u_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.total_units / gridDim.x);
     const int warp = tid >> 5, lane = tid & 31;
 
     uint32_t issued = 0;
     if (warp < kConsumerWarps) {
-        run_consumer<kRank>(warp, lane, p, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end);
-    } else if (warp == kProducerWarp) {
+        run_consumer<kRank>(warp, lane, p, uc, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end);
+    } else {
         if (lane == 0) {
             prefetch_tmap(&tmx);
             prefetch_tmap(&tmo_ld);
-            issued = run_producer<kStaged>(p, &tmx, &tmo_ld, tiles, facts, full, empty, abort, u_begin, u_end);
         }
-    } else if constexpr (!kStaged) {
-        run_decoder<kRank, kDec>(warp - kFirstDecodeWarp, lane, p, facts, tab, lut_s, full, empty, abort, u_begin,
-                                 u_end);
+        issued = run_feeder<kRank, kStaged, kFeed>(warp - kFirstFeedWarp, lane, p, uc, &tmx, &tmo_ld, tiles, facts,
+                                                   tab, lut_s, full, empty, abort, u_begin, u_end);
     }
     __syncthreads();
-    // After an aborted pipeline, let the producer's last TMA loads land before the block's
-    // shared memory is released (bounded: loads complete in microseconds).
-    if (*abort && warp == kProducerWarp && lane == 0) {
+    // After an aborted pipeline, let every feeder's last TMA loads land before the block's
+    // shared memory is released (bounded: loads complete in microseconds).  Each of its
+    // issued positions has its arrival, so the full barrier completes once the bytes are in.
+    if (*abort && warp >= kFirstFeedWarp && lane == 0) {
+        const uint32_t d = static_cast<uint32_t>(warp - kFirstFeedWarp);
         const uint64_t t0 = global_timer_ns();
         const uint32_t first = issued > static_cast<uint32_t>(kStages) ? issued - kStages : 0u;
         for (uint32_t q = first; q < issued; ++q) {
+            if (q % kFeed != d) continue;
             const uint32_t s = q % kStages, ph = (q / kStages) & 1u;
             while (!mbar_try_wait(&full[s], ph) && global_timer_ns() - t0 < 20000000ull) {
             }
@@ -635,11 +761,11 @@ __global__ void __launch_bounds__(256) decode_bdec_kernel(const __grid_constant_
     }
 }
 
-template <int kRank, bool kStaged, int kDec = kDecodeWarps>
+template <int kRank, bool kStaged, int kFeed = kStaged ? kFeedStaged : kDecodeWarps>
 static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, const SgmvParams& p, int grid,
                            int device, int sms, int32_t batch, uint8_t* ws, cudaStream_t stream) {
     static bool configured[64] = {false};
-    auto kern = sgmv_index_kernel<kRank, kStaged, kDec>;
+    auto kern = sgmv_index_kernel<kRank, kStaged, kFeed>;
     if (!configured[device]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmemBytes));
@@ -654,7 +780,7 @@ static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, co
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "decode_chunks_kernel launch");
     }
-    kern<<<grid, kStaged ? kThreadsStaged : 32 * (kConsumerWarps + 1 + kDec), kSmemBytes, stream>>>(tmx, tmo_ld, p);
+    kern<<<grid, 32 * (kConsumerWarps + kFeed), kSmemBytes, stream>>>(tmx, tmo_ld, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "sgmv_index_kernel launch");
     return LITHE_OK;
@@ -940,15 +1066,23 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
 
     CUtensorMap tmx, tmo_ld;
     // Tensor maps over the flattened (batch * m) rows: measured on B200, a (d, m, batch) map
-    // with a (64, 64, 1) box streams about 15% slower than a 2-D map over the same rows.  The
+    // with a (64, 64, 1) box streams about 15% slower than a map over the same rows.  The
     // last tile of a sample may then read the next sample's first rows; those rows are never
     // stored (stores are bounded by the sample's own m), and rows past the tensor read zeros.
-    rc = encode_bf16_3d(&tmx, x, d_in, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
+    // x and, when d_out % 64 == 0, out are read as chunk pairs through chunked maps (one
+    // 16 KB TMA op per stage); a ragged d_out is read one 64-column chunk per op.
+    const uint64_t rows_total = static_cast<uint64_t>(m) * batch;
+    rc = encode_bf16_chunked(&tmx, x, d_in, rows_total, kBM, kStageChunks);
     if (rc != LITHE_OK) return rc;
+    p.out_pairs = 0;
     if (prep) {
         tmo_ld = tmx;                 // no out tiles in shrink-only mode
+    } else if (d_out % kChunk == 0) {
+        rc = encode_bf16_chunked(&tmo_ld, out, d_out, rows_total, kBM, kStageChunks);
+        if (rc != LITHE_OK) return rc;
+        p.out_pairs = 1;
     } else {
-        rc = encode_bf16_3d(&tmo_ld, out, d_out, static_cast<uint64_t>(m) * batch, 1, kChunk, kBM);
+        rc = encode_bf16_3d(&tmo_ld, out, d_out, rows_total, 1, kChunk, kBM);
         if (rc != LITHE_OK) return rc;
     }
 
