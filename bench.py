@@ -42,7 +42,7 @@ BATCH, TOKENS, RANK, LEVELS = 14, 4096 + 512, 16, 3
 BANK_SLOTS = 10_000
 METRIC = "SGMV tokens/s at B=14 FLUX shapes"
 FALLBACK_HBM_GBS = 6650.0
-CPU_SAMPLE_TOKENS = 256
+CPU_SAMPLE_TOKENS = TOKENS          # the CPU baseline times whole samples of the workload
 
 
 def algorithmic_bytes(d_in: int, d_out: int, batch: int = BATCH, m: int = TOKENS, distinct: int = BATCH,
@@ -169,20 +169,25 @@ def traffic_per_launch():
 
 
 # --------------------------------------------------------------------------------------- CPU arm
-def cpu_reference_rate(seconds: float, seed: int = 0):
-    """Tokens/s of the oracle port of serve.py's forward (LoRA path: decode + bmm + add) on the
-    host cores, over a bounded sample: 1 sample x CPU_SAMPLE_TOKENS tokens of every shape, fp32."""
+def cpu_reference_passes(n_passes: int, warmup: int = 2, seed: int = 0) -> dict:
+    """The reference's CPU path on the host cores: the oracle port of serve.py's routed forward
+    (decode of the sample's adapter in fp32, bmm, bmm, out + delta) over one full sample of the
+    workload -- 1 sample x 4608 tokens, fp32 -- of each of the four shapes per pass.  Every pass
+    is timed on its own; the rate is tokens / median pass time, with the fastest and slowest
+    pass as the spread.  Both bench arms call this with the same pass counts, so the reference
+    arm's value and the GPU arm's cpu_baseline measure the same thing."""
     from oracle import codebook_ref, sgmv_ref
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
     pa, pb = codebook_ref.twin_pools()
     rng = np.random.default_rng(seed)
     cases = []
+    gen = torch.Generator().manual_seed(seed)
     for d_in, d_out in SHAPES:
         bank_a = rng.integers(0, 512, (1, LEVELS, RANK * d_in // 64))
         bank_b = rng.integers(0, 512, (1, LEVELS, d_out * RANK // 64))
-        x = torch.randn(1, CPU_SAMPLE_TOKENS, d_in, generator=torch.Generator().manual_seed(seed))
-        base = torch.randn(1, CPU_SAMPLE_TOKENS, d_out, generator=torch.Generator().manual_seed(seed + 1))
+        x = torch.randn(1, CPU_SAMPLE_TOKENS, d_in, generator=gen)
+        base = torch.randn(1, CPU_SAMPLE_TOKENS, d_out, generator=gen)
         cases.append((x, base, bank_a, bank_b, d_out))
     ids, w = sgmv_ref.routes_to_tables([[(0, 1.0)]])
 
@@ -190,40 +195,38 @@ def cpu_reference_rate(seconds: float, seed: int = 0):
         for x, base, ba, bb, d_out in cases:
             sgmv_ref.serve_forward(base, x, ba, bb, [1.0], ids, w, RANK, d_out, pa, pb)
 
-    one_pass()                                   # warm-up
-    passes, t0 = 0, time.perf_counter()
-    while True:
+    for _ in range(max(1, warmup)):
         one_pass()
-        passes += 1
-        el = time.perf_counter() - t0
-        if el >= seconds:
-            break
-    tokens = passes * len(SHAPES) * CPU_SAMPLE_TOKENS
-    return tokens / el, threads, passes, el
+    times = []
+    for _ in range(max(1, n_passes)):
+        t0 = time.perf_counter()
+        one_pass()
+        times.append(time.perf_counter() - t0)
+    tokens = len(SHAPES) * CPU_SAMPLE_TOKENS
+    med = statistics.median(times)
+    return {"value": tokens / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+            "spread": {"min": tokens / max(times), "median": tokens / med, "max": tokens / min(times)},
+            "passes": len(times), "pass_ms_median": 1000.0 * med,
+            "sample": f"oracle port of lithe/serve.py MultiAdapterLinear forward, fp32, {threads} host threads: "
+                      f"1 sample x {CPU_SAMPLE_TOKENS} tokens of each of the 4 shapes per pass, {len(times)} passes "
+                      f"timed one by one after {max(1, warmup)} warm-up passes, rate = tokens / median pass"}
 
 
 def run_reference(args):
     world, rank, _ = dist_env()
     if rank != 0:
         return
-    seconds_per_step = max(0.5, min(10.0, 60.0 / max(1, args.steps + args.warmup)))
-    for _ in range(args.warmup):
-        cpu_reference_rate(seconds_per_step / 4)
-    rates = []
-    for _ in range(args.steps):
-        rate, threads, passes, el = cpu_reference_rate(seconds_per_step)
-        rates.append(rate)
-    value = statistics.median(rates)
-    sample = (f"1 sample x {CPU_SAMPLE_TOKENS} tokens of each of the 4 shapes per pass, fp32, "
-              f"~{seconds_per_step:.1f} s of passes per step")
+    cpu = cpu_reference_passes(args.steps, warmup=args.warmup)
+    value = cpu["value"]
     line = {
         "impl": "reference", "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": args.gpus,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1000.0 * len(SHAPES) * CPU_SAMPLE_TOKENS / value,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": cpu["pass_ms_median"],
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded uniform 9-bit indices, x ~ N(0,1)",
         "config": {"workload": "flux_sweep_b14", "shapes": SHAPES, "batch": BATCH, "tokens_per_sample": TOKENS,
-                   "rank": RANK, "path": "oracle port of lithe/serve.py MultiAdapterLinear (torch CPU)"},
-        "cpu_baseline": {"value": value, "unit": "tokens/s", "cores": threads, "kind": "port", "sample": sample},
+                   "rank": RANK, "path": "oracle port of lithe/serve.py MultiAdapterLinear (torch CPU)",
+                   "step": "one pass: 1 sample x 4608 tokens of each of the 4 shapes"},
+        "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -355,10 +358,7 @@ def run_lithe(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        rate, threads, passes, el = cpu_reference_rate(args.cpu_seconds)
-        cpu = {"value": rate, "unit": "tokens/s", "cores": threads, "kind": "port",
-               "sample": f"oracle port of serve.py forward, fp32, 1 sample x {CPU_SAMPLE_TOKENS} tokens of each "
-                         f"of the 4 shapes, {passes} passes in {el:.1f} s"}
+        cpu = cpu_reference_passes(args.steps, warmup=args.warmup)
 
     peak, peak_kind = measured_peaks()
     alg = [algorithmic_bytes(a, b, batch=nb, distinct=nb) for a, b in SHAPES]
@@ -1096,7 +1096,8 @@ def main():
                                            "denoise_1024_kohya", "hotswap_kohya304", "lora_gemm_flux"],
                     default="flux_sweep_b14", help="flux_sweep_b14: fused decode+SGMV (default); decode_*: "
                     "standalone packed decode of 14 resident adapters per launch")
-    ap.add_argument("--cpu-seconds", type=float, default=15.0, help="CPU-baseline sample length (rank 0, N=1)")
+    ap.add_argument("--cpu-seconds", type=float, default=15.0,
+                    help="CPU-baseline sample length of the decode and hot-swap workloads (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
     ap.add_argument("--mode", choices=["staged", "fused"], default=None,
