@@ -66,8 +66,10 @@ def stream_handle(device: torch.device) -> int:
 _lut_cache: dict = {}
 
 
-def lut_array(lut: np.ndarray) -> ctypes.Array:
+def lut_array(lut) -> ctypes.Array:
     """The level LUT as a ctypes float array (cached per LUT array object; LUTs are immutable)."""
+    if isinstance(lut, ctypes.Array):
+        return lut
     key = id(lut)
     hit = _lut_cache.get(key)
     if hit is not None and hit[0] is lut:
@@ -76,6 +78,22 @@ def lut_array(lut: np.ndarray) -> ctypes.Array:
     if len(_lut_cache) > 256:
         _lut_cache.clear()
     _lut_cache[key] = (lut, arr)
+    return arr
+
+
+_lut_list_cache: dict = {}
+
+
+def lut_from_list(lut) -> ctypes.Array:
+    """A flat list of LUT floats (the form the custom ops take) as a ctypes array, cached by
+    the list's values."""
+    key = tuple(float(v) for v in lut)
+    arr = _lut_list_cache.get(key)
+    if arr is None:
+        if len(_lut_list_cache) > 256:
+            _lut_list_cache.clear()
+        arr = _lib.float_array(key)
+        _lut_list_cache[key] = arr
     return arr
 
 

@@ -21,14 +21,21 @@ from torch import nn
 
 from .. import _modtree
 from .. import codebook as cb
-from . import _launch
+from . import _launch, ops
 from .packed import PackedBank
-from .shared import packed_codebook_lora_delta_, shared_codebook_lora_delta_
+from .shared import _check
 
 
 def _inference_only(out: torch.Tensor) -> None:
     if out.requires_grad and torch.is_grad_enabled():
         raise RuntimeError("lithe_b200 layers are inference-only: run them under torch.no_grad()")
+
+
+def _slot_ids(assign: Optional[torch.Tensor], x3: torch.Tensor) -> torch.Tensor:
+    """The (B,) int32 slot ids of a forward: ``assign``, or slot 0 for every sample when unset."""
+    if assign is None:
+        return torch.zeros(x3.shape[0], dtype=torch.int32, device=x3.device)
+    return assign.to(device=x3.device, dtype=torch.int32).contiguous()
 
 
 def _as3d(x: torch.Tensor, out: torch.Tensor):
@@ -57,6 +64,11 @@ class IndexLoRALinear(nn.Module):
         self.d_out = base.out_features
         self.scaling = float(scaling)
         self.assign: Optional[torch.Tensor] = None
+        # the same argument checks as the functional API, once; the forward then calls the op
+        probe = torch.empty(1, 1, base.in_features, device="meta")
+        _check(probe, self.idx_a, self.pool_a, self.idx_b, self.pool_b, torch.empty(1, device="meta"),
+               self.rank, self.d_out)
+        self._lut = [float(v) for v in cb.kernel_lut(self.pool_a, self.pool_b).reshape(-1)]
 
     @property
     def num_slots(self) -> int:
@@ -66,11 +78,11 @@ class IndexLoRALinear(nn.Module):
         out = self.base(x)
         _inference_only(out)
         x3, out3 = _as3d(x, out)
-        assign = self.assign
-        if assign is None:
-            assign = torch.zeros(x3.shape[0], dtype=torch.int32, device=x.device)
-        shared_codebook_lora_delta_(out3, x3, self.idx_a, self.pool_a, self.idx_b, self.pool_b, assign,
-                                    self.rank, self.d_out, self.scaling, accumulate=True)
+        ids = _slot_ids(self.assign, x3)
+        torch.ops.lithe_b200.sgmv_index_(out3, x3.contiguous(), self.idx_a, self.idx_b,
+                                         ops.view_params(_launch.level_major_view(self.idx_a)),
+                                         ops.view_params(_launch.level_major_view(self.idx_b)), self.num_slots, ids,
+                                         None, self.rank, self._lut, self.scaling, True)
         return out
 
 
@@ -121,7 +133,9 @@ class PackedLoRALinear(nn.Module):
         # largest in_features the fused path takes (None: any); larger linears stay on cuBLAS +
         # the fused decode/SGMV kernel (FUSED_GEMM_MAX_K gives the measured reason)
         self.fused_gemm_max_k: Optional[int] = FUSED_GEMM_MAX_K
-        self._views = None                 # (bank storage key, (view_a, view_b)) of the fused path
+        # the custom ops' arguments that do not change between calls
+        self._va, self._vb = bank.view_params(name, self.rows)
+        self._lut = bank.lut_list
 
     def _gemm_ok(self, x3: torch.Tensor) -> bool:
         w = self.base.weight
@@ -140,12 +154,16 @@ class PackedLoRALinear(nn.Module):
         out = self.base(x)
         _inference_only(out)
         x3, out3 = _as3d(x, out)
-        assign = self.assign
-        if assign is None:
-            assign = torch.zeros(x3.shape[0], dtype=torch.int32, device=x.device)
-        packed_codebook_lora_delta_(out3, x3, self.bank, self.name, assign, scaling=self.scaling,
-                                    weights=self.weights, rows=self.rows)
+        words = self.bank.words
+        torch.ops.lithe_b200.sgmv_index_(out3, x3.contiguous(), words, words, self._va, self._vb, self.bank.n_slots,
+                                         _slot_ids(self.assign, x3), self._weights(x3), self.rank, self._lut,
+                                         self.scaling, True)
         return out
+
+    def _weights(self, x3: torch.Tensor) -> Optional[torch.Tensor]:
+        if self.weights is None:
+            return None
+        return self.weights.to(device=x3.device, dtype=torch.float32).contiguous()
 
     def _h_key(self, x3, ids, w):
         """(tensors compared by identity, values compared by equality)."""
@@ -171,29 +189,23 @@ class PackedLoRALinear(nn.Module):
     def _forward_fused_gemm(self, x: torch.Tensor, x3: torch.Tensor) -> torch.Tensor:
         bsz, m, d_in = x3.shape
         d_out = self.base.out_features
-        assign = self.assign
-        if assign is None:
-            assign = torch.zeros(bsz, dtype=torch.int32, device=x.device)
-        ids = assign.to(device=x.device, dtype=torch.int32).contiguous()
-        w = None if self.weights is None else self.weights.to(device=x.device, dtype=torch.float32).contiguous()
-        key = (self.bank.words.data_ptr(), self.bank.slot_stride)
-        if self._views is None or self._views[0] != key:
-            self._views = (key, self.bank.views(self.name, self.rows))
-        va, vb = self._views[1]
+        ids = _slot_ids(self.assign, x3)
+        w = self._weights(x3)
         # Split targets of one fused module (Kohya q/k/v, q/k/v/proj_mlp) share its A factor and are
-        # called with the same input, so h = x . A^T is computed once and reused by the others.
-        h = self._shared_h(x3, ids, w) if self.rows is not None else None
+        # called with the same input, so h = x . A^T is computed once and reused by the others.  The
+        # reuse keys on tensor identity, which a traced graph does not have: under torch.compile
+        # every target computes its own h (the same values).
+        share = self.rows is not None and not torch.compiler.is_compiling()
+        h = self._shared_h(x3, ids, w) if share else None
         fresh = h is None
+        words = self.bank.words
+        h_new, b_dec = torch.ops.lithe_b200.lora_prep(x3, words, words, self._va, self._vb, self.bank.n_slots, ids, w,
+                                                      d_out, self._lut, self.scaling, fresh)
         if fresh:
-            h = torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device)
-        b_dec = torch.empty(bsz, d_out, 16, dtype=torch.bfloat16, device=x.device)
-        _launch.lora_prep_(x3, view_a=va, view_b=vb, n_slots=self.bank.n_slots, ids=ids, weights=w, d_out=d_out,
-                           lut=self.bank.lut, scaling=self.scaling, h=h if fresh else None, b_dec=b_dec)
-        if fresh and self.rows is not None:
-            self._store_h(x3, ids, w, h)
-        out = torch.empty(bsz * m, d_out, dtype=torch.bfloat16, device=x.device)
-        _launch.lora_gemm_(x3.view(bsz * m, d_in), self.base.weight, self.base.bias, out, h=h, b_dec=b_dec,
-                           rows_per_sample=m)
+            h = h_new
+            if share:
+                self._store_h(x3, ids, w, h)
+        out = torch.ops.lithe_b200.lora_gemm(x3.view(bsz * m, d_in), self.base.weight, self.base.bias, h, b_dec, m)
         return out.view(*x.shape[:-1], d_out)
 
 

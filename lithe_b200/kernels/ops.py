@@ -1,0 +1,102 @@
+"""The C-ABI entry points as PyTorch custom operators (namespace ``lithe_b200``).
+
+Registering the kernels with ``torch.library`` makes them visible to torch.compile: each op
+has a fake (meta) implementation that gives its outputs' shapes and dtypes without running
+anything, so a model whose linears are wrapped by the layers of this package traces into one
+graph with no break at every LoRA linear (the reference's timed renders run the wrapped
+transformer under torch.compile).  At run time every op calls the same C entry point as the
+tensor wrappers in ``_launch`` -- there is no second implementation.
+
+Index banks are passed as tensors (``bank_a`` / ``bank_b``; the same tensor for the two sides
+of a packed bank) plus five integers per side, the fields of ``lithe_index_view`` after its base
+pointer: (format, levels, slot_stride, offset, level_stride).  ``lut`` is the level LUT of the C
+ABI as a flat list of 2 * levels * 10 floats.
+
+  sgmv_index_(out!, x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, rank, lut,
+              scaling, accumulate)                       lithe_sgmv_index, out updated in place
+  lora_prep(x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, d_out, lut, scaling,
+            compute_h) -> (h, b_dec)                     lithe_lora_prep (h is (0, 16) when
+                                                         compute_h is False)
+  lora_gemm(x, weight, bias, h, b_dec, rows_per_sample) -> out       lithe_lora_gemm
+  decode_packed(words, n_blocks, levels, sides, lut, fp32) -> out    lithe_decode_packed
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import torch
+
+from .. import _lib
+from . import _launch
+
+_NS = "lithe_b200"
+
+
+def view_params(view: _lib.IndexView) -> List[int]:
+    """The integer fields of an index view (everything but its base pointer)."""
+    return [int(view.format), int(view.num_levels), int(view.slot_stride), int(view.offset), int(view.level_stride)]
+
+
+def _view(base: torch.Tensor, params: List[int]) -> _lib.IndexView:
+    if len(params) != 5:
+        raise ValueError("an index view is (format, levels, slot_stride, offset, level_stride)")
+    fmt, levels, slot_stride, offset, level_stride = (int(v) for v in params)
+    return _lib.IndexView(base.data_ptr(), fmt, levels, slot_stride, offset, level_stride)
+
+
+@torch.library.custom_op(f"{_NS}::sgmv_index_", mutates_args=("out",), device_types="cuda")
+def sgmv_index_(out: torch.Tensor, x: torch.Tensor, bank_a: torch.Tensor, bank_b: torch.Tensor, view_a: List[int],
+                view_b: List[int], n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor], rank: int,
+                lut: List[float], scaling: float, accumulate: bool) -> None:
+    _launch.sgmv_index_(x, out, accumulate=accumulate, view_a=_view(bank_a, view_a), view_b=_view(bank_b, view_b),
+                        n_slots=n_slots, ids=ids, weights=weights, rank=rank, lut=_launch.lut_from_list(lut),
+                        scaling=scaling)
+
+
+@sgmv_index_.register_fake
+def _sgmv_index_fake(out, x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, rank, lut, scaling, accumulate):
+    return None
+
+
+@torch.library.custom_op(f"{_NS}::lora_prep", mutates_args=(), device_types="cuda")
+def lora_prep(x: torch.Tensor, bank_a: torch.Tensor, bank_b: torch.Tensor, view_a: List[int], view_b: List[int],
+              n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor], d_out: int, lut: List[float],
+              scaling: float, compute_h: bool) -> Tuple[torch.Tensor, torch.Tensor]:
+    bsz, m, _ = x.shape
+    h = torch.empty(bsz * m if compute_h else 0, 16, dtype=torch.bfloat16, device=x.device)
+    b_dec = torch.empty(bsz, d_out, 16, dtype=torch.bfloat16, device=x.device)
+    _launch.lora_prep_(x, view_a=_view(bank_a, view_a), view_b=_view(bank_b, view_b), n_slots=n_slots, ids=ids,
+                       weights=weights, d_out=d_out, lut=_launch.lut_from_list(lut), scaling=scaling,
+                       h=h if compute_h else None, b_dec=b_dec)
+    return h, b_dec
+
+
+@lora_prep.register_fake
+def _lora_prep_fake(x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, d_out, lut, scaling, compute_h):
+    bsz, m, _ = x.shape
+    h = x.new_empty(bsz * m if compute_h else 0, 16, dtype=torch.bfloat16)
+    return h, x.new_empty(bsz, d_out, 16, dtype=torch.bfloat16)
+
+
+@torch.library.custom_op(f"{_NS}::lora_gemm", mutates_args=(), device_types="cuda")
+def lora_gemm(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tensor], h: Optional[torch.Tensor],
+              b_dec: Optional[torch.Tensor], rows_per_sample: int) -> torch.Tensor:
+    out = torch.empty(x.shape[0], weight.shape[0], dtype=torch.bfloat16, device=x.device)
+    return _launch.lora_gemm_(x, weight, bias, out, h=h, b_dec=b_dec, rows_per_sample=rows_per_sample)
+
+
+@lora_gemm.register_fake
+def _lora_gemm_fake(x, weight, bias, h, b_dec, rows_per_sample):
+    return x.new_empty(x.shape[0], weight.shape[0], dtype=torch.bfloat16)
+
+
+@torch.library.custom_op(f"{_NS}::decode_packed", mutates_args=(), device_types="cuda")
+def decode_packed(words: torch.Tensor, n_blocks: int, levels: int, sides: Optional[torch.Tensor], lut: List[float],
+                  fp32: bool) -> torch.Tensor:
+    out = torch.empty(n_blocks, 64, dtype=torch.float32 if fp32 else torch.bfloat16, device=words.device)
+    return _launch.decode_packed_(words, n_blocks, levels, sides, _launch.lut_from_list(lut), out)
+
+
+@decode_packed.register_fake
+def _decode_packed_fake(words, n_blocks, levels, sides, lut, fp32):
+    return words.new_empty(n_blocks, 64, dtype=torch.float32 if fp32 else torch.bfloat16)

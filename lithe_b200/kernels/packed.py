@@ -319,6 +319,18 @@ class PackedBank:
                                 L * (self.layout.b_off[i] + b_first))
         return va, vb
 
+    def view_params(self, name: str, rows: Optional[Tuple[int, int]] = None) -> Tuple[List[int], List[int]]:
+        """``views(name, rows)`` without the base pointers: the integer fields the custom ops
+        take next to the bank tensor (``self.words``)."""
+        from .ops import view_params
+        va, vb = self.views(name, rows)
+        return view_params(va), view_params(vb)
+
+    @property
+    def lut_list(self) -> List[float]:
+        """The level LUT as the flat float list the custom ops take."""
+        return [float(v) for v in np.asarray(self.lut, dtype=np.float32).reshape(-1)]
+
     def decode(self, slot_ids, dtype: torch.dtype = torch.bfloat16, out: Optional[torch.Tensor] = None) -> torch.Tensor:
         """(n_sel, total_blocks, 64) decode of the given slots in one launch (into ``out`` if given)."""
         ids = torch.as_tensor(slot_ids, dtype=torch.int32).reshape(-1).to(self.device)

@@ -21,7 +21,7 @@ from typing import Optional, Tuple
 import torch
 
 from .. import codebook as cb
-from . import _launch
+from . import _launch, ops
 
 
 def _check(x, idx_A, pools_A, idx_B, pools_B, assign, R, D_out):
@@ -50,6 +50,10 @@ def _bank(idx: torch.Tensor, device) -> torch.Tensor:
     return idx.to(device).contiguous()
 
 
+def _lut_list(pools_A: torch.Tensor, pools_B: torch.Tensor) -> list:
+    return [float(v) for v in cb.kernel_lut(pools_A, pools_B).reshape(-1)]
+
+
 def shared_codebook_lora_delta_(out: torch.Tensor, x: torch.Tensor, idx_A: torch.Tensor, pools_A: torch.Tensor,
                                 idx_B: torch.Tensor, pools_B: torch.Tensor, assign: torch.Tensor, R: int,
                                 D_out: int, scaling: float, accumulate: bool = True,
@@ -66,9 +70,10 @@ def shared_codebook_lora_delta_(out: torch.Tensor, x: torch.Tensor, idx_A: torch
     ia, ib = _bank(idx_A, x.device), _bank(idx_B, x.device)
     ids = assign.to(device=x.device, dtype=torch.int32).contiguous()
     w = None if weights is None else weights.to(device=x.device, dtype=torch.float32).contiguous()
-    return _launch.sgmv_index_(x.contiguous(), out, accumulate=accumulate, view_a=_launch.level_major_view(ia),
-                               view_b=_launch.level_major_view(ib), n_slots=ia.shape[0], ids=ids, weights=w,
-                               rank=R, lut=cb.kernel_lut(pools_A, pools_B), scaling=scaling)
+    torch.ops.lithe_b200.sgmv_index_(out, x.contiguous(), ia, ib, ops.view_params(_launch.level_major_view(ia)),
+                                     ops.view_params(_launch.level_major_view(ib)), ia.shape[0], ids, w, R,
+                                     _lut_list(pools_A, pools_B), float(scaling), bool(accumulate))
+    return out
 
 
 def shared_codebook_lora_delta(x: torch.Tensor, idx_A: torch.Tensor, pools_A: torch.Tensor, idx_B: torch.Tensor,
@@ -103,9 +108,10 @@ def packed_codebook_lora_delta_(out: torch.Tensor, x: torch.Tensor, bank, name: 
     d_out = bank.layout.shapes_b[i][0] if rows is None else int(rows[1]) - int(rows[0])
     if x.dim() != 3 or x.shape[-1] != d_in or out.shape != (x.shape[0], x.shape[1], d_out):
         raise ValueError(f"{name}: x must be (B, M, {d_in}) and out (B, M, {d_out})")
-    va, vb = bank.views(name, rows)
+    va, vb = bank.view_params(name, rows)
     ids = assign.to(device=x.device, dtype=torch.int32).contiguous()
     w = None if weights is None else weights.to(device=x.device, dtype=torch.float32).contiguous()
-    return _launch.sgmv_index_(x.contiguous(), out, accumulate=accumulate, view_a=va, view_b=vb,
-                               n_slots=bank.n_slots, ids=ids, weights=w, rank=rank, lut=bank.lut,
-                               scaling=bank.layout.scaling if scaling is None else scaling)
+    torch.ops.lithe_b200.sgmv_index_(out, x.contiguous(), bank.words, bank.words, va, vb, bank.n_slots, ids, w, rank,
+                                     bank.lut_list, float(bank.layout.scaling if scaling is None else scaling),
+                                     bool(accumulate))
+    return out

@@ -18,7 +18,7 @@ import numpy as np
 import torch
 from torch import nn
 
-from . import _modtree
+from . import _lib, _modtree
 from . import codebook as cb
 from . import quant
 from .kernels import _launch
@@ -126,6 +126,7 @@ class LitheLinear(nn.Module):
         self._levels = ia.shape[0]
         self._na = na
         self._ids = torch.zeros(1, dtype=torch.int32, device=dev)
+        self._lut = [float(v) for v in self.codebook.lut.reshape(-1)]
         self._idx = (ia, ib)
         self._cache = None
         self._frozen = True
@@ -156,10 +157,9 @@ class LitheLinear(nn.Module):
         x3 = x.reshape(1, -1, self.in_features).contiguous()
         out3 = out.view(1, -1, self.out_features)
         L = self._levels
-        va = _launch.index_view(self._words, 0, L, 0, 0)
-        vb = _launch.index_view(self._words, 0, L, 0, L * self._na)
-        _launch.sgmv_index_(x3, out3, accumulate=True, view_a=va, view_b=vb, n_slots=1, ids=self._ids,
-                            weights=None, rank=self.rank, lut=self.codebook.lut, scaling=self.scaling)
+        torch.ops.lithe_b200.sgmv_index_(out3, x3, self._words, self._words, [_lib.IDX_PACKED9, L, 0, 0, 0],
+                                         [_lib.IDX_PACKED9, L, 0, L * self._na, 0], 1, self._ids, None, self.rank,
+                                         self._lut, self.scaling, True)
         return out
 
 

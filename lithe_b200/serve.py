@@ -22,7 +22,7 @@ from . import _modtree
 from . import codebook as cb
 from . import quant
 from .fileio import LitheAdapter
-from .kernels import _launch
+from .kernels import _launch, ops
 from .kernels.layers import FUSED_GEMM_MAX_K, _inference_only
 
 Route = Sequence[Tuple[int, float]]
@@ -119,6 +119,7 @@ class MultiAdapterLinear(nn.Module):
                              persistent=False)
         self.scales: List[float] = []
         self.lut = cb.kernel_lut(pool_a, pool_b)      # computed once from the (host) pools
+        self._lut = [float(v) for v in self.lut.reshape(-1)]
 
     def add_adapter(self, idx_a: np.ndarray, idx_b: np.ndarray, scale: float) -> None:
         dev = self.idx_a.device
@@ -141,15 +142,15 @@ class MultiAdapterLinear(nn.Module):
                             w: torch.Tensor) -> torch.Tensor:
         bsz, m, d_in = xs.shape
         d_out = self.base.out_features
-        va, vb = _launch.level_major_view(self.idx_a), _launch.level_major_view(self.idx_b)
-        h = torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device)
-        b_dec = torch.empty(bsz, d_out, 16, dtype=torch.bfloat16, device=x.device)
-        _launch.lora_prep_(xs, view_a=va, view_b=vb, n_slots=self.idx_a.shape[0], ids=slot_ids, weights=w,
-                           d_out=d_out, lut=self.lut, scaling=1.0, h=h, b_dec=b_dec)
-        out = torch.empty(bsz * m, d_out, dtype=torch.bfloat16, device=x.device)
-        _launch.lora_gemm_(xs.view(bsz * m, d_in), self.base.weight, self.base.bias, out, h=h, b_dec=b_dec,
-                           rows_per_sample=m)
+        va, vb = self._view_params()
+        h, b_dec = torch.ops.lithe_b200.lora_prep(xs, self.idx_a, self.idx_b, va, vb, self.idx_a.shape[0], slot_ids, w,
+                                                  d_out, self._lut, 1.0, True)
+        out = torch.ops.lithe_b200.lora_gemm(xs.view(bsz * m, d_in), self.base.weight, self.base.bias, h, b_dec, m)
         return out.view(*x.shape[:-1], d_out)
+
+    def _view_params(self):
+        return (ops.view_params(_launch.level_major_view(self.idx_a)),
+                ops.view_params(_launch.level_major_view(self.idx_b)))
 
     def forward(self, x: torch.Tensor) -> torch.Tensor:
         if self.fused_gemm:
@@ -172,10 +173,10 @@ class MultiAdapterLinear(nn.Module):
         bsz = ids.shape[0]
         xs = x.reshape(bsz, -1, x.shape[-1]).contiguous()
         out3 = out.view(bsz, -1, out.shape[-1])
-        va, vb = _launch.level_major_view(self.idx_a), _launch.level_major_view(self.idx_b)
+        va, vb = self._view_params()
         for slot_ids, w in self.router.columns(x.device, tuple(self.scales)):
-            _launch.sgmv_index_(xs, out3, accumulate=True, view_a=va, view_b=vb, n_slots=self.idx_a.shape[0],
-                                ids=slot_ids, weights=w, rank=self.rank, lut=self.lut, scaling=1.0)
+            torch.ops.lithe_b200.sgmv_index_(out3, xs, self.idx_a, self.idx_b, va, vb, self.idx_a.shape[0], slot_ids, w,
+                                             self.rank, self._lut, 1.0, True)
         return out
 
 

@@ -76,3 +76,32 @@ def test_decode_argument_errors():
     assert lib.lithe_decode_packed(0x1000, 0, 3, None, lut, 0x2000, 0, None) == _lib.OK
     assert lib.lithe_decode_packed_batch(0x1000, 2, 4, 0x3000, 1, 100, 3, None, lut, 0x2000, 0, None, None) \
         == _lib.ERR_ARG                                    # slot_stride shorter than the stream
+
+
+def test_custom_ops_registered_with_fake_kernels():
+    """The kernels are torch.library ops with fake (meta) kernels: shapes and dtypes of their
+    outputs are known without a GPU, which is what torch.compile traces with."""
+    import torch
+    from torch._subclasses.fake_tensor import FakeTensorMode
+    import lithe_b200.kernels.ops  # noqa: F401  (registers the ops)
+
+    for name in ("sgmv_index_", "lora_prep", "lora_gemm", "decode_packed"):
+        assert hasattr(torch.ops.lithe_b200, name)
+    view = [0, 3, 64, 0, 0]
+    with FakeTensorMode():
+        x = torch.empty(2, 256, 512, dtype=torch.bfloat16, device="cuda")
+        words = torch.empty(10, 64, dtype=torch.int64, device="cuda")
+        ids = torch.empty(2, dtype=torch.int32, device="cuda")
+        h, b_dec = torch.ops.lithe_b200.lora_prep(x, words, words, view, view, 10, ids, None, 768, [0.0] * 60, 1.0,
+                                                  True)
+        assert tuple(h.shape) == (512, 16) and tuple(b_dec.shape) == (2, 768, 16) and h.dtype == torch.bfloat16
+        h0, _ = torch.ops.lithe_b200.lora_prep(x, words, words, view, view, 10, ids, None, 768, [0.0] * 60, 1.0, False)
+        assert tuple(h0.shape) == (0, 16)
+        w = torch.empty(768, 512, dtype=torch.bfloat16, device="cuda")
+        out = torch.ops.lithe_b200.lora_gemm(x.view(512, 512), w, None, h, b_dec, 256)
+        assert tuple(out.shape) == (512, 768) and out.dtype == torch.bfloat16
+        dec = torch.ops.lithe_b200.decode_packed(words.view(-1), 100, 3, None, [0.0] * 60, True)
+        assert tuple(dec.shape) == (100, 64) and dec.dtype == torch.float32
+        y = torch.empty(2, 256, 768, dtype=torch.bfloat16, device="cuda")
+        assert torch.ops.lithe_b200.sgmv_index_(y, x, words, words, view, view, 10, ids, None, 16, [0.0] * 60, 1.0,
+                                                True) is None
