@@ -51,6 +51,7 @@ extern "C" {
 
 #define LITHE_DTYPE_BF16 0
 #define LITHE_DTYPE_F32 1
+#define LITHE_DTYPE_F16 2
 
 #define LITHE_MAX_LEVELS 4
 
@@ -107,6 +108,22 @@ LITHE_API int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate,
                          int64_t n_slots, const int32_t* ids, const float* weights,
                          int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank,
                          const float* lut, float scaling, int32_t* err_flag, void* stream);
+
+/*
+ * lithe_sgmv_index with the element types given: x (and out when accumulating) in
+ * x_dtype = LITHE_DTYPE_BF16 or LITHE_DTYPE_F16, the decoded factors, h and the MMAs in that
+ * type (fp32 accumulation); out_dtype is x_dtype, or LITHE_DTYPE_F32 when accumulate == 0
+ * (the delta alone, written in fp32 without a rounding to 16 bits).  Replaces the dtype
+ * handling of shared_codebook_lora_delta (lithe/kernels/shared.py:210-218: pools cast to
+ * x.dtype, the delta in out_dtype, default x.dtype).  Other combinations return
+ * LITHE_ERR_UNSUPPORTED.  lithe_sgmv_index is this call with both dtypes LITHE_DTYPE_BF16.
+ */
+LITHE_API int32_t lithe_sgmv_index_typed(const void* x, void* out, int32_t accumulate,
+                         const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                         int64_t n_slots, const int32_t* ids, const float* weights,
+                         int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank,
+                         const float* lut, float scaling, int32_t x_dtype, int32_t out_dtype,
+                         int32_t* err_flag, void* stream);
 
 /* Bytes of device workspace lithe_sgmv_index_ws needs for a (batch, d_in, d_out) call:
  * batch * (d_in/64 + ceil(d_out/64)) * 512. */

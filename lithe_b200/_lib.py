@@ -27,6 +27,7 @@ IDX_I32 = 2
 
 DTYPE_BF16 = 0
 DTYPE_F32 = 1
+DTYPE_F16 = 2
 
 MAX_LEVELS = 4
 NOALLOC_WS_BYTES = 4 << 20       # LITHE_NOALLOC_WS_BYTES
@@ -63,6 +64,10 @@ _SIGNATURES.update({
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64,
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32,
         _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p, _c.c_void_p]),
+    "lithe_sgmv_index_typed": (_c.c_int32, [
+        _c.c_void_p, _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64,
+        _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32,
+        _c.POINTER(_c.c_float), _c.c_float, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_void_p]),
     "lithe_sgmv_workspace_bytes": (_c.c_int64, [_c.c_int32, _c.c_int32, _c.c_int32]),
     "lithe_sgmv_index_ws": (_c.c_int32, [
         _c.c_void_p, _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64,

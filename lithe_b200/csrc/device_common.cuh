@@ -4,6 +4,7 @@
 
 #include <cstdint>
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda.h>
 
 #include "lithe_b200.h"
@@ -343,5 +344,53 @@ __device__ __forceinline__ void mma_bf16_16816(float d[4], const uint32_t a[4], 
         : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
           "f"(c[2]), "f"(c[3]));
 }
+
+// D = A(16x16 fp16, row) * B(16x8 fp16, col) + C, fp32 accumulate
+__device__ __forceinline__ void mma_f16_16816(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1,
+                                              const float c[4]) {
+    asm volatile(
+        "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9},"
+        " {%10,%11,%12,%13};\n"
+        : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+        : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1), "f"(c[0]), "f"(c[1]),
+          "f"(c[2]), "f"(c[3]));
+}
+
+// The 16-bit activation types the SGMV kernels compute in (kF16: fp16, else bf16): packing two
+// fp32 values into a 32-bit word (round to nearest even), the two halves of a word as fp32
+// (exact), one value rounded to the type, and the warp MMA on that type (fp32 accumulate).
+template <bool kF16>
+struct Act;
+
+template <>
+struct Act<false> {
+    static __device__ __forceinline__ uint32_t pack(float lo, float hi) { return pack_bf16x2(lo, hi); }
+    static __device__ __forceinline__ float lo(uint32_t w) { return bf16lo_to_f32(w); }
+    static __device__ __forceinline__ float hi(uint32_t w) { return bf16hi_to_f32(w); }
+    static __device__ __forceinline__ float round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+    static __device__ __forceinline__ void mma(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1,
+                                               const float c[4]) {
+        mma_bf16_16816(d, a, b0, b1, c);
+    }
+};
+
+template <>
+struct Act<true> {
+    static __device__ __forceinline__ uint32_t pack(float lo, float hi) {
+        __half2 h = __floats2half2_rn(lo, hi);
+        return *reinterpret_cast<uint32_t*>(&h);
+    }
+    static __device__ __forceinline__ float lo(uint32_t w) {
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xffffu)));
+    }
+    static __device__ __forceinline__ float hi(uint32_t w) {
+        return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+    }
+    static __device__ __forceinline__ float round(float v) { return __half2float(__float2half_rn(v)); }
+    static __device__ __forceinline__ void mma(float d[4], const uint32_t a[4], uint32_t b0, uint32_t b1,
+                                               const float c[4]) {
+        mma_f16_16816(d, a, b0, b1, c);
+    }
+};
 
 }  // namespace lithe

@@ -74,7 +74,8 @@ struct SgmvParams {
     int32_t a_blocks_per_row;   // d_in / 64
     int32_t b_blocks;           // d_out * rank / 64
     float scaling;
-    __nv_bfloat16* out;
+    void* out;                  // x's 16-bit type, or fp32 when out_f32
+    int32_t out_f32;            // delta-only form (accumulate == 0) writing fp32
     const uint8_t* ws;          // staged mode: decoded factor chunks, (batch, n_chunks, 512 B)
     int32_t n_chunks;           // n_xchunks + n_ochunks (per-sample stride of ws, in chunks)
     __nv_bfloat16* h_out;       // shrink-only mode (lithe_lora_prep): h rows (batch * m, 16), else null
@@ -142,9 +143,10 @@ __device__ __forceinline__ float unit_weight(const SgmvParams& p, const UnitCach
 __device__ __forceinline__ uint4 lds128(const uint8_t* a) { return *reinterpret_cast<const uint4*>(a); }
 __device__ __forceinline__ void sts128(uint8_t* a, uint4 v) { *reinterpret_cast<uint4*>(a) = v; }
 
-// bf16x2 word + (dlo, dhi) in fp32, rounded to nearest even
-__device__ __forceinline__ uint32_t add_bf16x2(uint32_t w, float dlo, float dhi) {
-    return pack_bf16x2(bf16lo_to_f32(w) + dlo, bf16hi_to_f32(w) + dhi);
+// 16-bit pair word + (dlo, dhi) in fp32, rounded to nearest even
+template <bool kF16>
+__device__ __forceinline__ uint32_t add_x2(uint32_t w, float dlo, float dhi) {
+    return Act<kF16>::pack(Act<kF16>::lo(w) + dlo, Act<kF16>::hi(w) + dhi);
 }
 
 // ---------------------------------------------------------------------------------------
@@ -182,10 +184,11 @@ __device__ __forceinline__ void decode_values(const SgmvParams& p, const DecodeT
 // [0,1,8,9, 2,3,10,11, 4,5,12,13, 6,7,14,15] so that an mma B fragment is one 8-byte read.
 // Logical column N = 16j + n covers the output columns of block G = N / per, pattern
 // offset e = N % per (per = 16/kRank): B[o, r] = w_G[kRank*e + r].
-template <int kRank>
+template <int kRank, bool kF16>
 __device__ __forceinline__ void decode_chunk(const SgmvParams& p, const DecodeTables* tab, const float* lut_s,
                                              const Unit& un, int c, bool live, const uint32_t* k, uint8_t* fact,
                                              int lane) {
+    using T = Act<kF16>;
     const int row = lane >> 1;
     const uint32_t half = lane & 1;
     if (c < un.nx) {
@@ -193,8 +196,7 @@ __device__ __forceinline__ void decode_chunk(const SgmvParams& p, const DecodeTa
         if (live) {
             float v[8];
             decode_values(p, tab, lut_s, 0, k, half, v);
-            q = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                           pack_bf16x2(v[6], v[7]));
+            q = make_uint4(T::pack(v[0], v[1]), T::pack(v[2], v[3]), T::pack(v[4], v[5]), T::pack(v[6], v[7]));
         }
         sts128(fact + row * 32 + half * 16, q);
         return;
@@ -220,7 +222,7 @@ __device__ __forceinline__ void decode_chunk(const SgmvParams& p, const DecodeTa
     }
     uint32_t* dst = reinterpret_cast<uint32_t*>(fact + row * 32);
 #pragma unroll
-    for (int i = 0; i < 8; i += 2) dst[(i >> 1) * 2 + half] = pack_bf16x2(val[i], val[i + 1]);
+    for (int i = 0; i < 8; i += 2) dst[(i >> 1) * 2 + half] = T::pack(val[i], val[i + 1]);
 }
 
 // The chunks of stage q of a unit, in the unit's chunk numbering (x chunks 0 .. nx-1, then
@@ -271,7 +273,7 @@ __device__ __forceinline__ uint32_t load_stage_tiles(const SgmvParams& p, const 
 // four to eight warps the same stream reaches 33-37 GB/s per SM (measured with a streaming
 // probe, 57344 x 3072 bf16, one CTA per SM).
 // Returns one past the last position this warp issued (all of them have arrived).
-template <int kRank, bool kStaged, int kFeed>
+template <int kRank, bool kStaged, int kFeed, bool kF16>
 __device__ uint32_t run_feeder(int d, int lane, const SgmvParams& p, const UnitCache* uc, const CUtensorMap* tmx,
                                const CUtensorMap* tmo, uint8_t* tiles, uint8_t* facts, const DecodeTables* tab,
                                const float* lut_s, uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin,
@@ -360,7 +362,8 @@ __device__ uint32_t run_feeder(int d, int lane, const SgmvParams& p, const UnitC
                     if (k < n) {
                         uint32_t kk[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
                         if (live[k]) finish_raw<LITHE_MAX_LEVELS>(c0 + k < cur.nx ? p.ia : p.ib, raw[k], kk, p.err);
-                        decode_chunk<kRank>(p, tab, lut_s, cur, c0 + k, live[k], kk, fdst + k * kFactBytes, lane);
+                        decode_chunk<kRank, kF16>(p, tab, lut_s, cur, c0 + k, live[k], kk, fdst + k * kFactBytes,
+                                                  lane);
                     }
                 }
             }
@@ -377,23 +380,57 @@ __device__ uint32_t run_feeder(int d, int lane, const SgmvParams& p, const UnitC
 // ---------------------------------------------------------------------------------------
 // Add the two expand results (c0 -> logical column 2t, c1 -> 2t+1 of n8 tile q) to the 8
 // contiguous output values a thread owns per row (ranks 16 and 8).
-template <int kRank>
+template <int kRank, bool kF16>
 __device__ __forceinline__ uint4 add_delta8(uint4 v, float c0, float c1) {
     if constexpr (kRank == 16) {   // columns: c0 c0 c0 c0 c1 c1 c1 c1
-        v.x = add_bf16x2(v.x, c0, c0);
-        v.y = add_bf16x2(v.y, c0, c0);
-        v.z = add_bf16x2(v.z, c1, c1);
-        v.w = add_bf16x2(v.w, c1, c1);
+        v.x = add_x2<kF16>(v.x, c0, c0);
+        v.y = add_x2<kF16>(v.y, c0, c0);
+        v.z = add_x2<kF16>(v.z, c1, c1);
+        v.w = add_x2<kF16>(v.w, c1, c1);
     } else {                       // columns: c0 c1 c0 c1 ...
-        v.x = add_bf16x2(v.x, c0, c1);
-        v.y = add_bf16x2(v.y, c0, c1);
-        v.z = add_bf16x2(v.z, c0, c1);
-        v.w = add_bf16x2(v.w, c0, c1);
+        v.x = add_x2<kF16>(v.x, c0, c1);
+        v.y = add_x2<kF16>(v.y, c0, c1);
+        v.z = add_x2<kF16>(v.z, c0, c1);
+        v.w = add_x2<kF16>(v.w, c0, c1);
     }
     return v;
 }
 
+// The fp32 delta of one out chunk (rows row0 and row0 + 8, the thread's 8 columns per n8 tile qq):
+// the same column pattern as add_delta8 and the small-rank path, written as fp32.
 template <int kRank>
+__device__ __forceinline__ void store_delta_f32(float* out_b, const SgmvParams& p, int row0, int col0, int t4,
+                                                const float (&d)[2][4]) {
+#pragma unroll
+    for (int hr = 0; hr < 2; ++hr) {
+        const int row = row0 + 8 * hr;
+        if (row >= p.m) continue;
+        float* orow = out_b + static_cast<int64_t>(row) * p.d_out;
+#pragma unroll
+        for (int qq = 0; qq < 2; ++qq) {
+            const float c0 = d[qq][2 * hr], c1 = d[qq][2 * hr + 1];
+            if constexpr (kRank >= 8) {
+                const int col = col0 + 32 * qq + 8 * t4;
+                if (col >= p.d_out) continue;
+                const float4 a = kRank == 16 ? make_float4(c0, c0, c0, c0) : make_float4(c0, c1, c0, c1);
+                const float4 b = kRank == 16 ? make_float4(c1, c1, c1, c1) : make_float4(c0, c1, c0, c1);
+                __stcs(reinterpret_cast<float4*>(orow + col), a);
+                __stcs(reinterpret_cast<float4*>(orow + col + 4), b);
+            } else {
+                constexpr int kPer = 16 / kRank;
+                const int nl = 8 * qq + 2 * t4;
+                const int base = (nl / kPer) * (4 * kPer) + (nl % kPer);
+#pragma unroll
+                for (int pp = 0; pp < 4; ++pp) {
+                    const int col = col0 + base + pp * kPer;
+                    if (col < p.d_out) *reinterpret_cast<float2*>(orow + col) = make_float2(c0, c1);
+                }
+            }
+        }
+    }
+}
+
+template <int kRank, bool kF16>
 __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCache* uc, uint8_t* tiles,
                              const uint8_t* facts, uint64_t* full, uint64_t* empty, float* xchg, uint64_t* xbar,
                              volatile int* abort, int u_begin, int u_end) {
@@ -450,10 +487,10 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
                     const uint4 xb = lds128(rb + (((4 * win + t4) ^ gr) << 4));
                     const uint32_t a0[4] = {xa.x, xb.x, xa.y, xb.y};
                     const uint32_t a1[4] = {xa.z, xb.z, xa.w, xb.w};
-                    mma_bf16_16816(acc[0][win], a0, f0.x, f0.y, acc[0][win]);
-                    mma_bf16_16816(acc[1][win], a0, f1.x, f1.y, acc[1][win]);
-                    mma_bf16_16816(acc[0][win], a1, f0.z, f0.w, acc[0][win]);
-                    mma_bf16_16816(acc[1][win], a1, f1.z, f1.w, acc[1][win]);
+                    Act<kF16>::mma(acc[0][win], a0, f0.x, f0.y, acc[0][win]);
+                    Act<kF16>::mma(acc[1][win], a0, f1.x, f1.y, acc[1][win]);
+                    Act<kF16>::mma(acc[0][win], a1, f0.z, f0.w, acc[0][win]);
+                    Act<kF16>::mma(acc[1][win], a1, f1.z, f1.w, acc[1][win]);
                 }
             }
             __syncwarp();
@@ -494,8 +531,8 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
             h0[i] = part[i] * sc;
             h1[i] = part[4 + i] * sc;
         }
-        const uint32_t ha[4] = {pack_bf16x2(h0[0], h0[1]), pack_bf16x2(h0[2], h0[3]), pack_bf16x2(h1[0], h1[1]),
-                                pack_bf16x2(h1[2], h1[3])};
+        const uint32_t ha[4] = {Act<kF16>::pack(h0[0], h0[1]), Act<kF16>::pack(h0[2], h0[3]),
+                                Act<kF16>::pack(h1[0], h1[1]), Act<kF16>::pack(h1[2], h1[3])};
         const int row0 = un.mt * kBM + r0;                   // token rows row0 and row0 + 8
         if (p.h_out) {
             // shrink-only: store h (ranks 2 t4, 2 t4 + 1 and 8 + 2 t4, 9 + 2 t4 of rows row0, row0 + 8)
@@ -512,7 +549,8 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
             }
             continue;
         }
-        __nv_bfloat16* out_b = p.out + static_cast<int64_t>(un.b) * p.m * p.d_out;
+        uint16_t* out_b = static_cast<uint16_t*>(p.out) + static_cast<int64_t>(un.b) * p.m * p.d_out;
+        float* outf_b = static_cast<float*>(p.out) + static_cast<int64_t>(un.b) * p.m * p.d_out;
         for (int q = 0; q < un.so; ++q, ++pos) {
             if (static_cast<int>(pos % kGroups) != grp) continue;
             const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
@@ -529,10 +567,19 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
                     const uint8_t* fb = facts + s * kStageFactBytes + k * kFactBytes;
                     const uint2 b0 = *reinterpret_cast<const uint2*>(fb + g * 32 + t4 * 8);
                     const uint2 b1 = *reinterpret_cast<const uint2*>(fb + (g + 8) * 32 + t4 * 8);
-                    mma_bf16_16816(d[0], ha, b0.x, b0.y, zero);
-                    mma_bf16_16816(d[1], ha, b1.x, b1.y, zero);
+                    Act<kF16>::mma(d[0], ha, b0.x, b0.y, zero);
+                    Act<kF16>::mma(d[1], ha, b1.x, b1.y, zero);
                 }
                 const int col0 = j * kChunk;
+                if (p.out_f32) {
+                    // delta-only form with an fp32 output: nothing is read from the tile
+                    if (release) {
+                        __syncwarp();
+                        if (lane == 0) mbar_arrive(&empty[s]);
+                    }
+                    store_delta_f32<kRank>(outf_b, p, row0, col0, t4, d);
+                    continue;
+                }
                 if constexpr (kRank >= 8) {
                     uint4 v[2][2];          // [n8 tile q][row half]
 #pragma unroll
@@ -541,7 +588,7 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
                         for (int hr = 0; hr < 2; ++hr) {
                             const uint4 o = accum ? lds128(tile + (r0 + 8 * hr) * 128 + ((((qq << 2) + t4) ^ gr) << 4))
                                                   : make_uint4(0, 0, 0, 0);
-                            v[qq][hr] = add_delta8<kRank>(o, d[qq][2 * hr], d[qq][2 * hr + 1]);
+                            v[qq][hr] = add_delta8<kRank, kF16>(o, d[qq][2 * hr], d[qq][2 * hr + 1]);
                         }
                     if (release) {
                         __syncwarp();
@@ -576,7 +623,7 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
                                                                tile + (r0 + 8 * hr) * 128 + (((col >> 3) ^ gr) << 4) +
                                                                (col & 7) * 2)
                                                          : 0u;
-                                v[qq][hr][pp] = add_bf16x2(o, d[qq][2 * hr], d[qq][2 * hr + 1]);
+                                v[qq][hr][pp] = add_x2<kF16>(o, d[qq][2 * hr], d[qq][2 * hr + 1]);
                             }
                     }
                     if (release) {
@@ -607,7 +654,7 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
     }
 }
 
-template <int kRank, bool kStaged, int kFeed>
+template <int kRank, bool kStaged, int kFeed, bool kF16>
 __global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
     sgmv_index_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmo_ld,
                       const __grid_constant__ SgmvParams p) {
@@ -653,13 +700,13 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
 
     uint32_t issued = 0;
     if (warp < kConsumerWarps) {
-        run_consumer<kRank>(warp, lane, p, uc, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end);
+        run_consumer<kRank, kF16>(warp, lane, p, uc, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end);
     } else {
         if (lane == 0) {
             prefetch_tmap(&tmx);
             prefetch_tmap(&tmo_ld);
         }
-        issued = run_feeder<kRank, kStaged, kFeed>(warp - kFirstFeedWarp, lane, p, uc, &tmx, &tmo_ld, tiles, facts,
+        issued = run_feeder<kRank, kStaged, kFeed, kF16>(warp - kFirstFeedWarp, lane, p, uc, &tmx, &tmo_ld, tiles, facts,
                                                    tab, lut_s, full, empty, abort, u_begin, u_end);
     }
     __syncthreads();
@@ -682,7 +729,7 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
 // Staged mode, phase 1: decode every routed sample's factor chunks once into the workspace,
 // in the exact 512-byte layout the decoder warps write into a stage (decode_chunk).  One warp
 // per (sample, chunk); every CTA builds the decode tables once and grid-strides.
-template <int kRank>
+template <int kRank, bool kF16>
 __global__ void __launch_bounds__(256) decode_chunks_kernel(const __grid_constant__ SgmvParams p, uint8_t* ws,
                                                             int32_t batch) {
     __shared__ DecodeTables tab;
@@ -709,7 +756,7 @@ __global__ void __launch_bounds__(256) decode_chunks_kernel(const __grid_constan
         const bool live = chunk_fetch<kRank>(p, un, c, lane, raw);
         uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
         if (live) finish_raw<LITHE_MAX_LEVELS>(c < un.nx ? p.ia : p.ib, raw, k, p.err);
-        decode_chunk<kRank>(p, &tab, lut_s, un, c, live, k, ws + w * kFactBytes, lane);
+        decode_chunk<kRank, kF16>(p, &tab, lut_s, un, c, live, k, ws + w * kFactBytes, lane);
     }
 }
 
@@ -761,11 +808,11 @@ __global__ void __launch_bounds__(256) decode_bdec_kernel(const __grid_constant_
     }
 }
 
-template <int kRank, bool kStaged, int kFeed = kStaged ? kFeedStaged : kDecodeWarps>
+template <int kRank, bool kStaged, bool kF16, int kFeed = kStaged ? kFeedStaged : kDecodeWarps>
 static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, const SgmvParams& p, int grid,
                            int device, int sms, int32_t batch, uint8_t* ws, cudaStream_t stream) {
     static bool configured[64] = {false};
-    auto kern = sgmv_index_kernel<kRank, kStaged, kFeed>;
+    auto kern = sgmv_index_kernel<kRank, kStaged, kFeed, kF16>;
     if (!configured[device]) {
         cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                              static_cast<int>(kSmemBytes));
@@ -776,7 +823,7 @@ static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, co
         const int64_t warps_needed = static_cast<int64_t>(batch) * p.n_chunks;
         int64_t blocks = (warps_needed + 7) / 8;
         if (blocks > 2LL * sms) blocks = 2LL * sms;
-        decode_chunks_kernel<kRank><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p, ws, batch);
+        decode_chunks_kernel<kRank, kF16><<<static_cast<unsigned>(blocks), 256, 0, stream>>>(p, ws, batch);
         cudaError_t e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "decode_chunks_kernel launch");
     }
@@ -805,18 +852,18 @@ static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, co
 constexpr int kSmallM = 8;
 constexpr int kSmallThreads = 256;
 
-__device__ __forceinline__ float bf16_round(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
-
+template <bool kF16>
 __device__ __forceinline__ void decode_block16(const float* lut_side, const uint32_t* k, int levels, float v[16]) {
     decode_eight<LITHE_MAX_LEVELS>(lut_side, k, levels, 0, v);
     decode_eight<LITHE_MAX_LEVELS>(lut_side, k, levels, 1, v + 8);
 #pragma unroll
-    for (int u = 0; u < 16; ++u) v[u] = bf16_round(v[u]);
+    for (int u = 0; u < 16; ++u) v[u] = Act<kF16>::round(v[u]);
 }
 
-template <int kRank, int kM>
-__global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const __nv_bfloat16* __restrict__ x,
+template <int kRank, int kM, bool kF16>
+__global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const uint16_t* __restrict__ x,
                                                                    const __grid_constant__ SgmvParams p) {
+    using T = Act<kF16>;
     constexpr int kCols = kSmallThreads / kRank;   // chunk stride of the shrink
     constexpr int kRowsPerBlock = 64 / kRank;      // output rows of one B block
     __shared__ float lut_s[kLutFloats];
@@ -844,7 +891,7 @@ __global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const __nv_bf
             uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
             fetch_indices<LITHE_MAX_LEVELS>(p.ia, sid, static_cast<int64_t>(r) * p.a_blocks_per_row + c, k, p.err);
             float a[16];
-            decode_block16(lut_s, k, p.ia.levels, a);
+            decode_block16<kF16>(lut_s, k, p.ia.levels, a);
 #pragma unroll
             for (int i = 0; i < kM; ++i) {
                 if (i < m) {
@@ -859,8 +906,8 @@ __global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const __nv_bf
                         const uint32_t ww[4] = {w.x, w.y, w.z, w.w};
 #pragma unroll
                         for (int j = 0; j < 4; ++j) {
-                            f[8 * (q & 1) + 2 * j] += bf16lo_to_f32(ww[j]);
-                            f[8 * (q & 1) + 2 * j + 1] += bf16hi_to_f32(ww[j]);
+                            f[8 * (q & 1) + 2 * j] += T::lo(ww[j]);
+                            f[8 * (q & 1) + 2 * j + 1] += T::hi(ww[j]);
                         }
                     }
                     float s = 0.f;
@@ -879,7 +926,7 @@ __global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const __nv_bf
         float s = 0.f;
         for (int c0 = 0; c0 < kCols; ++c0) s += part_s[i][rr + kRank * c0];
         const float sc = p.scaling * (p.weights ? __ldg(p.weights + b) : 1.0f);
-        h_s[i][rr] = active ? bf16_round(s * sc) : 0.f;
+        h_s[i][rr] = active ? T::round(s * sc) : 0.f;
     }
     __syncthreads();
 
@@ -891,7 +938,7 @@ __global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const __nv_bf
         if (active) {
             uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
             fetch_indices<LITHE_MAX_LEVELS>(p.ib, sid, G, k, p.err);
-            decode_block16(lut_b, k, p.ia.levels, v);
+            decode_block16<kF16>(lut_b, k, p.ia.levels, v);
         } else {
 #pragma unroll
             for (int u = 0; u < 16; ++u) v[u] = 0.f;
@@ -899,7 +946,7 @@ __global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const __nv_bf
 #pragma unroll
         for (int i = 0; i < kM; ++i) {
             if (i < m) {
-                __nv_bfloat16* orow = p.out + (static_cast<int64_t>(b) * m + i) * p.d_out + G * kRowsPerBlock;
+                const int64_t orow = (static_cast<int64_t>(b) * m + i) * p.d_out + G * kRowsPerBlock;
 #pragma unroll
                 for (int q0 = 0; q0 < kRowsPerBlock; q0 += 4) {   // 4 output rows = one 8-byte access
                     float d[4];
@@ -910,42 +957,48 @@ __global__ void __launch_bounds__(kSmallThreads) sgmv_small_kernel(const __nv_bf
                         for (int rr = 0; rr < kRank; ++rr) s = fmaf(h_s[i][rr], v[(kRank * (q0 + e) + rr) & 15], s);
                         d[e] = s;
                     }
-                    uint2* dst = reinterpret_cast<uint2*>(orow + q0);
+                    if (p.out_f32) {      // delta-only form with an fp32 output
+                        *reinterpret_cast<float4*>(static_cast<float*>(p.out) + orow + q0) =
+                            make_float4(d[0], d[1], d[2], d[3]);
+                        continue;
+                    }
+                    uint2* dst = reinterpret_cast<uint2*>(static_cast<uint16_t*>(p.out) + orow + q0);
                     uint2 o = make_uint2(0u, 0u);
                     if (p.accumulate) o = *dst;
-                    *dst = make_uint2(add_bf16x2(o.x, d[0], d[1]), add_bf16x2(o.y, d[2], d[3]));
+                    *dst = make_uint2(add_x2<kF16>(o.x, d[0], d[1]), add_x2<kF16>(o.y, d[2], d[3]));
                 }
             }
         }
     }
 }
 
-template <int kRank>
-static int32_t launch_small_rank(const __nv_bfloat16* x, const SgmvParams& p, int32_t batch, int sms,
+template <int kRank, bool kF16>
+static int32_t launch_small_rank(const uint16_t* x, const SgmvParams& p, int32_t batch, int sms,
                                  cudaStream_t stream) {
     // one B block per thread, but no more CTAs per sample than fill ~2 waves of the SMs
     const int64_t per_sample = (static_cast<int64_t>(p.b_blocks) + kSmallThreads - 1) / kSmallThreads;
     const int64_t fill = (2LL * sms + batch - 1) / batch;
     const int64_t split = per_sample < fill ? per_sample : (fill < 1 ? 1 : fill);
     const dim3 grid(static_cast<unsigned>(split), static_cast<unsigned>(batch));
-    if (p.m <= 1) sgmv_small_kernel<kRank, 1><<<grid, kSmallThreads, 0, stream>>>(x, p);
-    else if (p.m <= 2) sgmv_small_kernel<kRank, 2><<<grid, kSmallThreads, 0, stream>>>(x, p);
-    else if (p.m <= 4) sgmv_small_kernel<kRank, 4><<<grid, kSmallThreads, 0, stream>>>(x, p);
-    else sgmv_small_kernel<kRank, kSmallM><<<grid, kSmallThreads, 0, stream>>>(x, p);
+    if (p.m <= 1) sgmv_small_kernel<kRank, 1, kF16><<<grid, kSmallThreads, 0, stream>>>(x, p);
+    else if (p.m <= 2) sgmv_small_kernel<kRank, 2, kF16><<<grid, kSmallThreads, 0, stream>>>(x, p);
+    else if (p.m <= 4) sgmv_small_kernel<kRank, 4, kF16><<<grid, kSmallThreads, 0, stream>>>(x, p);
+    else sgmv_small_kernel<kRank, kSmallM, kF16><<<grid, kSmallThreads, 0, stream>>>(x, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "sgmv_small_kernel launch");
     return LITHE_OK;
 }
 
-static int32_t launch_small(const __nv_bfloat16* x, const SgmvParams& p, int32_t rank, int32_t batch, int sms,
+template <bool kF16>
+static int32_t launch_small(const uint16_t* x, const SgmvParams& p, int32_t rank, int32_t batch, int sms,
                             cudaStream_t stream) {
     if (batch > 65535) return fail_unsupported("the small-m form takes at most 65535 samples, got %d", batch);
     switch (rank) {
-        case 16: return launch_small_rank<16>(x, p, batch, sms, stream);
-        case 8: return launch_small_rank<8>(x, p, batch, sms, stream);
-        case 4: return launch_small_rank<4>(x, p, batch, sms, stream);
-        case 2: return launch_small_rank<2>(x, p, batch, sms, stream);
-        default: return launch_small_rank<1>(x, p, batch, sms, stream);
+        case 16: return launch_small_rank<16, kF16>(x, p, batch, sms, stream);
+        case 8: return launch_small_rank<8, kF16>(x, p, batch, sms, stream);
+        case 4: return launch_small_rank<4, kF16>(x, p, batch, sms, stream);
+        case 2: return launch_small_rank<2, kF16>(x, p, batch, sms, stream);
+        default: return launch_small_rank<1, kF16>(x, p, batch, sms, stream);
     }
 }
 
@@ -989,8 +1042,18 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
                         const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids, const float* weights,
                         int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank, const float* lut,
                         float scaling, int32_t* err_flag, void* ws, int64_t ws_bytes, void* stream,
-                        void* h_out = nullptr, void* bdec_out = nullptr, bool prep = false) {
+                        void* h_out = nullptr, void* bdec_out = nullptr, bool prep = false,
+                        int32_t x_dtype = LITHE_DTYPE_BF16, int32_t out_dtype = LITHE_DTYPE_BF16) {
     if (batch < 0 || m < 0) return fail_arg("batch (%d) and m (%d) must be >= 0", batch, m);
+    if (x_dtype != LITHE_DTYPE_BF16 && x_dtype != LITHE_DTYPE_F16)
+        return fail_unsupported("x_dtype must be LITHE_DTYPE_BF16 or LITHE_DTYPE_F16, got %d", x_dtype);
+    if (out_dtype != x_dtype && !(out_dtype == LITHE_DTYPE_F32 && !accumulate))
+        return fail_unsupported("out_dtype must be x's dtype, or LITHE_DTYPE_F32 when accumulate == 0 (got x %d, "
+                                "out %d, accumulate %d)", x_dtype, out_dtype, accumulate);
+    if (prep && x_dtype != LITHE_DTYPE_BF16) return fail_unsupported("lithe_lora_prep takes bf16 activations");
+    if (ws && out_dtype == LITHE_DTYPE_F32)
+        return fail_unsupported("the staged form writes the activation dtype; use lithe_sgmv_index_typed");
+    const bool f16 = x_dtype == LITHE_DTYPE_F16;
     if (rank != 1 && rank != 2 && rank != 4 && rank != 8 && rank != 16)
         return fail_unsupported("rank must be one of 1, 2, 4, 8, 16; got %d", rank);
     if (d_in <= 0 || d_in % 64) return fail_arg("d_in must be a positive multiple of 64, got %d", d_in);
@@ -1047,7 +1110,8 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     p.a_blocks_per_row = d_in / 64;
     p.b_blocks = static_cast<int32_t>(static_cast<int64_t>(d_out) * rank / 64);
     p.scaling = scaling;
-    p.out = static_cast<__nv_bfloat16*>(out);
+    p.out = out;
+    p.out_f32 = out_dtype == LITHE_DTYPE_F32 ? 1 : 0;
     expand_lut(lut, idx_a->num_levels, p.lut);
 
     p.n_chunks = p.n_xchunks + p.n_ochunks;
@@ -1061,7 +1125,10 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     }
     // A few token rows per sample (decode-time serving, modulation linears): the small-m form,
     // in every entry point (it needs no workspace, so the staged and fused modes agree).
-    if (!prep && m <= kSmallM) return launch_small(static_cast<const __nv_bfloat16*>(x), p, rank, batch, sms,
+    if (!prep && m <= kSmallM)
+        return f16 ? launch_small<true>(static_cast<const uint16_t*>(x), p, rank, batch, sms,
+                                        static_cast<cudaStream_t>(stream))
+                   : launch_small<false>(static_cast<const uint16_t*>(x), p, rank, batch, sms,
                                                           static_cast<cudaStream_t>(stream));
 
     CUtensorMap tmx, tmo_ld;
@@ -1111,12 +1178,14 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
     const int grid = static_cast<int>(p.total_units < sms ? p.total_units : sms);
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     uint8_t* w = static_cast<uint8_t*>(ws);
-#define LITHE_LAUNCH(R)                                                                         \
-    return ws ? launch_rank<R, true>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)          \
-              : launch_rank<R, false>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)
-    // Shrink-only form (lithe_lora_prep): every 8 KB x tile needs an A-chunk decode and no
-    // output tile is streamed, so the decode dominates; it runs with 8 decoder warps.
-    if (prep) return launch_rank<16, false, 2 * kDecodeWarps>(tmx, tmo_ld, p, grid, device, sms, batch, w, s);
+#define LITHE_LAUNCH(R)                                                                                     \
+    if (ws) return f16 ? launch_rank<R, true, true>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)               \
+                       : launch_rank<R, true, false>(tmx, tmo_ld, p, grid, device, sms, batch, w, s);             \
+    return f16 ? launch_rank<R, false, true>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)                      \
+               : launch_rank<R, false, false>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)
+    // Shrink-only form (lithe_lora_prep): every x tile needs an A-chunk decode and no output
+    // tile is streamed, so the decode dominates; it runs with 8 feeder warps.
+    if (prep) return launch_rank<16, false, false, 2 * kDecodeWarps>(tmx, tmo_ld, p, grid, device, sms, batch, w, s);
     switch (rank) {
         case 16: LITHE_LAUNCH(16);
         case 8: LITHE_LAUNCH(8);
@@ -1136,6 +1205,18 @@ extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate
     lithe::clear_error();
     return lithe::sgmv_index_impl(x, out, accumulate, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
                                   rank, lut, scaling, err_flag, nullptr, 0, stream);
+}
+
+extern "C" int32_t lithe_sgmv_index_typed(const void* x, void* out, int32_t accumulate,
+                                          const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                                          int64_t n_slots, const int32_t* ids, const float* weights, int32_t batch,
+                                          int32_t m, int32_t d_in, int32_t d_out, int32_t rank, const float* lut,
+                                          float scaling, int32_t x_dtype, int32_t out_dtype, int32_t* err_flag,
+                                          void* stream) {
+    lithe::clear_error();
+    return lithe::sgmv_index_impl(x, out, accumulate, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
+                                  rank, lut, scaling, err_flag, nullptr, 0, stream, nullptr, nullptr, false, x_dtype,
+                                  out_dtype);
 }
 
 extern "C" int32_t lithe_lora_prep(const void* x, const lithe_index_view* idx_a, const lithe_index_view* idx_b,

@@ -15,8 +15,9 @@ import torch
 
 from .. import _lib
 
-# Activation dtypes the sgmv kernels compute in.
-ACTIVATION_DTYPES = (torch.bfloat16,)
+# Activation dtypes the sgmv kernels compute in, and their C-ABI codes.
+ACTIVATION_DTYPES = (torch.bfloat16, torch.float16)
+_DTYPE_CODE = {torch.bfloat16: _lib.DTYPE_BF16, torch.float16: _lib.DTYPE_F16, torch.float32: _lib.DTYPE_F32}
 
 _err_words: dict = {}
 _err_lock = threading.Lock()
@@ -134,14 +135,18 @@ def sgmv_index_(x: torch.Tensor, out: torch.Tensor, *, accumulate: bool, view_a:
                 view_b: _lib.IndexView, n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor],
                 rank: int, lut: np.ndarray, scaling: float, err: Optional[torch.Tensor] = None,
                 mode: Optional[str] = None, workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """lithe_sgmv_index(_ws) on torch tensors; ``out`` (B, M, d_out) bf16 is written in place.
+    """lithe_sgmv_index(_typed, _ws) on torch tensors; ``out`` (B, M, d_out) is written in place.
 
-    ``mode`` "fused" or "staged" (None: DEFAULT_MODE); a staged call takes ``workspace``
-    (uint8 CUDA tensor) or allocates one from torch's caching allocator.
+    x is bfloat16 or float16; out has x's dtype, or float32 when ``accumulate`` is False (the
+    delta alone, lithe_sgmv_index_typed).  ``mode`` "fused" or "staged" (None: DEFAULT_MODE);
+    a staged call (bf16 only) takes ``workspace`` (uint8 CUDA tensor) or allocates one from
+    torch's caching allocator.
     """
     _require_cuda(x, "x")
-    if x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16:
-        raise TypeError(f"x and out must be bfloat16 (got {x.dtype}, {out.dtype})")
+    if x.dtype not in ACTIVATION_DTYPES:
+        raise TypeError(f"x must be one of {ACTIVATION_DTYPES}, got {x.dtype}")
+    if out.dtype != x.dtype and not (out.dtype == torch.float32 and not accumulate):
+        raise TypeError(f"out must have x's dtype ({x.dtype}), or float32 when not accumulating; got {out.dtype}")
     if x.dim() != 3 or out.dim() != 3 or x.shape[:2] != out.shape[:2]:
         raise ValueError(f"x (B, M, d_in) and out (B, M, d_out) disagree: {tuple(x.shape)} vs {tuple(out.shape)}")
     if not (x.is_contiguous() and out.is_contiguous()):
@@ -162,8 +167,14 @@ def sgmv_index_(x: torch.Tensor, out: torch.Tensor, *, accumulate: bool, view_a:
     common = (x.data_ptr(), out.data_ptr(), 1 if accumulate else 0, ctypes.byref(view_a), ctypes.byref(view_b),
               int(n_slots), ids.data_ptr(), weights.data_ptr() if weights is not None else None,
               bsz, m, d_in, out.shape[2], int(rank), lut_array(lut), float(scaling), err.data_ptr())
+    typed = x.dtype != torch.bfloat16 or out.dtype != torch.bfloat16
+    if typed and mode == "staged":
+        raise NotImplementedError("the staged form takes bfloat16 x and out")
     with torch.cuda.device(x.device):
-        if mode == "fused":
+        if typed:
+            rc = _lib.lib().lithe_sgmv_index_typed(*common[:-1], _DTYPE_CODE[x.dtype], _DTYPE_CODE[out.dtype],
+                                                   common[-1], stream_handle(x.device))
+        elif mode == "fused":
             rc = _lib.lib().lithe_sgmv_index(*common, stream_handle(x.device))
         else:
             need = workspace_bytes(bsz, d_in, out.shape[2])
@@ -172,7 +183,8 @@ def sgmv_index_(x: torch.Tensor, out: torch.Tensor, *, accumulate: bool, view_a:
             _require_cuda(workspace, "workspace")
             rc = _lib.lib().lithe_sgmv_index_ws(*common, workspace.data_ptr(), workspace.numel(),
                                                 stream_handle(x.device))
-    _lib.check(rc, "lithe_sgmv_index" if mode == "fused" else "lithe_sgmv_index_ws")
+    _lib.check(rc, "lithe_sgmv_index_typed" if typed else "lithe_sgmv_index" if mode == "fused"
+               else "lithe_sgmv_index_ws")
     return out
 
 

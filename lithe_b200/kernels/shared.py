@@ -50,15 +50,20 @@ def _bank(idx: torch.Tensor, device) -> torch.Tensor:
     return idx.to(device).contiguous()
 
 
-def _lut_list(pools_A: torch.Tensor, pools_B: torch.Tensor) -> list:
-    return [float(v) for v in cb.kernel_lut(pools_A, pools_B).reshape(-1)]
+def _lut_list(pools_A: torch.Tensor, pools_B: torch.Tensor, dtype: torch.dtype) -> list:
+    """The level LUT of the pools as the reference's kernel uses them: cast to the activation
+    dtype before decoding (lithe/kernels/shared.py:215-218).  Every pool entry is one of the
+    LUT's values, so rounding the LUT equals rounding the pools."""
+    lut = torch.from_numpy(cb.kernel_lut(pools_A, pools_B).reshape(-1))
+    return [float(v) for v in lut.to(dtype).float().tolist()]
 
 
 def shared_codebook_lora_delta_(out: torch.Tensor, x: torch.Tensor, idx_A: torch.Tensor, pools_A: torch.Tensor,
                                 idx_B: torch.Tensor, pools_B: torch.Tensor, assign: torch.Tensor, R: int,
                                 D_out: int, scaling: float, accumulate: bool = True,
                                 weights: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """out (B, M, D_out) bf16 += (or =, accumulate=False) the per-sample delta, in place.
+    """out (B, M, D_out) += (or =, accumulate=False) the per-sample delta, in place; out has
+    x's dtype (bf16 or fp16), or float32 with accumulate=False.
 
     ``weights`` (B,) fp32 multiplies each sample's delta (mixture gains); assign[b] < 0
     leaves sample b without a delta.  Out-of-range slots are reported in the device error
@@ -72,7 +77,7 @@ def shared_codebook_lora_delta_(out: torch.Tensor, x: torch.Tensor, idx_A: torch
     w = None if weights is None else weights.to(device=x.device, dtype=torch.float32).contiguous()
     torch.ops.lithe_b200.sgmv_index_(out, x.contiguous(), ia, ib, ops.view_params(_launch.level_major_view(ia)),
                                      ops.view_params(_launch.level_major_view(ib)), ia.shape[0], ids, w, R,
-                                     _lut_list(pools_A, pools_B), float(scaling), bool(accumulate))
+                                     _lut_list(pools_A, pools_B, x.dtype), float(scaling), bool(accumulate))
     return out
 
 
@@ -81,14 +86,19 @@ def shared_codebook_lora_delta(x: torch.Tensor, idx_A: torch.Tensor, pools_A: to
                                out_dtype: Optional[torch.dtype] = None) -> torch.Tensor:
     """Per-sample LoRA delta (B, M, D_out) decoded on the fly from index pools.
 
-    x (B, M, D_in) bfloat16 on a CUDA device; idx_A (n_slots, L, n_blocks_A) and idx_B
-    (n_slots, L, n_blocks_B) integer; pools (L, K, 64) float (any dtype, Hadamard
-    structure checked); assign (B,) slot per sample.  Returns a bfloat16 tensor.
+    x (B, M, D_in) bfloat16 or float16 on a CUDA device; idx_A (n_slots, L, n_blocks_A) and
+    idx_B (n_slots, L, n_blocks_B) integer; pools (L, K, 64) float (any dtype, Hadamard
+    structure checked; cast to x's dtype as the reference's kernel does); assign (B,) slot per
+    sample.  The delta comes back in ``out_dtype`` (default x.dtype): x's dtype, or float32,
+    which the kernel writes straight from its fp32 result.
     """
     _check(x, idx_A, pools_A, idx_B, pools_B, assign, R, D_out)
-    if out_dtype not in (None, torch.bfloat16):
-        raise NotImplementedError("the sm_100a kernel produces bfloat16 deltas")
-    out = torch.empty((x.shape[0], x.shape[1], D_out), dtype=torch.bfloat16, device=x.device)
+    out_dtype = x.dtype if out_dtype is None else out_dtype
+    if x.dtype not in _launch.ACTIVATION_DTYPES:
+        raise TypeError(f"x must be one of {_launch.ACTIVATION_DTYPES}, got {x.dtype}")
+    if out_dtype not in (x.dtype, torch.float32):
+        raise NotImplementedError(f"out_dtype must be x's dtype ({x.dtype}) or float32, got {out_dtype}")
+    out = torch.empty((x.shape[0], x.shape[1], D_out), dtype=out_dtype, device=x.device)
     return shared_codebook_lora_delta_(out, x, idx_A, pools_A, idx_B, pools_B, assign, R, D_out, scaling,
                                        accumulate=False)
 
