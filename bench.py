@@ -160,12 +160,29 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def kernel_source_digest() -> str:
+    """SHA-256 of the sources the fused SGMV kernel is built from (the recorded DRAM traffic is
+    valid only for the kernel it was captured on)."""
+    import hashlib
+    h = hashlib.sha256()
+    for name in ("sgmv_index.cu", "device_common.cuh", "host_common.cu"):
+        h.update((ROOT / "lithe_b200" / "csrc" / name).read_bytes())
+    return h.hexdigest()
+
+
 def traffic_per_launch():
-    """dram bytes per launch per shape from the committed ncu summary (None if not captured)."""
+    """(DRAM bytes per launch per shape, provenance) from the committed ncu record.  The figure
+    is a recorded one: it is used only while the kernel sources hash to the digest it was
+    captured with; otherwise (None, why)."""
     p = ROOT / "profiles" / "sgmv_index_flux_b14_traffic.json"
     if not p.exists():
-        return None
-    return json.loads(p.read_text()).get("dram_bytes_per_launch")
+        return None, "no recorded ncu capture"
+    rec = json.loads(p.read_text())
+    note = (f"recorded: ncu dram__bytes_read.sum + dram__bytes_write.sum of one launch per shape, captured at "
+            f"commit {rec.get('commit', '?')} ({rec.get('source', 'profiles/')})")
+    if rec.get("source_sha256") != kernel_source_digest():
+        return None, "stale: " + note + "; the kernel sources changed since, so no traffic is reported"
+    return rec.get("dram_bytes_per_launch"), note
 
 
 # --------------------------------------------------------------------------------------- CPU arm
@@ -233,47 +250,30 @@ def run_reference(args):
 
 
 # --------------------------------------------------------------------------------------- GPU arm
-def run_lithe(args):
+def _time_sweep(args, bank, slots, dev, world, local, seed):
+    """K timed steps of the four-shape sweep over ``slots`` (the samples this rank runs): one
+    fused decode+SGMV launch per shape per step, per-launch CUDA events on the launching
+    stream, max over ranks of the whole region.  Returns the timings and the device buffers."""
     from lithe_b200 import device_errors
-    from lithe_b200.kernels import PackedBank, PackedLayout, packed_codebook_lora_delta_
-
-    world, rank, local = dist_env()
-    init_dist(world, local)
-    dev = torch.device("cuda", local)
-    layout = PackedLayout.from_modules(modules())
-    bank = PackedBank(layout, BANK_SLOTS, dev)
-    bank.fill_random(seed=1234)                                  # replicated: identical on every rank
-    if args.shard_batch:
-        # strong scaling: the fixed B=14 batch is split by sample across the ranks
-        from lithe_b200.shard import shard_bounds
-        lo, hi = shard_bounds(BATCH, world, rank)
-        slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100))[:BATCH][lo:hi]
-    else:
-        slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100 + rank))[:BATCH]
-    nb = int(slots.numel())                                      # samples this rank runs
+    from lithe_b200.kernels import packed_codebook_lora_delta_
+    nb = int(slots.numel())
     ids = slots.to(torch.int32).to(dev)
     g = torch.Generator(device=dev)
-    g.manual_seed(10 + rank)
+    g.manual_seed(seed)
     xs = [torch.randn(nb, TOKENS, a, generator=g, device=dev, dtype=torch.bfloat16) for a, _ in SHAPES]
     outs = [(torch.randn(nb, TOKENS, b, generator=g, device=dev, dtype=torch.bfloat16) * 0.05) for _, b in SHAPES]
-    names = layout.names
+    names = bank.layout.names
     stream = torch.cuda.current_stream(dev)
 
-    def step(evs=None):
-        for i in range(len(SHAPES)):
-            if evs is not None:
-                evs[i][0].record(stream)
-            packed_codebook_lora_delta_(outs[i], xs[i], bank, names[i], ids, scaling=1.0)
-            if evs is not None:
-                evs[i][1].record(stream)
+    def call(i):
+        packed_codebook_lora_delta_(outs[i], xs[i], bank, names[i], ids, scaling=1.0)
 
     for _ in range(args.warmup):
-        step()
+        for i in range(len(SHAPES)):
+            call(i)
     torch.cuda.synchronize(dev)
     if device_errors(dev):
         raise RuntimeError("kernel reported a device error during warm-up")
-
-    # ---- device-timed region: K steps, per-launch events on the launching stream
     evs = [[(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
             for _ in SHAPES] for _ in range(args.steps)]
     t_start, t_end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -282,24 +282,53 @@ def run_lithe(args):
     with ClockSampler(local) as clocks:
         t_start.record(stream)
         for k in range(args.steps):
-            step(evs[k])
+            for i in range(len(SHAPES)):
+                evs[k][i][0].record(stream)
+                call(i)
+                evs[k][i][1].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize(dev)
     barrier(world)
-    total_ms = t_start.elapsed_time(t_end)
-    total_ms = max_over_ranks(total_ms, world)
-    ms_per_step = total_ms / args.steps
+    total_ms = max_over_ranks(t_start.elapsed_time(t_end), world)
     per_shape_ms = [statistics.mean(evs[k][i][0].elapsed_time(evs[k][i][1]) for k in range(args.steps))
                     for i in range(len(SHAPES))]
+    return {"nb": nb, "ids": ids, "xs": xs, "outs": outs, "ms_per_step": total_ms / args.steps,
+            "per_shape_ms": per_shape_ms, "clocks": clocks.summary(), "call": call}
+
+
+def run_lithe(args):
+    from lithe_b200 import device_errors
+    from lithe_b200.kernels import PackedBank, PackedLayout, packed_codebook_lora_delta_
+    from lithe_b200.shard import bind_host_to_gpu, imbalance, shard_bounds, shard_sizes
+
+    world, rank, local = dist_env()
+    init_dist(world, local)
+    dev = torch.device("cuda", local)
+    # host threads and pinned staging buffers on the GPU's NUMA node (before any pinned allocation)
+    numa_node = bind_host_to_gpu(local)
+    layout = PackedLayout.from_modules(modules())
+    bank = PackedBank(layout, BANK_SLOTS, dev)
+    bank.fill_random(seed=1234)                                  # replicated: identical on every rank
+    # Headline: the fixed B=14 batch split by sample across the ranks (strong scaling, the
+    # sharding of the benchmark spec's config 5); with --scaling weak every rank runs its own B=14.
+    strong = args.scaling == "strong"
+    batch_slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100))[:BATCH]
+    if strong:
+        lo, hi = shard_bounds(BATCH, world, rank)
+        slots = batch_slots[lo:hi]
+    else:
+        slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100 + rank))[:BATCH]
+    head = _time_sweep(args, bank, slots, dev, world, local, seed=10 + rank)
+    nb, xs, outs, ids = head["nb"], head["xs"], head["outs"], head["ids"]
+    ms_per_step, per_shape_ms, sweep_clocks = head["ms_per_step"], head["per_shape_ms"], head["clocks"]
     from lithe_b200.kernels import _launch as _lk
     mode = _lk.DEFAULT_MODE
     launches = args.steps * len(SHAPES) * (2 if mode == "staged" else 1)
-    tokens_per_step = len(SHAPES) * BATCH * TOKENS * (1 if args.shard_batch else world)
+    tokens_per_step = len(SHAPES) * (BATCH if strong else BATCH * world) * TOKENS
     value = tokens_per_step / (ms_per_step / 1000.0)
 
     # ---- end-to-end through the public API with host buffers (pinned), copies timed
     max_in = max(a for a, _ in SHAPES)
-    max_out = max(b for _, b in SHAPES)
     if not args.no_e2e:
         # x is only read from the host, so the shapes share one buffer; each shape's output has
         # its own, written back every step and read again as the next step's base output
@@ -310,6 +339,7 @@ def run_lithe(args):
             o.normal_().mul_(0.05)
     h2d = sum(nb * TOKENS * (a + b) * 2 for a, b in SHAPES)
     d2h = sum(nb * TOKENS * b * 2 for _, b in SHAPES)
+    stream = torch.cuda.current_stream(dev)
     # Copies in on one stream, the call on the current stream, copies out on a third: PCIe is
     # full duplex, so one shape's output read-back overlaps the next shape's input upload.
     copy_in, copy_out = torch.cuda.Stream(dev), torch.cuda.Stream(dev)
@@ -327,7 +357,7 @@ def run_lithe(args):
                 uploaded = torch.cuda.Event()
                 uploaded.record(copy_in)
             stream.wait_event(uploaded)
-            packed_codebook_lora_delta_(outs[i], xs[i], bank, names[i], ids, scaling=1.0)
+            packed_codebook_lora_delta_(outs[i], xs[i], bank, layout.names[i], ids, scaling=1.0)
             done_call[i] = torch.cuda.Event()
             done_call[i].record(stream)
             with torch.cuda.stream(copy_out):
@@ -354,7 +384,19 @@ def run_lithe(args):
         torch.cuda.synchronize(dev)
         barrier(world)
         e2e_ms = max_over_ranks(e0.elapsed_time(e1) / e2e_steps, world)
+        del x_host, o_hosts
     errors = device_errors(dev)
+    del head, xs, outs
+
+    # ---- secondary: weak scaling (every rank its own B=14), only meaningful for N > 1
+    weak = None
+    if world > 1 and strong:
+        wk = _time_sweep(args, bank, torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100 + rank))[
+            :BATCH], dev, world, local, seed=20 + rank)
+        weak = {"value": len(SHAPES) * BATCH * world * TOKENS / (wk["ms_per_step"] / 1000.0), "unit": "tokens/s",
+                "ms_per_step": wk["ms_per_step"], "parallelism": f"dp{world}: every rank its own B=14 batch"}
+        del wk
+    errors |= device_errors(dev)
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
@@ -363,7 +405,7 @@ def run_lithe(args):
     peak, peak_kind = measured_peaks()
     alg = [algorithmic_bytes(a, b, batch=nb, distinct=nb) for a, b in SHAPES]
     achieved = sum(alg) / (sum(per_shape_ms) / 1000.0) / 1e9
-    traffic = traffic_per_launch()
+    traffic, traffic_note = traffic_per_launch()
     shapes_out = []
     for i, (a, b) in enumerate(SHAPES):
         key = f"{a}x{b}"
@@ -373,36 +415,50 @@ def run_lithe(args):
                            "tflops": flops(a, b, batch=nb) / (per_shape_ms[i] / 1e3) / 1e12,
                            "dram_bytes": None if traffic is None else traffic.get(key)})
     mean_traffic = None
-    if traffic is not None and all(s["dram_bytes"] is not None for s in shapes_out):
-        mean_traffic = sum(s["dram_bytes"] for s in shapes_out) / len(shapes_out)
+    if traffic is not None and all(s_["dram_bytes"] is not None for s_ in shapes_out):
+        # the recorded per-launch traffic is for B=14; scale it to the samples this rank ran
+        mean_traffic = sum(s_["dram_bytes"] for s_ in shapes_out) / len(shapes_out) * nb / BATCH
+
+    # ---- the metric's second half: the 28-step 1024^2 B=14 denoise, sharded by sample
+    denoise = None
+    del bank
+    torch.cuda.empty_cache()
+    if not args.no_denoise:
+        denoise = denoise_record(world, rank, local, dev)
 
     if rank == 0:
+        sizes = shard_sizes(BATCH, world)
         line = {
             "metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
             "warmup": args.warmup, "ms_per_step": ms_per_step, "higher_is_better": True,
-            "scaling": "strong" if args.shard_batch else "weak",
-            "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: seeded uniform 9-bit packed indices (10,000-slot bank), x ~ N(0,1) bf16",
             "config": {"workload": "flux_sweep_b14", "shapes": [f"{a}->{b}" for a, b in SHAPES], "batch": BATCH,
                        "tokens_per_sample": TOKENS, "rank": RANK, "bank_slots": BANK_SLOTS,
-                       "distinct_adapters": BATCH, "parallelism": (f"B=14 split by sample over {world} ranks (rank 0 runs {nb})" if args.shard_batch
+                       "distinct_adapters": BATCH,
+                       "parallelism": (f"B=14 split by sample over {world} ranks ({','.join(map(str, sizes))}; "
+                                       f"max/mean {imbalance(BATCH, world):.2f})" if strong
                                        else f"dp{world}: every rank runs its own B=14 batch") + ", bank replicated",
-                       "l2": "inputs larger than L2 (>= 396 MB of activations per launch), no flush",
-                       "mode": mode},
+                       "l2": "inputs larger than L2 (>= 396 MB of activations per launch at B=14), no flush",
+                       "mode": mode, "host_numa_node": numa_node},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                          "peak_source": f"hbm_gbs of {peak_kind}", "traffic": mean_traffic,
+                         "traffic_source": traffic_note,
                          "algorithmic_bytes_per_launch": sum(alg) / len(alg),
                          "kernel": "lithe::sgmv_index_kernel<16, staged>" if mode == "staged" else "lithe::sgmv_index_kernel<16, fused>",
-                         "timed": "the whole op per launch" + (" (decode_chunks_kernel + sgmv_index_kernel)" if mode == "staged" else "")},
+                         "timed": "the whole op per launch, rank 0" + (" (decode_chunks_kernel + sgmv_index_kernel)" if mode == "staged" else "")},
             "cpu_baseline": cpu,
             "e2e": None if e2e_ms is None else {
                 "value": tokens_per_step / (e2e_ms / 1000.0), "unit": "tokens/s",
                 "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h, "ms_per_step": e2e_ms,
-                "api": "lithe_b200.kernels.packed_codebook_lora_delta_ (C ABI lithe_sgmv_index), pinned host buffers; "
-                       "uploads, calls and read-backs on three streams (one shape's read-back overlaps the next upload)"},
-            "clocks": clocks.summary(),
+                "api": "lithe_b200.kernels.packed_codebook_lora_delta_ (C ABI lithe_sgmv_index), pinned host buffers "
+                       "on the GPU's NUMA node; uploads, calls and read-backs on three streams (one shape's read-back "
+                       "overlaps the next upload); bytes are rank 0's"},
+            "clocks": sweep_clocks,
             "gpu_launches": launches,
             "per_shape": shapes_out,
+            "weak_scaling": weak,
+            "denoise": denoise,
             "device_errors": errors,
         }
         print(json.dumps(line), flush=True)
@@ -556,6 +612,167 @@ def run_decode(args):
 
 
 # --------------------------------------------------------------------------------------- denoise workloads
+
+
+class _DenoiseSetup:
+    """A random-init FLUX.1-dev-shaped transformer (bf16) with every LoRA target linear served four
+    ways, swapped in place: base only (cuBLAS); index-resident LoRA from a 9-bit packed
+    10,000-slot bank (``PackedLoRALinear``, cuBLAS + the fused decode/SGMV kernel, or with
+    ``fused_gemm`` lithe_lora_prep + the expand inside lithe_lora_gemm); a dense resident-LoRA
+    comparator (the batch's decoded bf16 factors resident in HBM, cuBLAS bmm + in-place baddbmm);
+    and a diagnostic with the base linears on lithe_lora_gemm without LoRA.  Samples [lo, hi) of
+    the batch run on this rank; the bank and the base weights are identical on every rank."""
+
+    def __init__(self, dev, img_tok, txt_tok, batch, key_format, lo, hi, slot_seed, input_seed):
+        from lithe_b200 import kohya
+        from lithe_b200.flux_model import FluxShapedTransformer, lora_targets
+        from lithe_b200.kernels import PackedBank, PackedLayout, PackedLoRALinear, PerSampleLoRALinear, split_decoded
+        from lithe_b200.kernels import _launch as _launch_k
+
+        torch.manual_seed(0)
+        with torch.device(dev):
+            model = FluxShapedTransformer()
+        self.model = model.to(torch.bfloat16).eval()
+        if key_format == "kohya":
+            layout = PackedLayout.from_modules(kohya.kohya_flux_modules(rank=RANK))
+            split = kohya.split_targets(layout.names, layout.shapes_a, layout.shapes_b, "kohya")
+            targets = [(path, self.model.get_submodule(path)) for path in split]
+        else:
+            targets = lora_targets(self.model)
+            layout = PackedLayout.from_modules([{"name": n, "shape_a": [RANK, m.in_features],
+                                                 "shape_b": [m.out_features, RANK]} for n, m in targets])
+            split = None
+        bank = PackedBank(layout, BANK_SLOTS, dev)
+        bank.fill_random(seed=1234)
+        slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(slot_seed))[:batch][lo:hi]
+        self.nb = int(slots.numel())
+        g = torch.Generator(device=dev)
+        g.manual_seed(input_seed)
+        self.inputs = (torch.randn(batch, img_tok, 64, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous(),
+                       torch.randn(batch, txt_tok, 4096, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous(),
+                       torch.randn(batch, 768, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous())
+        self.names = [n for n, _ in targets]
+        bases = {n: m for n, m in targets}
+
+        def _packed(path):
+            if split is None:
+                return PackedLoRALinear(bases[path], bank, path, RANK, 1.0)
+            name, r0, r1 = split[path]
+            full = r0 == 0 and r1 == layout.shapes_b[layout.index(name)][0]
+            return PackedLoRALinear(bases[path], bank, name, RANK, 1.0, rows=None if full else (r0, r1))
+
+        packed = {n: _packed(n) for n in self.names}
+        ids = slots.to(torch.int32).to(dev)
+        for m in packed.values():
+            m.assign = ids
+        dec = bank.decode(ids, dtype=torch.bfloat16)                   # the dense comparator's resident factors
+        per = [split_decoded(dec[i], layout) for i in range(self.nb)]
+        if split is not None:
+            per = [kohya.split_factors(p_) for p_ in per]
+        dense = {}
+        for n in self.names:
+            d = PerSampleLoRALinear(bases[n], "sgmv")
+            d.set_factors([(p[n][0].contiguous(), p[n][1].contiguous(), 1.0) for p in per])
+            d._build_stacked(torch.bfloat16)
+            dense[n] = d
+        del dec, per
+
+        class _PlainGemm(torch.nn.Module):
+            """The base linear on lithe_lora_gemm without a LoRA term, on the linears where the
+            fused path uses it (the rest stay on cuBLAS): the GEMM's own cost, apart from LoRA."""
+
+            def __init__(self, lin, gate):
+                super().__init__()
+                self.lin, self.gate = lin, gate
+
+            def forward(self, x):
+                x3 = x.unsqueeze(1) if x.dim() == 2 else x
+                if not self.gate._gemm_ok(x3):
+                    return self.lin(x)
+                x2 = x3.contiguous().view(-1, x3.shape[-1])
+                out = torch.empty(x2.shape[0], self.lin.out_features, dtype=x.dtype, device=x.device)
+                _launch_k.lora_gemm_(x2, self.lin.weight, self.lin.bias, out)
+                return out.view(*x.shape[:-1], self.lin.out_features)
+
+        plain = {n: _PlainGemm(bases[n], packed[n]) for n in self.names}
+        self.packed = packed
+        self.tables = {"base": bases, "plain_gemm": plain, "lithe": packed, "lithe_fused": packed,
+                       "lithe_fused_all": packed, "dense": dense}
+
+    def install(self, kind):
+        from lithe_b200.kernels.layers import FUSED_GEMM_MAX_K
+        for m in self.packed.values():
+            m.fused_gemm = kind.startswith("lithe_fused")
+            # lithe_fused: the default policy (in_features <= FUSED_GEMM_MAX_K); _all: every eligible linear
+            m.fused_gemm_max_k = None if kind in ("lithe_fused_all", "plain_gemm") else FUSED_GEMM_MAX_K
+        wrap_linears_any(self.model, self.names, self.tables[kind])
+
+    def time_abba(self, kinds, steps, world, local, dev):
+        """Wall time (s, max over ranks) of a ``steps``-step denoise per variant, in ABBA order:
+        the GPU runs under its power cap and its clocks drift as it heats up, so each variant is
+        timed once on the way out and once on the way back and the two are averaged (a linear
+        drift cancels).  Returns (mean per kind, passes per kind, clock summaries per kind)."""
+        from lithe_b200.flux_model import denoise
+        stream = torch.cuda.current_stream(dev)
+        runs = {k: [] for k in kinds}
+        clock_log = {k: [] for k in kinds}
+        with torch.no_grad():
+            for kind in tuple(kinds) + tuple(reversed(kinds)):
+                self.install(kind)
+                denoise(self.model, *self.inputs, 1)                      # warm-up (one step)
+                torch.cuda.synchronize(dev)
+                barrier(world)
+                e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+                with ClockSampler(local) as clocks:
+                    e0.record(stream)
+                    denoise(self.model, *self.inputs, steps)
+                    e1.record(stream)
+                    torch.cuda.synchronize(dev)
+                barrier(world)
+                runs[kind].append(max_over_ranks(e0.elapsed_time(e1) / 1000.0, world))
+                clock_log[kind].append(clocks.summary())
+        return {k: sum(v) / len(v) for k, v in runs.items()}, runs, clock_log
+
+
+DENOISE_RECORD = (4096, 512, 14, 28)       # 1024^2: image tokens, text tokens, batch, steps (config 5)
+
+
+def denoise_record(world, rank, local, dev):
+    """The second half of the metric, in the default bench line: the 28-step 1024^2 B=14
+    heterogeneous denoise on the random-init FLUX-shaped model, the B=14 batch split by sample
+    over the ranks (config 5), three variants in ABBA order: base only, LITHE with the default
+    policy (lithe_lora_prep + the expand inside lithe_lora_gemm for in_features <= 4096, cuBLAS +
+    the fused decode/SGMV kernel elsewhere), and the dense resident-LoRA comparator."""
+    from lithe_b200.shard import shard_bounds, shard_sizes
+    img_tok, txt_tok, batch, steps = DENOISE_RECORD
+    lo, hi = shard_bounds(batch, world, rank)
+    setup = _DenoiseSetup(dev, img_tok, txt_tok, batch, "diffusers", lo, hi, slot_seed=300, input_seed=7)
+    kinds = ("base", "lithe_fused", "dense")
+    mean, runs, clocks = setup.time_abba(kinds, steps, world, local, dev)
+    t_base, t_lithe, t_dense = mean["base"], mean["lithe_fused"], mean["dense"]
+    rec = {
+        "metric": f"{steps}-step denoise wall time", "unit": "s", "higher_is_better": False,
+        "config": {"image": "1024^2", "image_tokens": img_tok, "text_tokens": txt_tok, "batch": batch, "steps": steps,
+                   "lora_linears": len(setup.names), "adapter_format": "diffusers-342", "bank_slots": BANK_SLOTS,
+                   "distinct_adapters": batch, "model": "random-init FLUX.1-dev-shaped transformer (19 double + 38 "
+                   "single blocks, hidden 3072; rotary embeddings left out), bf16",
+                   "parallelism": f"B={batch} split by sample over {world} ranks "
+                                  f"({','.join(map(str, shard_sizes(batch, world)))}), bank replicated"},
+        "lithe_s": t_lithe, "base_s": t_base, "dense_resident_lora_s": t_dense,
+        "lithe_lora_overhead_s": t_lithe - t_base, "dense_lora_overhead_s": t_dense - t_base,
+        "overhead_ratio_lithe_vs_dense": (t_lithe - t_base) / max(1e-9, t_dense - t_base),
+        "lithe_path": "PackedLoRALinear(fused_gemm=True): lithe_lora_prep + lithe_lora_gemm (expand inside the tcgen05 "
+                      "base GEMM) on linears with in_features <= 4096, cuBLAS + the fused decode/SGMV kernel on the rest",
+        "passes_s": runs, "order": "ABBA: " + " ".join(kinds + tuple(reversed(kinds))),
+        "clocks": {k: v for k, v in clocks.items()}, "timing": "CUDA events around the whole loop, max over ranks",
+        "reference_published": {"value": 133.4, "unit": "s", "hardware": "A100", "note":
+                                "the reference's README render time for a real FLUX.1-dev 1024^2 render "
+                                "(not this synthetic model, which omits RoPE)"}}
+    del setup
+    torch.cuda.empty_cache()
+    return rec
+
+
 DENOISE = {  # workload -> (image tokens, text tokens, batch, steps, adapter key format)
     "denoise_512": (1024, 512, 14, 16, "diffusers"),        # config 3: 512^2, B=14, 16 steps
     "denoise_256_b96": (256, 512, 96, 4, "diffusers"),      # config 4: 256^2, B=96 distinct adapters, 4 steps
@@ -567,19 +784,12 @@ DENOISE = {  # workload -> (image tokens, text tokens, batch, steps, adapter key
 
 
 def run_denoise(args):
-    """Full denoise loop on a random-init FLUX.1-dev-shaped transformer (bf16), five ways: base
-    only (cuBLAS), the base on lithe_lora_gemm without LoRA (diagnostic), index-resident LoRA
-    on every target linear from a 9-bit packed 10,000-slot bank -- cuBLAS + the fused
-    decode/SGMV kernel, and lithe_lora_prep + lithe_lora_gemm with the expand inside the GEMM --
-    and a dense resident-LoRA comparator (decoded bf16 factors of the batch's adapters resident
-    in HBM, cuBLAS bmm + in-place baddbmm per linear).  Targets: the 342 diffusers linears, or
-    the 494 linears a Kohya-304 adapter covers (its fused q/k/v modules served in place)."""
-    from lithe_b200.flux_model import FluxShapedTransformer, denoise, lora_targets
-    from lithe_b200.kernels.layers import FUSED_GEMM_MAX_K
-    from lithe_b200.kernels import (PackedBank, PackedLayout, PackedLoRALinear, PerSampleLoRALinear, split_decoded,
-                                    wrap_linears)
+    """The denoise workloads with all six variants (base, plain tcgen05 GEMM without LoRA, LITHE
+    cuBLAS + decode/SGMV, LITHE fused GEMM with the default in_features policy, fused GEMM on
+    every eligible linear, dense resident LoRA), ABBA order.  Targets: the 342 diffusers
+    linears, or the 494 linears a Kohya-304 adapter covers (its fused q/k/v modules served in
+    place)."""
     from lithe_b200.shard import shard_bounds
-
     img_tok, txt_tok, batch, steps, key_format = DENOISE[args.workload]
     world, rank, local = dist_env()
     if args.impl == "reference":
@@ -590,107 +800,14 @@ def run_denoise(args):
         return
     init_dist(world, local)
     dev = torch.device("cuda", local)
-    torch.manual_seed(0)
-    model = FluxShapedTransformer().to(device=dev, dtype=torch.bfloat16).eval()
-    if key_format == "kohya":
-        from lithe_b200 import kohya
-        layout = PackedLayout.from_modules(kohya.kohya_flux_modules(rank=RANK))
-        split = kohya.split_targets(layout.names, layout.shapes_a, layout.shapes_b, "kohya")
-        targets = [(path, model.get_submodule(path)) for path in split]
-    else:
-        targets = lora_targets(model)
-        layout = PackedLayout.from_modules([{"name": n, "shape_a": [RANK, m.in_features],
-                                             "shape_b": [m.out_features, RANK]} for n, m in targets])
-    bank = PackedBank(layout, BANK_SLOTS, dev)
-    bank.fill_random(seed=1234)
-    lo, hi = shard_bounds(batch, world, rank) if args.shard_batch else (0, batch)
-    slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(300 if args.shard_batch else 300 + rank))[:batch][lo:hi]
-    nb = int(slots.numel())
-    g = torch.Generator(device=dev)
-    g.manual_seed(7 + (0 if args.shard_batch else rank))
-    lat = torch.randn(batch, img_tok, 64, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous()
-    txt = torch.randn(batch, txt_tok, 4096, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous()
-    pooled = torch.randn(batch, 768, generator=g, device=dev, dtype=torch.bfloat16)[lo:hi].contiguous()
-    names = [n for n, _ in targets]
-    bases = {n: m for n, m in targets}
-    if key_format == "kohya":
-        def _packed(path):
-            name, r0, r1 = split[path]
-            full = r0 == 0 and r1 == layout.shapes_b[layout.index(name)][0]
-            return PackedLoRALinear(bases[path], bank, name, RANK, 1.0, rows=None if full else (r0, r1))
-        packed = {n: _packed(n) for n in names}
-    else:
-        packed = {n: PackedLoRALinear(bases[n], bank, n, RANK, 1.0) for n in names}
-    ids = slots.to(torch.int32).to(dev)
-    for m in packed.values():
-        m.assign = ids
-    dec = bank.decode(ids, dtype=torch.bfloat16)                   # the dense comparator's resident factors
-    per = [split_decoded(dec[i], layout) for i in range(nb)]
-    if key_format == "kohya":
-        per = [kohya.split_factors(p_) for p_ in per]
-    dense = {}
-    for n in names:
-        d = PerSampleLoRALinear(bases[n], "sgmv")
-        d.set_factors([(p[n][0].contiguous(), p[n][1].contiguous(), 1.0) for p in per])
-        d._build_stacked(torch.bfloat16)
-        dense[n] = d
-    del dec, per
-
-    from lithe_b200.kernels import _launch as _launch_k
-
-    class _PlainGemm(torch.nn.Module):
-        """The base linear on lithe_lora_gemm without a LoRA term, on the linears where the fused
-        path uses it (the rest stay on cuBLAS): separates the GEMM's own cost from the LoRA work."""
-
-        def __init__(self, lin, gate):
-            super().__init__()
-            self.lin, self.gate = lin, gate
-
-        def forward(self, x):
-            x3 = x.unsqueeze(1) if x.dim() == 2 else x
-            if not self.gate._gemm_ok(x3):
-                return self.lin(x)
-            x2 = x3.contiguous().view(-1, x3.shape[-1])
-            out = torch.empty(x2.shape[0], self.lin.out_features, dtype=x.dtype, device=x.device)
-            _launch_k.lora_gemm_(x2, self.lin.weight, self.lin.bias, out)
-            return out.view(*x.shape[:-1], self.lin.out_features)
-
-    plain = {n: _PlainGemm(bases[n], packed[n]) for n in names}
-
-    def install(kind):
-        table = {"base": bases, "plain_gemm": plain, "lithe": packed, "lithe_fused": packed, "lithe_fused_all": packed,
-                 "dense": dense}[kind]
-        for m in packed.values():
-            m.fused_gemm = kind.startswith("lithe_fused")
-            # lithe_fused: the default policy (in_features <= FUSED_GEMM_MAX_K); _all: every eligible linear
-            m.fused_gemm_max_k = None if kind in ("lithe_fused_all", "plain_gemm") else FUSED_GEMM_MAX_K
-        wrap_linears_any(model, names, table)
-
-    stream = torch.cuda.current_stream(dev)
-    # ABBA order: the GPU runs under its power cap and its clocks drift as it heats up, so each
-    # variant is timed once on the way out and once on the way back and the two are averaged
-    # (a linear drift cancels); both passes are reported.
+    strong = args.scaling == "strong"
+    lo, hi = shard_bounds(batch, world, rank) if strong else (0, batch)
+    setup = _DenoiseSetup(dev, img_tok, txt_tok, batch, key_format, lo, hi,
+                          slot_seed=300 if strong else 300 + rank, input_seed=7 + (0 if strong else rank))
     kinds = ("base", "plain_gemm", "lithe", "lithe_fused", "lithe_fused_all", "dense")
-    runs = {k: [] for k in kinds}
-    clock_log = {k: [] for k in kinds}
-    with torch.no_grad():
-        for kind in kinds + tuple(reversed(kinds)):
-            install(kind)
-            denoise(model, lat, txt, pooled, 1)                       # warm-up (one step)
-            torch.cuda.synchronize(dev)
-            barrier(world)
-            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            with ClockSampler(local) as clocks:
-                e0.record(stream)
-                denoise(model, lat, txt, pooled, steps)
-                e1.record(stream)
-                torch.cuda.synchronize(dev)
-            barrier(world)
-            runs[kind].append(max_over_ranks(e0.elapsed_time(e1) / 1000.0, world))
-            clock_log[kind].append(clocks.summary())
-    results = {k: (sum(v) / len(v), clock_log[k][0]) for k, v in runs.items()}
-    t_base, t_lithe, t_dense = results["base"][0], results["lithe"][0], results["dense"][0]
-    t_fused = results["lithe_fused"][0]
+    mean, runs, clock_log = setup.time_abba(kinds, steps, world, local, dev)
+    t_base, t_lithe, t_dense = mean["base"], mean["lithe"], mean["dense"]
+    t_fused = mean["lithe_fused"]
     if rank == 0:
         print(json.dumps({
             "metric": f"{steps}-step denoise wall time", "value": t_fused, "unit": "s", "n_gpus": world, "steps": steps,
@@ -698,26 +815,25 @@ def run_denoise(args):
             "lora_path": "PackedLoRALinear(fused_gemm=True): lithe_lora_prep + lithe_lora_gemm (expand inside the "
                          "tcgen05 base GEMM) on linears with in_features <= 4096, cuBLAS + the fused decode/SGMV "
                          "kernel on the rest; lithe_s is cuBLAS + decode/SGMV everywhere",
-            "scaling": "strong" if args.shard_batch else "weak", "vs_baseline": None, "dtype": "bf16",
+            "scaling": "strong" if strong else "weak", "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic: random-init FLUX.1-dev-shaped transformer, seeded uniform 9-bit packed adapters",
             "config": {"workload": args.workload, "image_tokens": img_tok, "text_tokens": txt_tok, "batch": batch,
-                       "rank_batch": nb, "lora_linears": len(names), "bank_slots": BANK_SLOTS,
+                       "rank_batch": setup.nb, "lora_linears": len(setup.names), "bank_slots": BANK_SLOTS,
                        "adapter_format": key_format + ("-304 (all 494 linears; fused q/k/v share h)"
                                                        if key_format == "kohya" else "-342"),
-                       "parallelism": (f"B={batch} split by sample over {world} ranks" if args.shard_batch
+                       "parallelism": (f"B={batch} split by sample over {world} ranks" if strong
                                        else f"dp{world}: every rank its own B={batch}") + ", bank replicated"},
             "base_only_s": t_base, "lithe_s": t_lithe, "dense_resident_lora_s": t_dense,
             "lithe_lora_overhead_s": t_lithe - t_base, "dense_lora_overhead_s": t_dense - t_base,
             "overhead_ratio_lithe_vs_dense": (t_lithe - t_base) / max(1e-9, t_dense - t_base),
             "lithe_fused_gemm_s": t_fused, "lithe_fused_gemm_lora_overhead_s": t_fused - t_base,
             "overhead_ratio_fused_gemm_vs_dense": (t_fused - t_base) / max(1e-9, t_dense - t_base),
-            "clocks_fused_gemm": results["lithe_fused"][1],
-            "plain_gemm_base_s": results["plain_gemm"][0],
-            "lithe_fused_all_s": results["lithe_fused_all"][0],
-            "overhead_ratio_fused_all_vs_dense": (results["lithe_fused_all"][0] - t_base) / max(1e-9, t_dense - t_base),
-            "fused_all_lora_cost_over_plain_gemm_s": results["lithe_fused_all"][0] - results["plain_gemm"][0],
+            "plain_gemm_base_s": mean["plain_gemm"],
+            "lithe_fused_all_s": mean["lithe_fused_all"],
+            "overhead_ratio_fused_all_vs_dense": (mean["lithe_fused_all"] - t_base) / max(1e-9, t_dense - t_base),
+            "fused_all_lora_cost_over_plain_gemm_s": mean["lithe_fused_all"] - mean["plain_gemm"],
             "passes_s": runs, "order": "ABBA: " + " ".join(kinds + tuple(reversed(kinds))),
-            "clocks": results["lithe"][1], "gpu_launches": steps * len(names)}), flush=True)
+            "clocks": clock_log, "gpu_launches": steps * len(setup.names)}), flush=True)
     if world > 1:
         import torch.distributed as dist
         dist.destroy_process_group()
@@ -1103,9 +1219,11 @@ def main():
     ap.add_argument("--mode", choices=["staged", "fused"], default=None,
                     help="form of the fused op: fused (decode inside the SGMV kernel per 64-token tile, default) "
                          "or staged (decode once per call into a workspace)")
-    ap.add_argument("--shard-batch", action="store_true",
-                    help="strong scaling: split the fixed B=14 batch by sample across ranks (default: weak, "
-                         "every rank runs its own B=14 batch)")
+    ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
+                    help="N > 1: strong (default) splits the fixed B=14 batch by sample across the ranks; weak gives "
+                         "every rank its own B=14 batch (the default line also reports weak scaling as a secondary key)")
+    ap.add_argument("--no-denoise", action="store_true",
+                    help="leave out the 28-step 1024^2 denoise record of the default line")
     ap.add_argument("--shapes", default="", help="comma list of d_inxd_out to run (default: all four), "
                     "e.g. 3072x3072 for a single-shape profiling run; for lora_gemm_flux, shape tags (img_sq, ...)")
     ap.add_argument("--rows", type=int, default=0, help="lora_gemm_flux: total rows per shape instead of B x tokens "

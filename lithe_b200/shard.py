@@ -17,7 +17,7 @@ import os
 import socket
 import traceback
 from dataclasses import dataclass
-from typing import Any, Callable, Dict, List, Sequence, Tuple
+from typing import Any, Callable, Dict, List, Optional, Sequence, Tuple
 
 import torch.multiprocessing as mp
 
@@ -43,6 +43,51 @@ def imbalance(n: int, world: int) -> float:
     """max slice / mean slice: the strong-scaling efficiency bound of the split."""
     sizes = shard_sizes(n, world)
     return max(sizes) / (n / world) if n else 1.0
+
+
+def _parse_cpulist(text: str) -> List[int]:
+    """'0-3,8,10-11' -> [0, 1, 2, 3, 8, 10, 11] (the sysfs cpulist format)."""
+    cpus: List[int] = []
+    for part in text.strip().split(","):
+        if not part:
+            continue
+        lo, _, hi = part.partition("-")
+        cpus.extend(range(int(lo), int(hi or lo) + 1))
+    return cpus
+
+
+def gpu_numa_node(device_index: int, sysfs: str = "/sys") -> Optional[int]:
+    """NUMA node of the host bridge a CUDA device hangs off (sysfs ``numa_node`` of its PCI
+    function), or None where the platform does not say."""
+    import torch
+    props = torch.cuda.get_device_properties(device_index)
+    addr = f"{getattr(props, 'pci_domain_id', 0):04x}:{props.pci_bus_id:02x}:{props.pci_device_id:02x}.0"
+    try:
+        with open(os.path.join(sysfs, "bus", "pci", "devices", addr, "numa_node")) as f:
+            node = int(f.read().strip())
+    except (OSError, ValueError):
+        return None
+    return node if node >= 0 else None
+
+
+def bind_host_to_gpu(device_index: int, sysfs: str = "/sys") -> Optional[int]:
+    """Restrict this process's host threads to the CPUs of the GPU's NUMA node, so that pinned
+    staging buffers allocated afterwards (pages are placed on the node of the thread that first
+    touches them) sit next to the GPU's PCIe root.  Best effort: returns the node, or None when
+    the node or its CPUs are unknown or outside the current affinity (nothing is changed)."""
+    node = gpu_numa_node(device_index, sysfs)
+    if node is None:
+        return None
+    try:
+        with open(os.path.join(sysfs, "devices", "system", "node", f"node{node}", "cpulist")) as f:
+            cpus = set(_parse_cpulist(f.read()))
+        cpus &= os.sched_getaffinity(0)
+        if not cpus:
+            return None
+        os.sched_setaffinity(0, cpus)
+    except (OSError, ValueError):
+        return None
+    return node
 
 
 class RankFailure(RuntimeError):
