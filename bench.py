@@ -755,7 +755,7 @@ def denoise_record(world, rank, local, dev):
         "config": {"image": "1024^2", "image_tokens": img_tok, "text_tokens": txt_tok, "batch": batch, "steps": steps,
                    "lora_linears": len(setup.names), "adapter_format": "diffusers-342", "bank_slots": BANK_SLOTS,
                    "distinct_adapters": batch, "model": "random-init FLUX.1-dev-shaped transformer (19 double + 38 "
-                   "single blocks, hidden 3072; rotary embeddings left out), bf16",
+                   "single blocks, hidden 3072, FLUX's 3-axis rotary embedding), bf16",
                    "parallelism": f"B={batch} split by sample over {world} ranks "
                                   f"({','.join(map(str, shard_sizes(batch, world)))}), bank replicated"},
         "lithe_s": t_lithe, "base_s": t_base, "dense_resident_lora_s": t_dense,
@@ -766,8 +766,8 @@ def denoise_record(world, rank, local, dev):
         "passes_s": runs, "order": "ABBA: " + " ".join(kinds + tuple(reversed(kinds))),
         "clocks": {k: v for k, v in clocks.items()}, "timing": "CUDA events around the whole loop, max over ranks",
         "reference_published": {"value": 133.4, "unit": "s", "hardware": "A100", "note":
-                                "the reference's README render time for a real FLUX.1-dev 1024^2 render "
-                                "(not this synthetic model, which omits RoPE)"}}
+                                "the reference's README render time for a real FLUX.1-dev 1024^2 render, "
+                                "text encoders and VAE included; context, not a comparison"}}
     del setup
     torch.cuda.empty_cache()
     return rec

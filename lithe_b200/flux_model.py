@@ -10,9 +10,11 @@ restatement of the architecture's dimensions, not a port of diffusers' code:
   hidden 3072, 24 heads of 128, FFN 12288, latent channels 64, text features 4096
 
 The attention + FFN linears carry the diffusers names that FLUX LoRA adapters target
-(``module.FLUX_TARGET_MODULES``; 19 x 12 + 38 x 3 = 342 linears).  Rotary position
-embeddings are omitted (an elementwise cost that does not touch the LoRA path).  Weights are
-N(0, 0.02); outputs are meaningless, only shapes and costs are real.
+(``module.FLUX_TARGET_MODULES``; 19 x 12 + 38 x 3 = 342 linears).  Attention applies FLUX's
+rotary position embedding: three axes (an index axis, image row, image column) over head-dim
+slices of 16, 56 and 56 (scaled with the head size), theta 10000, text tokens at position 0 of
+every axis and image tokens on a near-square grid.  Weights are N(0, 0.02); outputs are
+meaningless, only shapes and costs are real.
 """
 from __future__ import annotations
 
@@ -97,10 +99,51 @@ def _mod(x, shift, scale):
     return x * (1 + scale[:, None]) + shift[:, None]
 
 
-def _attend(q, k, v, heads):
+def rope_tables(n_txt: int, n_img: int, head_dim: int, device, theta: float = 10000.0):
+    """(cos, sin), each (n_txt + n_img, head_dim / 2) fp32, for the joint [text; image] sequence.
+
+    Positions are 3-axis ids (index, row, col): text tokens sit at (0, 0, 0), image token i at
+    (0, i // w, i % w) on a grid of width w = ceil(sqrt(n_img)).  Each axis owns a slice of the
+    head's rotation pairs (16 / 56 / 56 of 128 dims), with frequencies theta^(-2j / axis_dim).
+    """
+    axes = (head_dim // 8, 7 * head_dim // 16, head_dim - head_dim // 8 - 7 * head_dim // 16)
+    w = max(1, math.ceil(math.sqrt(n_img)))
+    idx = torch.arange(n_img, device=device)
+    ids = torch.zeros(n_txt + n_img, 3, device=device, dtype=torch.float32)
+    ids[n_txt:, 1] = (idx // w).float()
+    ids[n_txt:, 2] = (idx % w).float()
+    angles = []
+    for axis, dim in enumerate(axes):
+        freqs = theta ** (-torch.arange(0, dim, 2, device=device, dtype=torch.float32) / dim)
+        angles.append(ids[:, axis:axis + 1] * freqs[None])
+    ang = torch.cat(angles, dim=-1)
+    return torch.cos(ang), torch.sin(ang)
+
+
+def rope_full(cos, sin, dtype):
+    """The half-dim tables of ``rope_tables`` spread over the whole head dim in the activation
+    dtype: each angle's cos for both members of its pair, and its sin signed (-sin for the
+    pair's first member, +sin for the second), so that a rotation is one fused multiply-add."""
+    cos_f = cos.repeat_interleave(2, dim=-1)
+    sin_f = torch.stack([-sin, sin], dim=-1).flatten(-2)
+    return cos_f.to(dtype), sin_f.to(dtype)
+
+
+def _rotate(t, cos_f, sin_f):
+    """Rotate consecutive pairs (t[2j], t[2j+1]) of the last dim by the per-token angles:
+    (x0, x1) -> (x0 cos - x1 sin, x1 cos + x0 sin).  t is (b, heads, s, hd); cos_f / sin_f are
+    the (s, hd) tables of ``rope_full``.  Three elementwise passes: the pair swap, t * cos, and
+    the multiply-add."""
+    swapped = t.unflatten(-1, (-1, 2)).flip(-1).flatten(-2)
+    return torch.addcmul(t * cos_f, swapped, sin_f)
+
+
+def _attend(q, k, v, heads, rope=None):
     b, s, d = q.shape
     hd = d // heads
     q, k, v = (t.view(b, s, heads, hd).transpose(1, 2) for t in (q, k, v))
+    if rope is not None:
+        q, k = _rotate(q, *rope), _rotate(k, *rope)
     o = F.scaled_dot_product_attention(q, k, v)
     return o.transpose(1, 2).reshape(b, s, d)
 
@@ -135,7 +178,7 @@ class DoubleBlock(nn.Module):
         self.ff = FeedForward(d, d * cfg.mlp_ratio)
         self.ff_context = FeedForward(d, d * cfg.mlp_ratio)
 
-    def forward(self, img, txt, temb):
+    def forward(self, img, txt, temb, rope=None):
         sh, sc, g, sh2, sc2, g2 = self.norm1(temb)
         csh, csc, cg, csh2, csc2, cg2 = self.norm1_context(temb)
         a = self.attn
@@ -143,7 +186,7 @@ class DoubleBlock(nn.Module):
         xt = _mod(_ln(txt), csh, csc)
         qi, ki, vi = a._qkv(xi, a.to_q, a.to_k, a.to_v, a.norm_q, a.norm_k)
         qt, kt, vt = a._qkv(xt, a.add_q_proj, a.add_k_proj, a.add_v_proj, a.norm_added_q, a.norm_added_k)
-        o = _attend(torch.cat([qt, qi], 1), torch.cat([kt, ki], 1), torch.cat([vt, vi], 1), a.heads)
+        o = _attend(torch.cat([qt, qi], 1), torch.cat([kt, ki], 1), torch.cat([vt, vi], 1), a.heads, rope)
         ot, oi = o[:, : txt.shape[1]], o[:, txt.shape[1]:]
         img = img + g[:, None] * a.to_out[0](oi.contiguous())
         txt = txt + cg[:, None] * a.to_add_out(ot.contiguous())
@@ -161,12 +204,12 @@ class SingleBlock(nn.Module):
         self.proj_mlp = nn.Linear(d, d * cfg.mlp_ratio)
         self.proj_out = nn.Linear(d + d * cfg.mlp_ratio, d)
 
-    def forward(self, x, temb):
+    def forward(self, x, temb, rope=None):
         sh, sc, g = self.norm(temb)
         h = _mod(_ln(x), sh, sc)
         a = self.attn
         q, k, v = a._qkv(h, a.to_q, a.to_k, a.to_v, a.norm_q, a.norm_k)
-        o = _attend(q, k, v, a.heads)
+        o = _attend(q, k, v, a.heads, rope)
         mlp = F.gelu(self.proj_mlp(h), approximate="tanh")
         return x + g[:, None] * self.proj_out(torch.cat([o, mlp], dim=-1))
 
@@ -200,11 +243,13 @@ class FluxShapedTransformer(nn.Module):
         temb = self.time_in(self.timestep_embedding(t).to(dtype)) + self.pooled_in(pooled)
         img = self.x_embedder(latents)
         txt = self.context_embedder(text)
+        rope = rope_full(*rope_tables(txt.shape[1], img.shape[1], self.cfg.hidden // self.cfg.heads, img.device),
+                         img.dtype)
         for blk in self.transformer_blocks:
-            img, txt = blk(img, txt, temb)
+            img, txt = blk(img, txt, temb, rope)
         x = torch.cat([txt, img], dim=1)
         for blk in self.single_transformer_blocks:
-            x = blk(x, temb)
+            x = blk(x, temb, rope)
         img = x[:, txt.shape[1]:]
         sh, sc = self.norm_out(temb)
         return self.proj_out(_mod(_ln(img), sh, sc))

@@ -280,3 +280,53 @@ def test_attach_adapters_checks_on_cpu():
     other = random_adapter(SMALL[:1], 8, seed=3)
     with pytest.raises(ValueError):
         serve.attach_adapters(model_for(ads[0].modules), [ads[0], other])
+
+
+def test_flux_rope_tables():
+    """The FLUX-shaped model's rotary embedding: text tokens unrotated, rotations keep norms,
+    the fused form equals the pairwise rotation, and a query-key product depends only on the
+    offset between image positions of one row."""
+    from lithe_b200.flux_model import _rotate, rope_full, rope_tables
+    cos, sin = rope_tables(4, 16, 128, "cpu")
+    assert tuple(cos.shape) == (20, 64)
+    assert torch.equal(cos[:4], torch.ones(4, 64)) and torch.equal(sin[:4], torch.zeros(4, 64))
+    cf, sf = rope_full(cos, sin, torch.float32)
+    t = torch.randn(1, 2, 20, 128)
+    r = _rotate(t, cf, sf)
+    x0, x1 = t[..., 0::2], t[..., 1::2]
+    assert torch.allclose(r[..., 0::2], x0 * cos - x1 * sin, atol=1e-6)
+    assert torch.allclose(r[..., 1::2], x1 * cos + x0 * sin, atol=1e-6)
+    assert torch.allclose(r.norm(dim=-1), t.norm(dim=-1), atol=1e-4)
+    q, k = torch.randn(128), torch.randn(128)
+    grid = 4                                                # 16 image tokens on a 4 x 4 grid
+
+    def dot(i, j):                                          # image tokens i, j (row-major)
+        qi = _rotate(q.view(1, 1, 1, 128), cf[4 + i:5 + i], sf[4 + i:5 + i]).flatten()
+        kj = _rotate(k.view(1, 1, 1, 128), cf[4 + j:5 + j], sf[4 + j:5 + j]).flatten()
+        return float(qi @ kj)
+
+    assert abs(dot(1, 0) - dot(2, 1)) < 1e-3 and abs(dot(grid + 1, 1) - dot(2 * grid + 1, grid + 1)) < 1e-3
+
+
+def test_numa_binding_reads_sysfs(tmp_path, monkeypatch):
+    """bind_host_to_gpu: the GPU's PCI function -> its NUMA node -> that node's CPUs (here a
+    fake sysfs tree); unknown nodes change nothing."""
+    import os
+    from types import SimpleNamespace
+    from lithe_b200 import shard
+    props = SimpleNamespace(pci_domain_id=0, pci_bus_id=0x1b, pci_device_id=0)
+    monkeypatch.setattr(torch.cuda, "get_device_properties", lambda i: props)
+    dev = tmp_path / "bus" / "pci" / "devices" / "0000:1b:00.0"
+    dev.mkdir(parents=True)
+    cpus = sorted(os.sched_getaffinity(0))
+    node_dir = tmp_path / "devices" / "system" / "node" / "node1"
+    node_dir.mkdir(parents=True)
+    (node_dir / "cpulist").write_text(f"{cpus[0]}-{cpus[-1]}\n")
+    (dev / "numa_node").write_text("1\n")
+    seen = {}
+    monkeypatch.setattr(os, "sched_setaffinity", lambda pid, s: seen.setdefault("cpus", set(s)))
+    assert shard.gpu_numa_node(0, str(tmp_path)) == 1
+    assert shard.bind_host_to_gpu(0, str(tmp_path)) == 1 and seen["cpus"] == set(cpus)
+    (dev / "numa_node").write_text("-1\n")
+    assert shard.bind_host_to_gpu(0, str(tmp_path)) is None
+    assert shard._parse_cpulist("0-2,5,7-8") == [0, 1, 2, 5, 7, 8]
