@@ -228,6 +228,34 @@ LITHE_API int32_t lithe_lora_prep(const void* x, const lithe_index_view* idx_a, 
                         int32_t d_in, int32_t d_out, int32_t rank, const float* lut, float scaling, void* h,
                         void* b_dec, int32_t* err_flag, void* stream);
 
+/* Bytes of device workspace lithe_lora_prep_ws needs for a (batch, m, d_in) call on the current
+ * device: 8192 bytes per CTA of its shrink launch, min(SM count, batch * ceil(m/64) *
+ * ceil(d_in/128)).  0 for an empty call; a negative LITHE_ERR_* code when the device cannot be
+ * queried. */
+LITHE_API int64_t lithe_lora_prep_workspace_bytes(int32_t batch, int32_t m, int32_t d_in);
+
+/*
+ * lithe_lora_prep with the shrink's work split evenly over the SMs: its CTAs take equal runs of
+ * the (64-token tile, 128-column x stage) sequence instead of whole 64-token tiles, so a tile
+ * may be shared by neighbouring CTAs.  Each stores its fp32 partial h of a shared tile in
+ * `workspace`; the B-decode launch, which here follows the shrink on `stream`, adds the pieces
+ * in CTA order, scales, rounds to bf16 and writes those tiles' h, so h does not depend on
+ * timing.  h equals lithe_lora_prep's up to the fp32 summation order (one bf16 rounding step
+ * at most); b_dec is identical.  Same arguments and outputs as lithe_lora_prep; the B-decode
+ * kernel is launched even when b_dec is NULL if a tile is shared.  It pays where whole tiles
+ * would load the SMs unevenly (at B=14 x 4096 tokens: 896 tiles over 148 SMs) and the x row
+ * is long (d_in >= 12288); the Python host chooses it by that rule.  Replaces the same
+ * reference code as lithe_lora_prep.
+ *   workspace        device, 16-byte aligned, >= lithe_lora_prep_workspace_bytes(batch, m, d_in);
+ *                    contents on entry do not matter; calls sharing one workspace must be
+ *                    ordered on one stream.  Unused (may be NULL) when h is NULL.
+ */
+LITHE_API int32_t lithe_lora_prep_ws(const void* x, const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                        int64_t n_slots, const int32_t* ids, const float* weights, int32_t batch, int32_t m,
+                        int32_t d_in, int32_t d_out, int32_t rank, const float* lut, float scaling, void* h,
+                        void* b_dec, int32_t* err_flag, void* workspace, int64_t workspace_bytes,
+                        void* stream);
+
 /*
  * Base linear with the per-sample LoRA expand inside the GEMM (tcgen05, TMEM accumulators, TMA):
  *   out[r, :] = x[r, :] . w^T + bias + h[r, :] . b_dec[r / rows_per_sample]^T

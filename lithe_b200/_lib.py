@@ -81,6 +81,11 @@ _SIGNATURES.update({
         _c.c_void_p, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int32,
         _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p,
         _c.c_void_p, _c.c_void_p, _c.c_void_p]),
+    "lithe_lora_prep_ws": (_c.c_int32, [
+        _c.c_void_p, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.c_int64, _c.c_void_p, _c.c_void_p, _c.c_int32,
+        _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p,
+        _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p]),
+    "lithe_lora_prep_workspace_bytes": (_c.c_int64, [_c.c_int32, _c.c_int32, _c.c_int32]),
     "lithe_lora_gemm": (_c.c_int32, [
         _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_void_p,
         _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_void_p]),

@@ -79,6 +79,13 @@ struct SgmvParams {
     const uint8_t* ws;          // staged mode: decoded factor chunks, (batch, n_chunks, 512 B)
     int32_t n_chunks;           // n_xchunks + n_ochunks (per-sample stride of ws, in chunks)
     __nv_bfloat16* h_out;       // shrink-only mode (lithe_lora_prep): h rows (batch * m, 16), else null
+    // Shrink-only mode with a workspace: the CTAs take equal runs of x stages rather than of
+    // units, so a unit may be shared by neighbouring CTAs; each stores its fp32 partial h of a
+    // shared unit in the workspace, and the B-decode kernel that follows adds them up.
+    int32_t split;              // 0, or the stages of every unit (ceil(n_xchunks / 2))
+    int32_t split_grid;         // CTAs of the split shrink launch
+    int64_t split_total;        // total_units * split
+    float* split_part;          // [2 * CTA + (first unit of the CTA ? 0 : 1)][64 rows][16] partial h
     float lut[2][LITHE_MAX_LEVELS][16];
 };
 
@@ -138,6 +145,43 @@ constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * (kStageBytes 
 __device__ __forceinline__ float unit_weight(const SgmvParams& p, const UnitCache* uc, int b) {
     const int i = b - uc->b0;
     return i < uc->n ? uc->weight[i] : (p.weights ? __ldg(p.weights + b) : 1.0f);
+}
+
+// Split mode: every unit counts p.split stages (unrouted ones too), the stages of all units
+// form one sequence of T = p.split_total, and CTA c of the G = p.split_grid runs its stages
+// [c T / G, (c + 1) T / G).
+__device__ __forceinline__ int64_t split_begin(const SgmvParams& p, int c) {
+    return static_cast<int64_t>(c) * p.split_total / p.split_grid;
+}
+// The CTA whose run holds stage t.
+__device__ __forceinline__ int split_owner(const SgmvParams& p, int64_t t) {
+    return static_cast<int>(((t + 1) * p.split_grid - 1) / p.split_total);
+}
+// Where CTA c stores its partial h of unit u (u is its first or its last unit).
+__device__ __forceinline__ float* split_piece(const SgmvParams& p, int c, int u) {
+    const int first_unit = static_cast<int>(split_begin(p, c) / p.split);
+    return p.split_part + static_cast<int64_t>(2 * c + (u == first_unit ? 0 : 1)) * (kBM * 16);
+}
+
+// The stages [q0, q1) of unit u that this CTA runs, given its run [tb, te) of the stage
+// sequence (split mode); without split every unit of the CTA's range is whole.  A unit without
+// x stages (an unrouted sample) is run whole by the CTA holding its first stage and skipped
+// by the others.
+struct Span {
+    int q0, q1;
+    int mode;
+};
+constexpr int kWhole = 0, kPart = 1, kSkip = 2;
+
+__device__ __forceinline__ Span span_of(const SgmvParams& p, const Unit& un, int u, int64_t tb, int64_t te) {
+    const int n = un.sx + un.so;
+    if (!p.split) return Span{0, n, kWhole};
+    const int64_t s0 = static_cast<int64_t>(u) * p.split;
+    const int q0 = tb > s0 ? static_cast<int>(tb - s0) : 0;
+    const int q1 = te < s0 + p.split ? static_cast<int>(te - s0) : p.split;
+    if (q0 == 0 && q1 == p.split) return Span{0, n, kWhole};
+    if (un.sx != p.split) return q0 == 0 ? Span{0, n, kWhole} : Span{0, 0, kSkip};
+    return Span{q0, q1, kPart};
 }
 
 __device__ __forceinline__ uint4 lds128(const uint8_t* a) { return *reinterpret_cast<const uint4*>(a); }
@@ -277,31 +321,36 @@ template <int kRank, bool kStaged, int kFeed, bool kF16>
 __device__ uint32_t run_feeder(int d, int lane, const SgmvParams& p, const UnitCache* uc, const CUtensorMap* tmx,
                                const CUtensorMap* tmo, uint8_t* tiles, uint8_t* facts, const DecodeTables* tab,
                                const float* lut_s, uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin,
-                               int u_end) {
+                               int u_end, int64_t hb, int64_t he) {
     int u = u_begin, q = 0;          // cursor: unit, stage within the unit
     uint32_t pos = 0;                // pipeline position of (u, q)
     Unit un;
+    Span sp{0, 0, kWhole};
     // Move to the next position owned by this warp (the current one when first == true).
     auto seek = [&](bool first) {
+        bool fresh = first;          // entering unit u
         if (!first) {
             ++q;
             ++pos;
         }
         while (u < u_end) {
-            if (first || q == 0) un = unit_at(p, uc, u);
-            first = false;
-            const int n = un.sx + un.so;
-            if (q < n) {
+            if (fresh) {
+                un = unit_at(p, uc, u);
+                sp = span_of(p, un, u, hb, he);
+                q = sp.q0;
+                fresh = false;
+            }
+            if (q < sp.q1) {
                 const int skip = (d - static_cast<int>(pos % kFeed) + kFeed) % kFeed;
-                if (q + skip < n) {
+                if (q + skip < sp.q1) {
                     q += skip;
                     pos += skip;
                     return true;
                 }
-                pos += n - q;
+                pos += sp.q1 - q;
             }
             ++u;
-            q = 0;
+            fresh = true;
         }
         return false;
     };
@@ -433,7 +482,7 @@ __device__ __forceinline__ void store_delta_f32(float* out_b, const SgmvParams& 
 template <int kRank, bool kF16>
 __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCache* uc, uint8_t* tiles,
                              const uint8_t* facts, uint64_t* full, uint64_t* empty, float* xchg, uint64_t* xbar,
-                             volatile int* abort, int u_begin, int u_end) {
+                             volatile int* abort, int u_begin, int u_end, int64_t hb, int64_t he) {
     const int grp = w / kGroupWarps;     // this warp's group: positions pos % kGroups == grp
     const int wr = w % kGroupWarps;      // row block within the tile
     const int g = lane >> 2, t4 = lane & 3;
@@ -449,6 +498,8 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
     uint32_t pos = 0;
     for (int u = u_begin; u < u_end; ++u) {
         const Unit un = unit_at(p, uc, u);
+        const Span sp = span_of(p, un, u, hb, he);
+        if (sp.mode == kSkip) continue;
         if (w == 0 && lane == 0 && !un.active && un.slot >= p.n_slots && p.err) atomicOr(p.err, LITHE_DEVERR_SLOT);
         if (un.nx + un.no == 0) {
             if (p.h_out && grp == 0) {              // unrouted sample: its h rows are zero
@@ -468,7 +519,8 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
         float acc[2][2][4];
 #pragma unroll
         for (int i = 0; i < 16; ++i) (&acc[0][0][0])[i] = 0.f;
-        for (int q = 0; q < un.sx; ++q, ++pos) {
+        const int qx_end = sp.q1 < un.sx ? sp.q1 : un.sx;       // split spans hold x stages only
+        for (int q = sp.q0; q < qx_end; ++q, ++pos) {
             if (static_cast<int>(pos % kGroups) != grp) continue;
             const uint32_t s = pos % kStages, ph = (pos / kStages) & 1u;
             if (!mbar_wait(&full[s], ph, abort, p.err)) return;
@@ -523,6 +575,22 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
             part[0] += o0.x; part[1] += o0.y; part[2] += o0.z; part[3] += o0.w;
             part[4] += o1.x; part[5] += o1.y; part[6] += o1.z; part[7] += o1.w;
             ++n_xchg;
+        }
+        if (sp.mode == kPart) {
+            // A unit shared with neighbouring CTAs: group 0 stores this CTA's fp32 partial h of
+            // it (rows r0, r0 + 8; ranks 2 t4, 2 t4 + 1 and 8 + 2 t4, 9 + 2 t4), for the B-decode
+            // kernel to add up.
+            if (grp == 0) {
+                float* piece = split_piece(p, static_cast<int>(blockIdx.x), u);
+#pragma unroll
+                for (int hr = 0; hr < 2; ++hr) {
+                    float* row = piece + (r0 + 8 * hr) * 16;
+                    __stcg(reinterpret_cast<float2*>(row + 2 * t4), make_float2(part[2 * hr], part[2 * hr + 1]));
+                    __stcg(reinterpret_cast<float2*>(row + 8 + 2 * t4),
+                           make_float2(part[4 + 2 * hr], part[5 + 2 * hr]));
+                }
+            }
+            continue;
         }
         const float sc = p.scaling * unit_weight(p, uc, un.b);
         float h0[4], h1[4];
@@ -688,8 +756,19 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
         *abort = 0;
         fence_mbar_init();
     }
-    const int u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_units / gridDim.x);
-    const int u_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.total_units / gridDim.x);
+    // Units [u_begin, u_end); with split, the CTA's share is the stages [hb, he) and its first
+    // and last unit may be shared with the neighbouring CTAs.
+    int u_begin, u_end;
+    int64_t hb = 0, he = 0;
+    if (p.split) {
+        hb = split_begin(p, blockIdx.x);
+        he = split_begin(p, blockIdx.x + 1);
+        u_begin = static_cast<int>(hb / p.split);
+        u_end = he > hb ? static_cast<int>((he - 1) / p.split) + 1 : u_begin;
+    } else {
+        u_begin = static_cast<int>(static_cast<int64_t>(blockIdx.x) * p.total_units / gridDim.x);
+        u_end = static_cast<int>(static_cast<int64_t>(blockIdx.x + 1) * p.total_units / gridDim.x);
+    }
     fill_unit_cache(uc, p, u_begin, u_end, tid, blockDim.x);
     if constexpr (!kStaged) {
         for (int i = tid; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
@@ -700,14 +779,15 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
 
     uint32_t issued = 0;
     if (warp < kConsumerWarps) {
-        run_consumer<kRank, kF16>(warp, lane, p, uc, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end);
+        run_consumer<kRank, kF16>(warp, lane, p, uc, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end, hb,
+                                  he);
     } else {
         if (lane == 0) {
             prefetch_tmap(&tmx);
             prefetch_tmap(&tmo_ld);
         }
         issued = run_feeder<kRank, kStaged, kFeed, kF16>(warp - kFirstFeedWarp, lane, p, uc, &tmx, &tmo_ld, tiles, facts,
-                                                   tab, lut_s, full, empty, abort, u_begin, u_end);
+                                                   tab, lut_s, full, empty, abort, u_begin, u_end, hb, he);
     }
     __syncthreads();
     // After an aborted pipeline, let every feeder's last TMA loads land before the block's
@@ -760,11 +840,59 @@ __global__ void __launch_bounds__(256) decode_chunks_kernel(const __grid_constan
     }
 }
 
+// The split shrink's shared units, finished by one warp per CTA boundary c (1 .. G-1) of that
+// launch: the boundary that falls first inside a routed unit u adds the partial h of the
+// CTAs c - 1 .. (owner of u's last stage) in CTA order, scales by w_b * scaling, rounds to
+// bf16 and stores u's h rows -- the same sum whatever order the CTAs ran in.  Lane l takes
+// rows 2l and 2l + 1 of the tile.
+__device__ __forceinline__ void split_combine(const SgmvParams& p, int c, int lane) {
+    const int64_t t = split_begin(p, c);
+    if (t % p.split == 0) return;                               // the boundary is a unit edge
+    const int u = static_cast<int>(t / p.split);
+    const int64_t s0 = static_cast<int64_t>(u) * p.split;
+    if (split_owner(p, s0) != c - 1) return;                   // an earlier boundary takes u
+    const int b = u / p.n_mtiles, mt = u - b * p.n_mtiles;
+    const int32_t sid = __ldg(p.ids + b);
+    if (sid < 0 || static_cast<int64_t>(sid) >= p.n_slots) return;   // unrouted: run whole, not split
+    const int c_hi = split_owner(p, s0 + p.split - 1);
+    float acc[2][16];
+#pragma unroll
+    for (int r = 0; r < 2; ++r)
+#pragma unroll
+        for (int k = 0; k < 16; ++k) acc[r][k] = 0.f;
+    for (int cc = c - 1; cc <= c_hi; ++cc) {
+        const float* piece = split_piece(p, cc, u) + 2 * lane * 16;
+#pragma unroll
+        for (int r = 0; r < 2; ++r)
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                const float4 v = __ldcg(reinterpret_cast<const float4*>(piece + r * 16) + k);
+                acc[r][4 * k] += v.x;
+                acc[r][4 * k + 1] += v.y;
+                acc[r][4 * k + 2] += v.z;
+                acc[r][4 * k + 3] += v.w;
+            }
+    }
+    const float sc = p.scaling * (p.weights ? __ldg(p.weights + b) : 1.0f);
+#pragma unroll
+    for (int r = 0; r < 2; ++r) {
+        const int row = mt * kBM + 2 * lane + r;
+        if (row >= p.m) continue;
+        uint4* dst = reinterpret_cast<uint4*>(p.h_out + (static_cast<int64_t>(b) * p.m + row) * 16);
+        dst[0] = make_uint4(pack_bf16x2(acc[r][0] * sc, acc[r][1] * sc), pack_bf16x2(acc[r][2] * sc, acc[r][3] * sc),
+                            pack_bf16x2(acc[r][4] * sc, acc[r][5] * sc), pack_bf16x2(acc[r][6] * sc, acc[r][7] * sc));
+        dst[1] = make_uint4(pack_bf16x2(acc[r][8] * sc, acc[r][9] * sc), pack_bf16x2(acc[r][10] * sc, acc[r][11] * sc),
+                            pack_bf16x2(acc[r][12] * sc, acc[r][13] * sc),
+                            pack_bf16x2(acc[r][14] * sc, acc[r][15] * sc));
+    }
+}
+
 // lithe_lora_prep, B side: every sample's rank-16 B factor decoded into (batch, d_out, 16)
 // bf16, row o = B[o, :] (the operand of the GEMM's fused expand).  For rank 16 a B block G
 // holds four identical rows 4G .. 4G + 3, so one warp decodes a 64-column chunk (16 logical
 // columns x 2 rank halves, the lanes of decode_chunk) and writes each 8-value half 4 times.
 // The values are the fp32 level sums rounded to bf16, exactly as the expand path uses them.
+// After a split shrink, warps past the decode work finish its shared units (split_combine).
 __global__ void __launch_bounds__(256) decode_bdec_kernel(const __grid_constant__ SgmvParams p,
                                                           __nv_bfloat16* bdec, int32_t batch) {
     __shared__ DecodeTables tab;
@@ -775,8 +903,13 @@ __global__ void __launch_bounds__(256) decode_bdec_kernel(const __grid_constant_
     const int lane = threadIdx.x & 31;
     const uint32_t half = lane & 1;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
-    const int64_t total = static_cast<int64_t>(batch) * p.n_ochunks;
+    const int64_t n_dec = bdec ? static_cast<int64_t>(batch) * p.n_ochunks : 0;
+    const int64_t total = n_dec + (p.split ? p.split_grid - 1 : 0);
     for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        if (w >= n_dec) {
+            split_combine(p, static_cast<int>(w - n_dec) + 1, lane);
+            continue;
+        }
         const int b = static_cast<int>(w / p.n_ochunks);
         const int j = static_cast<int>(w - static_cast<int64_t>(b) * p.n_ochunks);
         const int32_t sid = __ldg(p.ids + b);
@@ -1036,8 +1169,20 @@ int64_t sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out) {
     return static_cast<int64_t>(batch) * (d_in / kChunk + (d_out + kChunk - 1) / kChunk) * kFactBytes;
 }
 
+// The split shrink (lithe_lora_prep_ws): per CTA two 64 x 16 fp32 partial-h pieces.  The grid
+// is min(total stages, SMs).
+constexpr int64_t kPrepPieceBytes = kBM * 16 * sizeof(float);
+int64_t prep_split_grid(int32_t batch, int32_t m, int32_t d_in, int sms) {
+    if (batch <= 0 || m <= 0 || d_in <= 0) return 0;
+    const int64_t units = (static_cast<int64_t>(m) + kBM - 1) / kBM * batch;
+    const int64_t stages = units * ((d_in / kChunk + kStageChunks - 1) / kStageChunks);
+    return stages < sms ? stages : sms;
+}
+int64_t prep_split_bytes(int64_t grid) { return grid * 2 * kPrepPieceBytes; }
+
 // Shared by the C entry points.  ws == nullptr: fused mode (decoder warps in the SGMV kernel);
-// otherwise staged mode with ws_bytes >= sgmv_workspace_bytes(batch, d_in, d_out).
+// otherwise staged mode with ws_bytes >= sgmv_workspace_bytes(batch, d_in, d_out), or, with
+// prep, the split shrink with ws_bytes >= prep_split_bytes(prep_split_grid(...)).
 int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lithe_index_view* idx_a,
                         const lithe_index_view* idx_b, int64_t n_slots, const int32_t* ids, const float* weights,
                         int32_t batch, int32_t m, int32_t d_in, int32_t d_out, int32_t rank, const float* lut,
@@ -1155,24 +1300,50 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
 
     if (prep) {
         cudaStream_t s = static_cast<cudaStream_t>(stream);
-        // B side first: every sample's decoded factor, (batch, d_out, 16)
-        if (bdec_out) {
-            const int64_t warps_needed = static_cast<int64_t>(batch) * p.n_ochunks;
+        int64_t grid = p.total_units < sms ? p.total_units : sms;
+        if (ws && h_out) {
+            // split shrink: equal runs of x stages per CTA, partial h of shared units in ws
+            grid = prep_split_grid(batch, m, d_in, sms);
+            if (reinterpret_cast<uintptr_t>(ws) % 16) return fail_arg("workspace must be 16-byte aligned");
+            const int64_t need = prep_split_bytes(grid);
+            if (ws_bytes < need)
+                return fail_arg("workspace holds %lld bytes, this call needs %lld", (long long)ws_bytes,
+                                (long long)need);
+            p.split = (p.n_xchunks + kStageChunks - 1) / kStageChunks;
+            p.split_grid = static_cast<int32_t>(grid);
+            p.split_total = static_cast<int64_t>(p.total_units) * p.split;
+            p.split_part = static_cast<float*>(ws);
+        }
+        p.h_out = static_cast<__nv_bfloat16*>(h_out);
+        // B side: every sample's decoded factor, (batch, d_out, 16), and after a split shrink
+        // the shared units' h
+        auto launch_bdec = [&]() -> int32_t {
+            const int64_t warps_needed =
+                (bdec_out ? static_cast<int64_t>(batch) * p.n_ochunks : 0) + (p.split ? p.split_grid - 1 : 0);
+            if (warps_needed == 0) return LITHE_OK;
             int64_t blocks = (warps_needed + 7) / 8;
             if (blocks > 2LL * sms) blocks = 2LL * sms;
             decode_bdec_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p, static_cast<__nv_bfloat16*>(bdec_out),
                                                                               batch);
             cudaError_t e = cudaGetLastError();
-            if (e != cudaSuccess) return fail_cuda(e, "decode_bdec_kernel launch");
+            return e == cudaSuccess ? LITHE_OK : fail_cuda(e, "decode_bdec_kernel launch");
+        };
+        if (!p.split) {
+            rc = launch_bdec();
+            if (rc != LITHE_OK || !h_out) return rc;
         }
-        if (!h_out) return LITHE_OK;
-        // A side: the fused kernel in shrink-only form (x tiles only, h stored after the shrink)
-        p.h_out = static_cast<__nv_bfloat16*>(h_out);
-        p.n_ochunks = 0;
-        p.accumulate = 1;             // unrouted samples skip all work (their h rows are zeroed)
-        p.n_chunks = p.n_xchunks;
-        p.out = nullptr;
-        ws = nullptr;
+        // A side: the fused kernel in shrink-only form (x tiles only, h stored after the shrink;
+        // unrouted samples skip all work and their h rows are zeroed).  Every x tile needs an
+        // A-chunk decode and no output tile is streamed, so the decode dominates: 8 feeder warps.
+        SgmvParams ps = p;
+        ps.n_ochunks = 0;
+        ps.accumulate = 1;
+        ps.n_chunks = ps.n_xchunks;
+        ps.out = nullptr;
+        rc = launch_rank<16, false, false, 2 * kDecodeWarps>(tmx, tmo_ld, ps, static_cast<int>(grid), device, sms,
+                                                             batch, nullptr, s);
+        if (rc != LITHE_OK || !p.split) return rc;
+        return launch_bdec();
     }
 
     const int grid = static_cast<int>(p.total_units < sms ? p.total_units : sms);
@@ -1183,9 +1354,6 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
                        : launch_rank<R, true, false>(tmx, tmo_ld, p, grid, device, sms, batch, w, s);             \
     return f16 ? launch_rank<R, false, true>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)                      \
                : launch_rank<R, false, false>(tmx, tmo_ld, p, grid, device, sms, batch, w, s)
-    // Shrink-only form (lithe_lora_prep): every x tile needs an A-chunk decode and no output
-    // tile is streamed, so the decode dominates; it runs with 8 feeder warps.
-    if (prep) return launch_rank<16, false, false, 2 * kDecodeWarps>(tmx, tmo_ld, p, grid, device, sms, batch, w, s);
     switch (rank) {
         case 16: LITHE_LAUNCH(16);
         case 8: LITHE_LAUNCH(8);
@@ -1227,6 +1395,26 @@ extern "C" int32_t lithe_lora_prep(const void* x, const lithe_index_view* idx_a,
     if (batch > 0 && m > 0 && !h && !b_dec) return lithe::fail_arg("h and b_dec are both NULL");
     return lithe::sgmv_index_impl(x, h ? h : b_dec, 1, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
                                   rank, lut, scaling, err_flag, nullptr, 0, stream, h, b_dec, true);
+}
+
+extern "C" int32_t lithe_lora_prep_ws(const void* x, const lithe_index_view* idx_a, const lithe_index_view* idx_b,
+                                      int64_t n_slots, const int32_t* ids, const float* weights, int32_t batch,
+                                      int32_t m, int32_t d_in, int32_t d_out, int32_t rank, const float* lut,
+                                      float scaling, void* h, void* b_dec, int32_t* err_flag, void* workspace,
+                                      int64_t workspace_bytes, void* stream) {
+    lithe::clear_error();
+    if (batch > 0 && m > 0 && !h && !b_dec) return lithe::fail_arg("h and b_dec are both NULL");
+    if (batch > 0 && m > 0 && h && !workspace) return lithe::fail_arg("workspace is NULL");
+    return lithe::sgmv_index_impl(x, h ? h : b_dec, 1, idx_a, idx_b, n_slots, ids, weights, batch, m, d_in, d_out,
+                                  rank, lut, scaling, err_flag, workspace, workspace_bytes, stream, h, b_dec, true);
+}
+
+extern "C" int64_t lithe_lora_prep_workspace_bytes(int32_t batch, int32_t m, int32_t d_in) {
+    lithe::clear_error();
+    int device = 0, sms = 0;
+    const int32_t rc = lithe::current_device_sms(&device, &sms);
+    if (rc != LITHE_OK) return rc;
+    return lithe::prep_split_bytes(lithe::prep_split_grid(batch, m, d_in, sms));
 }
 
 extern "C" int64_t lithe_sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out) {

@@ -60,6 +60,16 @@ def _require_cuda(t: torch.Tensor, what: str) -> None:
         raise ValueError(f"{what} must be a CUDA tensor (lithe_b200 has no CPU path), got {t.device}")
 
 
+_SMS: dict = {}
+
+
+def _sm_count(device: torch.device) -> int:
+    idx = device.index if device.index is not None else torch.cuda.current_device()
+    if idx not in _SMS:
+        _SMS[idx] = torch.cuda.get_device_properties(idx).multi_processor_count
+    return _SMS[idx]
+
+
 def stream_handle(device: torch.device) -> int:
     return torch.cuda.current_stream(device).cuda_stream
 
@@ -292,11 +302,41 @@ def lora_gemm_(x: torch.Tensor, weight: torch.Tensor, bias: Optional[torch.Tenso
     return out
 
 
+def prep_workspace_bytes(batch: int, m: int, d_in: int) -> int:
+    """Bytes of workspace the split shrink of lithe_lora_prep_ws needs on the current device."""
+    n = int(_lib.lib().lithe_lora_prep_workspace_bytes(batch, m, d_in))
+    if n < 0:
+        _lib.check(n, "lithe_lora_prep_workspace_bytes")
+    return n
+
+
+# The split shrink's cross-CTA combine costs about as much as 20-30 stages of x streaming
+# (measured on B200: at 14 x 4096 x 3072 the split and whole-tile forms time the same, with the
+# busiest whole-tile CTA 23 stages above the average; at 14 x 4096 x 12288, 91 stages above,
+# the split is 7% faster).  It is taken when the busiest whole-tile CTA would run at least this
+# many stages more than the average.
+PREP_SPLIT_MIN_GAIN_STAGES = 48
+
+
+def prep_split_pays(batch: int, m: int, d_in: int, sms: int) -> bool:
+    units = -(-m // 64) * batch
+    stages = -(-d_in // 128)
+    if units <= 0 or sms <= 0:
+        return False
+    busiest = -(-units // min(units, sms)) * stages
+    return busiest - units * stages / min(units * stages, sms) >= PREP_SPLIT_MIN_GAIN_STAGES
+
+
 def lora_prep_(x: torch.Tensor, *, view_a: _lib.IndexView, view_b: _lib.IndexView, n_slots: int, ids: torch.Tensor,
                weights: Optional[torch.Tensor], d_out: int, lut: np.ndarray, scaling: float,
-               h: Optional[torch.Tensor], b_dec: Optional[torch.Tensor], err: Optional[torch.Tensor] = None) -> None:
+               h: Optional[torch.Tensor], b_dec: Optional[torch.Tensor], err: Optional[torch.Tensor] = None,
+               split: Optional[bool] = None, workspace: Optional[torch.Tensor] = None) -> None:
     """lithe_lora_prep: h (B*M, 16) and b_dec (B, d_out, 16), bf16, for lithe_lora_gemm's fused expand.
-    Either may be None to skip its half (not both)."""
+    Either may be None to skip its half (not both).  With ``split`` h comes from
+    lithe_lora_prep_ws, whose CTAs take equal runs of the x stages rather than of 64-token
+    tiles; ``workspace`` (uint8 CUDA tensor of at least prep_workspace_bytes) is then used,
+    or one is allocated from torch's caching allocator.  ``split=None`` takes the split where
+    prep_split_pays says so."""
     _require_cuda(x, "x")
     if x.dtype != torch.bfloat16 or x.dim() != 3 or not x.is_contiguous():
         raise ValueError("x must be a contiguous (B, M, d_in) bfloat16 tensor")
@@ -314,12 +354,23 @@ def lora_prep_(x: torch.Tensor, *, view_a: _lib.IndexView, view_b: _lib.IndexVie
     if err is None:
         err = error_word(x.device)
     with device_ctx(x.device):
-        rc = _lib.lib().lithe_lora_prep(
-            x.data_ptr(), ctypes.byref(view_a), ctypes.byref(view_b), int(n_slots), ids.data_ptr(),
-            weights.data_ptr() if weights is not None else None, bsz, m, d_in, int(d_out), 16, lut_array(lut),
-            float(scaling), h.data_ptr() if h is not None else None, b_dec.data_ptr() if b_dec is not None else None,
-            err.data_ptr(), stream_handle(x.device))
-    _lib.check(rc, "lithe_lora_prep")
+        common = (x.data_ptr(), ctypes.byref(view_a), ctypes.byref(view_b), int(n_slots), ids.data_ptr(),
+                  weights.data_ptr() if weights is not None else None, bsz, m, d_in, int(d_out), 16, lut_array(lut),
+                  float(scaling), h.data_ptr() if h is not None else None,
+                  b_dec.data_ptr() if b_dec is not None else None, err.data_ptr())
+        if split is None:
+            split = prep_split_pays(bsz, m, d_in, _sm_count(x.device))
+        if split and h is not None and bsz * m > 0:
+            if workspace is None:
+                workspace = torch.empty(max(prep_workspace_bytes(bsz, m, d_in), 16), dtype=torch.uint8,
+                                        device=x.device)
+            _require_cuda(workspace, "workspace")
+            rc = _lib.lib().lithe_lora_prep_ws(*common, workspace.data_ptr(), workspace.numel(),
+                                                stream_handle(x.device))
+            _lib.check(rc, "lithe_lora_prep_ws")
+        else:
+            rc = _lib.lib().lithe_lora_prep(*common, stream_handle(x.device))
+            _lib.check(rc, "lithe_lora_prep")
 
 
 def pack_raw_batch_(raw: torch.Tensor, segments: torch.Tensor, levels: int, bank: torch.Tensor,

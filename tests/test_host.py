@@ -330,3 +330,14 @@ def test_numa_binding_reads_sysfs(tmp_path, monkeypatch):
     (dev / "numa_node").write_text("-1\n")
     assert shard.bind_host_to_gpu(0, str(tmp_path)) is None
     assert shard._parse_cpulist("0-2,5,7-8") == [0, 1, 2, 5, 7, 8]
+
+
+def test_prep_split_choice():
+    """The split shrink is chosen only where whole 64-token tiles leave the busiest CTA far above
+    the average (FLUX 1024^2 B=14: the 12288- and 15360-wide img inputs, not the 3072-wide ones,
+    nor the 4608-token single-block inputs whose 1008 tiles already spread evenly)."""
+    from lithe_b200.kernels._launch import prep_split_pays
+    assert prep_split_pays(14, 4096, 12288, 148) and prep_split_pays(14, 4096, 15360, 148)
+    assert not prep_split_pays(14, 4096, 3072, 148)
+    assert not prep_split_pays(14, 4608, 15360, 148) and not prep_split_pays(14, 512, 12288, 148)
+    assert not prep_split_pays(4, 4096, 3072, 148) and not prep_split_pays(0, 4096, 3072, 148)
