@@ -626,7 +626,8 @@ class _DenoiseSetup:
     def __init__(self, dev, img_tok, txt_tok, batch, key_format, lo, hi, slot_seed, input_seed):
         from lithe_b200 import kohya
         from lithe_b200.flux_model import FluxShapedTransformer, lora_targets
-        from lithe_b200.kernels import PackedBank, PackedLayout, PackedLoRALinear, PerSampleLoRALinear, split_decoded
+        from lithe_b200.kernels import (PackedBank, PackedLayout, PackedLoRALinear, PerSampleLoRALinear,
+                                        group_shared_inputs, split_decoded)
         from lithe_b200.kernels import _launch as _launch_k
 
         torch.manual_seed(0)
@@ -662,6 +663,8 @@ class _DenoiseSetup:
             return PackedLoRALinear(bases[path], bank, name, RANK, 1.0, rows=None if full else (r0, r1))
 
         packed = {n: _packed(n) for n in self.names}
+        # q / k / v triples that read one input share one prep on the fused-GEMM path
+        group_shared_inputs(packed)
         ids = slots.to(torch.int32).to(dev)
         for m in packed.values():
             m.assign = ids
@@ -1090,6 +1093,8 @@ LORA_GEMM_SHAPES = [  # (tag, tokens per sample, d_in, d_out, linears per forwar
     ("img_sq", 4096, 3072, 3072, 76), ("img_up", 4096, 3072, 12288, 19), ("img_dn", 4096, 12288, 3072, 19),
     ("txt_sq", 512, 3072, 3072, 76), ("txt_up", 512, 3072, 12288, 19), ("txt_dn", 512, 12288, 3072, 19),
     ("single_sq", 4608, 3072, 3072, 114)]
+# of those, the q / k / v triples that read one input (one shared-input prep group each)
+LORA_GEMM_QKV_GROUPS = {"img_sq": 19, "txt_sq": 19, "single_sq": 38}
 # the extra targets of the Kohya-304 layout (single blocks' proj_mlp and proj_out); run only when named by --shapes
 LORA_GEMM_KOHYA_SHAPES = [("single_mlp", 4608, 3072, 12288, 38), ("single_out", 4608, 15360, 3072, 38)]
 
@@ -1099,7 +1104,7 @@ def run_lora_gemm(args):
     lithe_lora_prep + lithe_lora_gemm (the LoRA-serving linear), the plain tcgen05 GEMM and
     cuBLAS's bf16 GEMM (torch.nn.functional.linear), interleaved, best of `steps` rounds."""
     import torch.nn.functional as F
-    from lithe_b200.kernels import PackedBank, PackedLayout, PackedLoRALinear
+    from lithe_b200.kernels import PackedBank, PackedLayout, PackedLoRALinear, SharedInputPrep
     from lithe_b200.kernels import _launch as _lk
 
     world, rank, local = dist_env()
@@ -1123,17 +1128,30 @@ def run_lora_gemm(args):
         if (named is None and (tag, m, d_in, d_out, count) in LORA_GEMM_KOHYA_SHAPES) or (named and tag not in named):
             continue
         mm = m if not rows_override else max(256, rows_override // batch // 256 * 256)
-        lay = PackedLayout.from_modules([{"name": "l", "shape_a": [RANK, d_in], "shape_b": [d_out, RANK]}])
+        n_groups = 0 if rows_override else LORA_GEMM_QKV_GROUPS.get(tag, 0)
+        n_mod = 3 if tag in LORA_GEMM_QKV_GROUPS else 1
+        lay = PackedLayout.from_modules([{"name": f"l{i}", "shape_a": [RANK, d_in], "shape_b": [d_out, RANK]}
+                                         for i in range(n_mod)])
         bank = PackedBank(lay, 1000, dev)
         bank.fill_random(seed=3)
-        base = torch.nn.Linear(d_in, d_out).to(device=dev, dtype=torch.bfloat16)
-        layer = PackedLoRALinear(base, bank, "l", RANK, 1.0, fused_gemm=True)
-        layer.assign = torch.randperm(1000, generator=torch.Generator().manual_seed(5))[:batch].to(torch.int32).to(dev)
+        ids = torch.randperm(1000, generator=torch.Generator().manual_seed(5))[:batch].to(torch.int32).to(dev)
+        layers = []
+        for i in range(n_mod):
+            lin = torch.nn.Linear(d_in, d_out).to(device=dev, dtype=torch.bfloat16)
+            layers.append(PackedLoRALinear(lin, bank, f"l{i}", RANK, 1.0, fused_gemm=True))
+            layers[-1].assign = ids
+        base = layers[0].base
+        layer = PackedLoRALinear(base, bank, "l0", RANK, 1.0, fused_gemm=True)     # a linear alone
+        layer.assign = ids
         x = torch.randn(batch, mm, d_in, device=dev, dtype=torch.bfloat16, generator=gen)
         x2 = x.view(-1, d_in)
         out = torch.empty(batch * mm, d_out, device=dev, dtype=torch.bfloat16)
         fs = {"ours": lambda: layer(x), "plain": lambda: _lk.lora_gemm_(x2, base.weight, base.bias, out),
               "cublas": lambda: F.linear(x2, base.weight, base.bias)}
+        if n_mod == 3:
+            # a q / k / v triple on one input: one shared-input prep for the three (SharedInputPrep)
+            SharedInputPrep(layers)
+            fs["ours_qkv"] = lambda: [lyr(x) for lyr in layers]
         best = {k: float("inf") for k in fs}
         stream = torch.cuda.current_stream(dev)
         with torch.no_grad():
@@ -1157,10 +1175,10 @@ def run_lora_gemm(args):
                     "ours_tflops": round(fl / best["ours"] / 1e12, 1)})
         c = 1 if rows_override else count
         total_flops += c * fl
-        total_ours += c * best["ours"]
+        total_ours += (c - 3 * n_groups) * best["ours"] + n_groups * best.get("ours_qkv", 0.0)
         total_plain += c * best["plain"]
         total_cublas += c * best["cublas"]
-        del bank, layer, base, x, out
+        del bank, layer, layers, base, x, out
         torch.cuda.empty_cache()
     errors = _lk.device_errors(dev)
     ms = max_over_ranks(total_ours * 1000.0, world)

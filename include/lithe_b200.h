@@ -256,6 +256,29 @@ LITHE_API int32_t lithe_lora_prep_ws(const void* x, const lithe_index_view* idx_
                         void* b_dec, int32_t* err_flag, void* workspace, int64_t workspace_bytes,
                         void* stream);
 
+/* Bytes of device workspace lithe_lora_prep_multi needs: batch * (d_in/64) * n_targets * 512. */
+LITHE_API int64_t lithe_lora_prep_multi_workspace_bytes(int32_t batch, int32_t d_in, int32_t n_targets);
+
+/*
+ * lithe_lora_prep for n_targets (1..4) rank-16 linears that read the same x (the q, k and v
+ * projections of one attention block, each with its own adapter module): x is read once for
+ * all of them.  Per target t, the same outputs and values as lithe_lora_prep with idx_a[t],
+ * idx_b[t], d_out[t] and scaling[t]: h[t] (batch * m, 16) and b_dec[t] (batch, d_out[t], 16),
+ * b_dec[t] may be NULL.  Two launches on `stream`: one decodes every routed sample's A chunks
+ * of every target into `workspace` (plus the b_dec asked for); the shrink then streams each
+ * x tile once and bulk-copies the targets' decoded chunks beside it.  Replaces the reference's
+ * per-linear shrink (lithe/kernels/shared.py:36-95) called once per target on the same input.
+ *   idx_a, idx_b, d_out, scaling, h, b_dec   HOST arrays of n_targets entries
+ *   workspace        device, 16-byte aligned, >= lithe_lora_prep_multi_workspace_bytes(batch,
+ *                    d_in, n_targets); contents on entry do not matter; calls sharing one
+ *                    workspace must be ordered on one stream.
+ */
+LITHE_API int32_t lithe_lora_prep_multi(const void* x, int32_t n_targets, const lithe_index_view* idx_a,
+                        const lithe_index_view* idx_b, const int32_t* d_out, int64_t n_slots, const int32_t* ids,
+                        const float* weights, int32_t batch, int32_t m, int32_t d_in, int32_t rank,
+                        const float* lut, const float* scaling, void* const* h, void* const* b_dec,
+                        int32_t* err_flag, void* workspace, int64_t workspace_bytes, void* stream);
+
 /*
  * Base linear with the per-sample LoRA expand inside the GEMM (tcgen05, TMEM accumulators, TMA):
  *   out[r, :] = x[r, :] . w^T + bias + h[r, :] . b_dec[r / rows_per_sample]^T

@@ -86,6 +86,12 @@ _SIGNATURES.update({
         _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.POINTER(_c.c_float), _c.c_float, _c.c_void_p,
         _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int64, _c.c_void_p]),
     "lithe_lora_prep_workspace_bytes": (_c.c_int64, [_c.c_int32, _c.c_int32, _c.c_int32]),
+    "lithe_lora_prep_multi_workspace_bytes": (_c.c_int64, [_c.c_int32, _c.c_int32, _c.c_int32]),
+    "lithe_lora_prep_multi": (_c.c_int32, [
+        _c.c_void_p, _c.c_int32, _c.POINTER(IndexView), _c.POINTER(IndexView), _c.POINTER(_c.c_int32), _c.c_int64,
+        _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_int32, _c.POINTER(_c.c_float),
+        _c.POINTER(_c.c_float), _c.POINTER(_c.c_void_p), _c.POINTER(_c.c_void_p), _c.c_void_p, _c.c_void_p,
+        _c.c_int64, _c.c_void_p]),
     "lithe_lora_gemm": (_c.c_int32, [
         _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_int32, _c.c_void_p,
         _c.c_void_p, _c.c_int32, _c.c_int32, _c.c_void_p, _c.c_void_p]),

@@ -60,6 +60,7 @@ constexpr int kStageBytes = kStageChunks * kTileBytes;
 constexpr int kStageFactBytes = kStageChunks * kFactBytes;
 constexpr int kLutFloats = 2 * LITHE_MAX_LEVELS * 16;
 constexpr int kXchgFloats = kConsumerWarps * 32 * 8;   // partial h of every consumer thread (one buffer)
+constexpr int kMaxTargets = 4;                    // linears sharing x in one lithe_lora_prep_multi call
 
 struct SgmvParams {
     IndexView ia, ib;
@@ -86,6 +87,14 @@ struct SgmvParams {
     int32_t split_grid;         // CTAs of the split shrink launch
     int64_t split_total;        // total_units * split
     float* split_part;          // [2 * CTA + (first unit of the CTA ? 0 : 1)][64 rows][16] partial h
+    // lithe_lora_prep_multi: n_targets linears that read the same x.  The staged shrink reads
+    // target t's A chunk c of sample b from ws + ((b * n_xchunks + c) * n_targets + t) * 512.
+    int32_t n_targets;
+    IndexView ia_t[kMaxTargets], ib_t[kMaxTargets];
+    int32_t d_out_t[kMaxTargets], b_blocks_t[kMaxTargets], n_ochunks_t[kMaxTargets];
+    float scaling_t[kMaxTargets];
+    __nv_bfloat16* h_t[kMaxTargets];
+    __nv_bfloat16* bdec_t[kMaxTargets];
     float lut[2][LITHE_MAX_LEVELS][16];
 };
 
@@ -138,9 +147,14 @@ __device__ __forceinline__ Unit unit_at(const SgmvParams& p, const UnitCache* uc
     return r;
 }
 
-constexpr size_t kSmemBytes = 1024 /*alignment slack*/ + kStages * (kStageBytes + kStageFactBytes) + sizeof(DecodeTables) +
-                              2 * kXchgFloats * sizeof(float) + (2 * kStages + 2) * sizeof(uint64_t) +
-                              kLutFloats * sizeof(float) + sizeof(UnitCache) + 16;
+// Dynamic shared memory of sgmv_index_kernel with kT targets' factor chunks per stage.
+constexpr size_t smem_bytes(int kT) {
+    return 1024 /*alignment slack*/ + kStages * (kStageBytes + kT * kStageFactBytes) + sizeof(DecodeTables) +
+           2 * kXchgFloats * sizeof(float) + (2 * kStages + 2) * sizeof(uint64_t) + kLutFloats * sizeof(float) +
+           sizeof(UnitCache) + 16;
+}
+constexpr size_t kSmemBytes = smem_bytes(1);
+static_assert(smem_bytes(kMaxTargets) <= 227 * 1024, "shared memory of the 4-target shrink");
 
 __device__ __forceinline__ float unit_weight(const SgmvParams& p, const UnitCache* uc, int b) {
     const int i = b - uc->b0;
@@ -200,20 +214,27 @@ __device__ __forceinline__ uint32_t add_x2(uint32_t w, float dlo, float dhi) {
 // c < nx, else B chunk c - nx).  Returns false when the lane's values are structurally zero
 // (rank rows >= kRank, or past the last B block); then nothing is loaded.
 template <int kRank>
-__device__ __forceinline__ bool chunk_fetch(const SgmvParams& p, const Unit& un, int c, int lane,
-                                            RawIndices<LITHE_MAX_LEVELS>& raw) {
+__device__ __forceinline__ bool chunk_fetch_v(const IndexView& ia, const IndexView& ib, int a_blocks_per_row,
+                                              int b_blocks, const Unit& un, int c, int lane,
+                                              RawIndices<LITHE_MAX_LEVELS>& raw) {
     const int row = lane >> 1;          // A: rank row r; B: logical column n
     const int half = lane & 1;
     if (c < un.nx) {
         if (row >= kRank) return false;
-        fetch_raw<LITHE_MAX_LEVELS>(p.ia, un.slot, static_cast<int64_t>(row) * p.a_blocks_per_row + c, raw);
+        fetch_raw<LITHE_MAX_LEVELS>(ia, un.slot, static_cast<int64_t>(row) * a_blocks_per_row + c, raw);
         return true;
     }
     constexpr int kPer = 16 / kRank;
     const int G = (16 * (c - un.nx) + row) / kPer;
-    if (G >= p.b_blocks || 8 * half >= kRank) return false;
-    fetch_raw<LITHE_MAX_LEVELS>(p.ib, un.slot, G, raw);
+    if (G >= b_blocks || 8 * half >= kRank) return false;
+    fetch_raw<LITHE_MAX_LEVELS>(ib, un.slot, G, raw);
     return true;
+}
+
+template <int kRank>
+__device__ __forceinline__ bool chunk_fetch(const SgmvParams& p, const Unit& un, int c, int lane,
+                                            RawIndices<LITHE_MAX_LEVELS>& raw) {
+    return chunk_fetch_v<kRank>(p.ia, p.ib, p.a_blocks_per_row, p.b_blocks, un, c, lane, raw);
 }
 
 __device__ __forceinline__ void decode_values(const SgmvParams& p, const DecodeTables* tab, const float* lut_s,
@@ -317,7 +338,7 @@ __device__ __forceinline__ uint32_t load_stage_tiles(const SgmvParams& p, const 
 // four to eight warps the same stream reaches 33-37 GB/s per SM (measured with a streaming
 // probe, 57344 x 3072 bf16, one CTA per SM).
 // Returns one past the last position this warp issued (all of them have arrived).
-template <int kRank, bool kStaged, int kFeed, bool kF16>
+template <int kRank, bool kStaged, int kFeed, bool kF16, int kT>
 __device__ uint32_t run_feeder(int d, int lane, const SgmvParams& p, const UnitCache* uc, const CUtensorMap* tmx,
                                const CUtensorMap* tmo, uint8_t* tiles, uint8_t* facts, const DecodeTables* tab,
                                const float* lut_s, uint64_t* full, uint64_t* empty, volatile int* abort, int u_begin,
@@ -385,19 +406,19 @@ __device__ uint32_t run_feeder(int d, int lane, const SgmvParams& p, const UnitC
         if (!mbar_wait(&empty[s], ph ^ 1u, abort, p.err)) return issued;
         const bool tile = cq < cur.sx || p.accumulate;
         uint8_t* dst = tiles + s * kStageBytes;
-        uint8_t* fdst = facts + s * kStageFactBytes;
+        uint8_t* fdst = facts + s * (kT * kStageFactBytes);
         int c0, n;
         stage_chunks(cur, cq, c0, n);
         if constexpr (kStaged) {
             if (lane == 0) {
-                const uint32_t fbytes = cur.active ? static_cast<uint32_t>(n * kFactBytes) : 0u;
+                const uint32_t fbytes = cur.active ? static_cast<uint32_t>(n * kT * kFactBytes) : 0u;
                 if (!tile && fbytes == 0) {
                     mbar_arrive(&full[s]);
                 } else {
                     if (tile) load_stage_tiles(p, tmx, tmo, cur, cq, dst, &full[s], true);
                     if (fbytes) {
                         mbar_expect_tx(&full[s], fbytes);
-                        bulk_load_1d(fdst, p.ws + (static_cast<int64_t>(cur.b) * p.n_chunks + c0) * kFactBytes,
+                        bulk_load_1d(fdst, p.ws + (static_cast<int64_t>(cur.b) * p.n_chunks + c0) * kT * kFactBytes,
                                      fbytes, &full[s]);
                     }
                     mbar_arrive(&full[s]);
@@ -479,7 +500,7 @@ __device__ __forceinline__ void store_delta_f32(float* out_b, const SgmvParams& 
     }
 }
 
-template <int kRank, bool kF16>
+template <int kRank, bool kF16, int kT>
 __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCache* uc, uint8_t* tiles,
                              const uint8_t* facts, uint64_t* full, uint64_t* empty, float* xchg, uint64_t* xbar,
                              volatile int* abort, int u_begin, int u_end, int64_t hb, int64_t he) {
@@ -504,21 +525,24 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
         if (un.nx + un.no == 0) {
             if (p.h_out && grp == 0) {              // unrouted sample: its h rows are zero
 #pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                    const int row = un.mt * kBM + r0 + 8 * hr;
-                    if (row < p.m) {
-                        uint32_t* hrow = reinterpret_cast<uint32_t*>(p.h_out + (static_cast<int64_t>(un.b) * p.m + row) * 16);
-                        hrow[t4] = 0u;
-                        hrow[4 + t4] = 0u;
+                for (int t = 0; t < kT; ++t)
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
+                        const int row = un.mt * kBM + r0 + 8 * hr;
+                        if (row < p.m) {
+                            __nv_bfloat16* hb_t = kT == 1 ? p.h_out : p.h_t[t];
+                            uint32_t* hrow = reinterpret_cast<uint32_t*>(hb_t + (static_cast<int64_t>(un.b) * p.m + row) * 16);
+                            hrow[t4] = 0u;
+                            hrow[4 + t4] = 0u;
+                        }
                     }
-                }
             }
             continue;
         }
-        // four independent accumulation chains: [rank half][32-column window]
-        float acc[2][2][4];
+        // per target, four independent accumulation chains: [rank half][32-column window]
+        float acc[kT][2][2][4];
 #pragma unroll
-        for (int i = 0; i < 16; ++i) (&acc[0][0][0])[i] = 0.f;
+        for (int i = 0; i < 16 * kT; ++i) (&acc[0][0][0][0])[i] = 0.f;
         const int qx_end = sp.q1 < un.sx ? sp.q1 : un.sx;       // split spans hold x stages only
         for (int q = sp.q0; q < qx_end; ++q, ++pos) {
             if (static_cast<int>(pos % kGroups) != grp) continue;
@@ -528,21 +552,29 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
             for (int k = 0; k < kStageChunks; ++k) {
                 if (kStageChunks * q + k >= un.nx) break;
                 const uint8_t* tile = tiles + s * kStageBytes + k * kTileBytes;
-                const uint8_t* fa = facts + s * kStageFactBytes + k * kFactBytes;
+                // the targets' factor chunks of chunk k: kT consecutive 512-byte blocks
+                const uint8_t* fa = facts + s * (kT * kStageFactBytes) + k * kT * kFactBytes;
                 const uint8_t* ra = tile + r0 * 128;
                 const uint8_t* rb = ra + 8 * 128;
-                const uint4 f0 = lds128(fa + g * 32 + (t4 & 1) * 16);
-                const uint4 f1 = lds128(fa + (g + 8) * 32 + (t4 & 1) * 16);
+                uint4 f0[kT], f1[kT];
+#pragma unroll
+                for (int t = 0; t < kT; ++t) {
+                    f0[t] = lds128(fa + t * kFactBytes + g * 32 + (t4 & 1) * 16);
+                    f1[t] = lds128(fa + t * kFactBytes + (g + 8) * 32 + (t4 & 1) * 16);
+                }
 #pragma unroll
                 for (int win = 0; win < 2; ++win) {
                     const uint4 xa = lds128(ra + (((4 * win + t4) ^ gr) << 4));
                     const uint4 xb = lds128(rb + (((4 * win + t4) ^ gr) << 4));
                     const uint32_t a0[4] = {xa.x, xb.x, xa.y, xb.y};
                     const uint32_t a1[4] = {xa.z, xb.z, xa.w, xb.w};
-                    Act<kF16>::mma(acc[0][win], a0, f0.x, f0.y, acc[0][win]);
-                    Act<kF16>::mma(acc[1][win], a0, f1.x, f1.y, acc[1][win]);
-                    Act<kF16>::mma(acc[0][win], a1, f0.z, f0.w, acc[0][win]);
-                    Act<kF16>::mma(acc[1][win], a1, f1.z, f1.w, acc[1][win]);
+#pragma unroll
+                    for (int t = 0; t < kT; ++t) {
+                        Act<kF16>::mma(acc[t][0][win], a0, f0[t].x, f0[t].y, acc[t][0][win]);
+                        Act<kF16>::mma(acc[t][1][win], a0, f1[t].x, f1[t].y, acc[t][1][win]);
+                        Act<kF16>::mma(acc[t][0][win], a1, f0[t].z, f0[t].w, acc[t][0][win]);
+                        Act<kF16>::mma(acc[t][1][win], a1, f1[t].z, f1[t].w, acc[t][1][win]);
+                    }
                 }
             }
             __syncwarp();
@@ -554,69 +586,81 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
         // warp rewrites copy k only at exchange k + 2, after every warp has arrived at
         // exchange k + 1, which each does only after reading its partner's values of
         // exchange k.  (fp32 addition commutes, so both partners form the same sum.)
-        float part[8];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            part[i] = acc[0][0][i] + acc[0][1][i];
-            part[4 + i] = acc[1][0][i] + acc[1][1][i];
-        }
-        {
-            float* buf = xchg + (n_xchg & 1u) * kXchgFloats;
-            uint64_t* bar = &xbar[n_xchg & 1u];
-            float4* mine = reinterpret_cast<float4*>(buf + (w * 32 + lane) * 8);
-            mine[0] = make_float4(part[0], part[1], part[2], part[3]);
-            mine[1] = make_float4(part[4], part[5], part[6], part[7]);
-            __syncwarp();
-            if (lane == 0) mbar_arrive(bar);
-            if (!mbar_wait(bar, (n_xchg >> 1) & 1u, abort, p.err)) return;
-            const int partner = (w + kGroupWarps) % kConsumerWarps;
-            const float4* other = reinterpret_cast<const float4*>(buf + (partner * 32 + lane) * 8);
-            const float4 o0 = other[0], o1 = other[1];
-            part[0] += o0.x; part[1] += o0.y; part[2] += o0.z; part[3] += o0.w;
-            part[4] += o1.x; part[5] += o1.y; part[6] += o1.z; part[7] += o1.w;
-            ++n_xchg;
-        }
-        if (sp.mode == kPart) {
-            // A unit shared with neighbouring CTAs: group 0 stores this CTA's fp32 partial h of
-            // it (rows r0, r0 + 8; ranks 2 t4, 2 t4 + 1 and 8 + 2 t4, 9 + 2 t4), for the B-decode
-            // kernel to add up.
-            if (grp == 0) {
-                float* piece = split_piece(p, static_cast<int>(blockIdx.x), u);
-#pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                    float* row = piece + (r0 + 8 * hr) * 16;
-                    __stcg(reinterpret_cast<float2*>(row + 2 * t4), make_float2(part[2 * hr], part[2 * hr + 1]));
-                    __stcg(reinterpret_cast<float2*>(row + 8 + 2 * t4),
-                           make_float2(part[4 + 2 * hr], part[5 + 2 * hr]));
-                }
-            }
-            continue;
-        }
-        const float sc = p.scaling * unit_weight(p, uc, un.b);
-        float h0[4], h1[4];
-#pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            h0[i] = part[i] * sc;
-            h1[i] = part[4 + i] * sc;
-        }
-        const uint32_t ha[4] = {Act<kF16>::pack(h0[0], h0[1]), Act<kF16>::pack(h0[2], h0[3]),
-                                Act<kF16>::pack(h1[0], h1[1]), Act<kF16>::pack(h1[2], h1[3])};
+        // (With several targets, one exchange per target.)
         const int row0 = un.mt * kBM + r0;                   // token rows row0 and row0 + 8
-        if (p.h_out) {
-            // shrink-only: store h (ranks 2 t4, 2 t4 + 1 and 8 + 2 t4, 9 + 2 t4 of rows row0, row0 + 8)
-            if (grp == 0) {
+        uint32_t ha[4];
+        bool unit_done = false;
 #pragma unroll
-                for (int hr = 0; hr < 2; ++hr) {
-                    const int row = row0 + 8 * hr;
-                    if (row < p.m) {
-                        uint32_t* hrow = reinterpret_cast<uint32_t*>(p.h_out + (static_cast<int64_t>(un.b) * p.m + row) * 16);
-                        hrow[t4] = ha[hr];
-                        hrow[4 + t4] = ha[2 + hr];
+        for (int t = 0; t < kT; ++t) {
+            float part[8];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                part[i] = acc[t][0][0][i] + acc[t][0][1][i];
+                part[4 + i] = acc[t][1][0][i] + acc[t][1][1][i];
+            }
+            {
+                float* buf = xchg + (n_xchg & 1u) * kXchgFloats;
+                uint64_t* bar = &xbar[n_xchg & 1u];
+                float4* mine = reinterpret_cast<float4*>(buf + (w * 32 + lane) * 8);
+                mine[0] = make_float4(part[0], part[1], part[2], part[3]);
+                mine[1] = make_float4(part[4], part[5], part[6], part[7]);
+                __syncwarp();
+                if (lane == 0) mbar_arrive(bar);
+                if (!mbar_wait(bar, (n_xchg >> 1) & 1u, abort, p.err)) return;
+                const int partner = (w + kGroupWarps) % kConsumerWarps;
+                const float4* other = reinterpret_cast<const float4*>(buf + (partner * 32 + lane) * 8);
+                const float4 o0 = other[0], o1 = other[1];
+                part[0] += o0.x; part[1] += o0.y; part[2] += o0.z; part[3] += o0.w;
+                part[4] += o1.x; part[5] += o1.y; part[6] += o1.z; part[7] += o1.w;
+                ++n_xchg;
+            }
+            if (sp.mode == kPart) {
+                // A unit shared with neighbouring CTAs (split shrink, one target): group 0 stores
+                // this CTA's fp32 partial h of it (rows r0, r0 + 8; ranks 2 t4, 2 t4 + 1 and
+                // 8 + 2 t4, 9 + 2 t4), for the B-decode kernel to add up.
+                if (grp == 0) {
+                    float* piece = split_piece(p, static_cast<int>(blockIdx.x), u);
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
+                        float* row = piece + (r0 + 8 * hr) * 16;
+                        __stcg(reinterpret_cast<float2*>(row + 2 * t4), make_float2(part[2 * hr], part[2 * hr + 1]));
+                        __stcg(reinterpret_cast<float2*>(row + 8 + 2 * t4),
+                               make_float2(part[4 + 2 * hr], part[5 + 2 * hr]));
                     }
                 }
+                unit_done = true;
+                continue;
             }
-            continue;
+            const float sc = (kT == 1 ? p.scaling : p.scaling_t[t]) * unit_weight(p, uc, un.b);
+            float h0[4], h1[4];
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                h0[i] = part[i] * sc;
+                h1[i] = part[4 + i] * sc;
+            }
+            ha[0] = Act<kF16>::pack(h0[0], h0[1]);
+            ha[1] = Act<kF16>::pack(h0[2], h0[3]);
+            ha[2] = Act<kF16>::pack(h1[0], h1[1]);
+            ha[3] = Act<kF16>::pack(h1[2], h1[3]);
+            if (p.h_out) {
+                // shrink-only: store h (ranks 2 t4, 2 t4 + 1 and 8 + 2 t4, 9 + 2 t4 of rows row0, row0 + 8)
+                if (grp == 0) {
+                    __nv_bfloat16* h_base = kT == 1 ? p.h_out : p.h_t[t];
+#pragma unroll
+                    for (int hr = 0; hr < 2; ++hr) {
+                        const int row = row0 + 8 * hr;
+                        if (row < p.m) {
+                            uint32_t* hrow = reinterpret_cast<uint32_t*>(h_base + (static_cast<int64_t>(un.b) * p.m + row) * 16);
+                            hrow[t4] = ha[hr];
+                            hrow[4 + t4] = ha[2 + hr];
+                        }
+                    }
+                }
+                unit_done = true;
+            }
         }
+        if (unit_done) continue;
+        if constexpr (kT > 1) continue;      // several targets: shrink-only
         uint16_t* out_b = static_cast<uint16_t*>(p.out) + static_cast<int64_t>(un.b) * p.m * p.d_out;
         float* outf_b = static_cast<float*>(p.out) + static_cast<int64_t>(un.b) * p.m * p.d_out;
         for (int q = 0; q < un.so; ++q, ++pos) {
@@ -722,7 +766,7 @@ __device__ void run_consumer(int w, int lane, const SgmvParams& p, const UnitCac
     }
 }
 
-template <int kRank, bool kStaged, int kFeed, bool kF16>
+template <int kRank, bool kStaged, int kFeed, bool kF16, int kT = 1>
 __global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
     sgmv_index_kernel(const __grid_constant__ CUtensorMap tmx, const __grid_constant__ CUtensorMap tmo_ld,
                       const __grid_constant__ SgmvParams p) {
@@ -732,11 +776,13 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
     // divide kStages; otherwise two feeders could share a stage in different phases.
     static_assert(kStages % kFeed == 0, "each feeder warp must own whole stages");
     static_assert(kStages % kGroups == 0, "each consumer group must own whole stages");
+    // several targets only in the staged shrink (their factor chunks come decoded)
+    static_assert(kT == 1 || (kStaged && kRank == 16 && kT <= kMaxTargets), "multi-target form");
     extern __shared__ uint8_t smem_raw[];
     uint8_t* base = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     uint8_t* tiles = base;
     uint8_t* facts = tiles + kStages * kStageBytes;
-    DecodeTables* tab = reinterpret_cast<DecodeTables*>(facts + kStages * kStageFactBytes);
+    DecodeTables* tab = reinterpret_cast<DecodeTables*>(facts + kStages * kT * kStageFactBytes);
     float* xchg = reinterpret_cast<float*>(tab + 1);                       // 2 x kXchgFloats
     uint64_t* full = reinterpret_cast<uint64_t*>(xchg + 2 * kXchgFloats);
     uint64_t* empty = full + kStages;
@@ -779,14 +825,15 @@ __global__ void __launch_bounds__(32 * (kConsumerWarps + kFeed), 1)
 
     uint32_t issued = 0;
     if (warp < kConsumerWarps) {
-        run_consumer<kRank, kF16>(warp, lane, p, uc, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end, hb,
+        run_consumer<kRank, kF16, kT>(warp, lane, p, uc, tiles, facts, full, empty, xchg, xbar, abort, u_begin, u_end, hb,
                                   he);
     } else {
         if (lane == 0) {
             prefetch_tmap(&tmx);
             prefetch_tmap(&tmo_ld);
         }
-        issued = run_feeder<kRank, kStaged, kFeed, kF16>(warp - kFirstFeedWarp, lane, p, uc, &tmx, &tmo_ld, tiles, facts,
+        issued = run_feeder<kRank, kStaged, kFeed, kF16, kT>(warp - kFirstFeedWarp, lane, p, uc, &tmx, &tmo_ld, tiles,
+                                                                 facts,
                                                    tab, lut_s, full, empty, abort, u_begin, u_end, hb, he);
     }
     __syncthreads();
@@ -837,6 +884,40 @@ __global__ void __launch_bounds__(256) decode_chunks_kernel(const __grid_constan
         uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
         if (live) finish_raw<LITHE_MAX_LEVELS>(c < un.nx ? p.ia : p.ib, raw, k, p.err);
         decode_chunk<kRank, kF16>(p, &tab, lut_s, un, c, live, k, ws + w * kFactBytes, lane);
+    }
+}
+
+// One 64-column chunk j of sample b's B factor (view ib, b_blocks blocks, d_out rows) decoded
+// into bdec (batch, d_out, 16) bf16 by one warp; zero for an unrouted sample.
+__device__ __forceinline__ void bdec_chunk(const SgmvParams& p, const IndexView& ib, int b_blocks, int d_out,
+                                           __nv_bfloat16* bdec, int b, int j, const DecodeTables* tab,
+                                           const float* lut_s, int lane) {
+    const uint32_t half = lane & 1;
+    const int32_t sid = __ldg(p.ids + b);
+    Unit un;
+    un.b = b;
+    un.mt = 0;
+    un.slot = sid;
+    un.active = sid >= 0 && static_cast<int64_t>(sid) < p.n_slots;
+    un.nx = 0;                        // chunk j of the B side
+    un.no = (d_out + kChunk - 1) / kChunk;
+    RawIndices<LITHE_MAX_LEVELS> raw;
+    const bool live = un.active && chunk_fetch_v<16>(p.ia, ib, p.a_blocks_per_row, b_blocks, un, j, lane, raw);
+    float v[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = 0.f;
+    if (live) {
+        uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
+        finish_raw<LITHE_MAX_LEVELS>(ib, raw, k, p.err);
+        decode_values(p, tab, lut_s, 1, k, half, v);
+    }
+    const int G = 16 * j + (lane >> 1);
+    if (4 * G < d_out) {
+        const uint4 q = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
+                                   pack_bf16x2(v[6], v[7]));
+        __nv_bfloat16* dst = bdec + (static_cast<int64_t>(b) * d_out + 4 * G) * 16 + 8 * half;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(dst + i * 16) = q;
     }
 }
 
@@ -901,7 +982,6 @@ __global__ void __launch_bounds__(256) decode_bdec_kernel(const __grid_constant_
     build_decode_tables(&tab, &p.lut[0][0][0], p.ia.levels, threadIdx.x, blockDim.x);
     __syncthreads();
     const int lane = threadIdx.x & 31;
-    const uint32_t half = lane & 1;
     const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
     const int64_t n_dec = bdec ? static_cast<int64_t>(batch) * p.n_ochunks : 0;
     const int64_t total = n_dec + (p.split ? p.split_grid - 1 : 0);
@@ -912,32 +992,59 @@ __global__ void __launch_bounds__(256) decode_bdec_kernel(const __grid_constant_
         }
         const int b = static_cast<int>(w / p.n_ochunks);
         const int j = static_cast<int>(w - static_cast<int64_t>(b) * p.n_ochunks);
-        const int32_t sid = __ldg(p.ids + b);
-        Unit un;
-        un.b = b;
-        un.mt = 0;
-        un.slot = sid;
-        un.active = sid >= 0 && static_cast<int64_t>(sid) < p.n_slots;
-        un.nx = p.n_xchunks;
-        un.no = p.n_ochunks;
-        RawIndices<LITHE_MAX_LEVELS> raw;
-        const bool live = un.active && chunk_fetch<16>(p, un, un.nx + j, lane, raw);
-        float v[8];
-#pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = 0.f;
-        if (live) {
+        bdec_chunk(p, p.ib, p.b_blocks, p.d_out, bdec, b, j, &tab, lut_s, lane);
+    }
+}
+
+// lithe_lora_prep_multi, phase 1: every routed sample's A chunks of the n_targets linears,
+// decoded once into ws in the staged shrink's layout (chunk c of target t of sample b at
+// ((b * n_xchunks + c) * n_targets + t) * 512 bytes), and each target's b_dec where asked.
+// One warp per (sample, chunk, target) or per (target, sample, out chunk).
+__global__ void __launch_bounds__(256) prep_multi_decode_kernel(const __grid_constant__ SgmvParams p, uint8_t* ws,
+                                                                int32_t batch) {
+    __shared__ DecodeTables tab;
+    __shared__ float lut_s[kLutFloats];
+    for (int i = threadIdx.x; i < kLutFloats; i += blockDim.x) lut_s[i] = (&p.lut[0][0][0])[i];
+    build_decode_tables(&tab, &p.lut[0][0][0], p.ia.levels, threadIdx.x, blockDim.x);
+    __syncthreads();
+    const int lane = threadIdx.x & 31;
+    const int nt = p.n_targets;
+    const int64_t warps = static_cast<int64_t>(gridDim.x) * (blockDim.x >> 5);
+    const int64_t n_a = static_cast<int64_t>(batch) * p.n_xchunks * nt;
+    int64_t n_b[kMaxTargets];
+    int64_t total = n_a;
+    for (int t = 0; t < kMaxTargets; ++t) {
+        n_b[t] = t < nt && p.bdec_t[t] ? static_cast<int64_t>(batch) * p.n_ochunks_t[t] : 0;
+        total += n_b[t];
+    }
+    for (int64_t w = static_cast<int64_t>(blockIdx.x) * (blockDim.x >> 5) + (threadIdx.x >> 5); w < total; w += warps) {
+        if (w < n_a) {
+            const int b = static_cast<int>(w / (static_cast<int64_t>(p.n_xchunks) * nt));
+            const int rem = static_cast<int>(w - static_cast<int64_t>(b) * p.n_xchunks * nt);
+            const int c = rem / nt, t = rem - (rem / nt) * nt;
+            const int32_t sid = __ldg(p.ids + b);
+            if (sid < 0 || static_cast<int64_t>(sid) >= p.n_slots) continue;   // its h rows are zeroed
+            Unit un;
+            un.b = b;
+            un.mt = 0;
+            un.slot = sid;
+            un.active = true;
+            un.nx = p.n_xchunks;
+            un.no = 0;
+            RawIndices<LITHE_MAX_LEVELS> raw;
+            const bool live = chunk_fetch_v<16>(p.ia_t[t], p.ib_t[t], p.a_blocks_per_row, p.b_blocks_t[t], un, c, lane,
+                                                raw);
             uint32_t k[LITHE_MAX_LEVELS] = {0, 0, 0, 0};
-            finish_raw<LITHE_MAX_LEVELS>(p.ib, raw, k, p.err);
-            decode_values(p, &tab, lut_s, 1, k, half, v);
+            if (live) finish_raw<LITHE_MAX_LEVELS>(p.ia_t[t], raw, k, p.err);
+            decode_chunk<16, false>(p, &tab, lut_s, un, c, live, k, ws + w * kFactBytes, lane);
+            continue;
         }
-        const int G = 16 * j + (lane >> 1);
-        if (4 * G < p.d_out) {
-            const uint4 q = make_uint4(pack_bf16x2(v[0], v[1]), pack_bf16x2(v[2], v[3]), pack_bf16x2(v[4], v[5]),
-                                       pack_bf16x2(v[6], v[7]));
-            __nv_bfloat16* dst = bdec + (static_cast<int64_t>(b) * p.d_out + 4 * G) * 16 + 8 * half;
-#pragma unroll
-            for (int i = 0; i < 4; ++i) *reinterpret_cast<uint4*>(dst + i * 16) = q;
-        }
+        int64_t r = w - n_a;
+        int t = 0;
+        while (r >= n_b[t]) r -= n_b[t++];
+        const int b = static_cast<int>(r / p.n_ochunks_t[t]);
+        const int j = static_cast<int>(r - static_cast<int64_t>(b) * p.n_ochunks_t[t]);
+        bdec_chunk(p, p.ib_t[t], p.b_blocks_t[t], p.d_out_t[t], p.bdec_t[t], b, j, &tab, lut_s, lane);
     }
 }
 
@@ -963,6 +1070,24 @@ static int32_t launch_rank(const CUtensorMap& tmx, const CUtensorMap& tmo_ld, co
     kern<<<grid, 32 * (kConsumerWarps + kFeed), kSmemBytes, stream>>>(tmx, tmo_ld, p);
     cudaError_t e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "sgmv_index_kernel launch");
+    return LITHE_OK;
+}
+
+// The staged shrink of kT targets (lithe_lora_prep_multi, phase 2).
+template <int kT>
+static int32_t launch_multi_shrink(const CUtensorMap& tmx, const SgmvParams& p, int grid, int device,
+                                   cudaStream_t stream) {
+    static bool configured[64] = {false};
+    auto kern = sgmv_index_kernel<16, true, kFeedStaged, false, kT>;
+    if (!configured[device]) {
+        cudaError_t e = cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             static_cast<int>(smem_bytes(kT)));
+        if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(sgmv_index_kernel, targets)");
+        configured[device] = true;
+    }
+    kern<<<grid, 32 * (kConsumerWarps + kFeedStaged), smem_bytes(kT), stream>>>(tmx, tmx, p);
+    cudaError_t e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "sgmv_index_kernel launch (targets)");
     return LITHE_OK;
 }
 
@@ -1364,6 +1489,117 @@ int32_t sgmv_index_impl(const void* x, void* out, int32_t accumulate, const lith
 #undef LITHE_LAUNCH
 }
 
+int64_t prep_multi_bytes(int32_t batch, int32_t d_in, int32_t n_targets) {
+    if (batch <= 0 || d_in <= 0 || n_targets <= 0) return 0;
+    return static_cast<int64_t>(batch) * (d_in / kChunk) * n_targets * kFactBytes;
+}
+
+// lithe_lora_prep_multi: n_targets rank-16 linears that read the same x.
+int32_t prep_multi_impl(const void* x, int32_t n_targets, const lithe_index_view* idx_a,
+                        const lithe_index_view* idx_b, const int32_t* d_out, int64_t n_slots, const int32_t* ids,
+                        const float* weights, int32_t batch, int32_t m, int32_t d_in, int32_t rank, const float* lut,
+                        const float* scaling, void* const* h, void* const* b_dec, int32_t* err_flag, void* ws,
+                        int64_t ws_bytes, void* stream) {
+    if (batch < 0 || m < 0) return fail_arg("batch (%d) and m (%d) must be >= 0", batch, m);
+    if (n_targets < 1 || n_targets > kMaxTargets)
+        return fail_unsupported("n_targets must be in [1, %d], got %d", kMaxTargets, n_targets);
+    if (!idx_a || !idx_b || !d_out || !scaling || !h || !b_dec)
+        return fail_arg("idx_a, idx_b, d_out, scaling, h and b_dec must be non-NULL arrays");
+    if (rank != 16) return fail_unsupported("lithe_lora_prep_multi supports rank 16, got %d", rank);
+    if (d_in <= 0 || d_in % 64) return fail_arg("d_in must be a positive multiple of 64, got %d", d_in);
+    if (!lut) return fail_arg("lut is NULL");
+    if (n_slots < 0) return fail_arg("n_slots must be >= 0");
+    int32_t rc = LITHE_OK;
+    for (int t = 0; t < n_targets; ++t) {
+        if (d_out[t] <= 0 || d_out[t] % 8) return fail_arg("d_out[%d] must be a positive multiple of 8", t);
+        rc = check_view(&idx_a[t], "idx_a");
+        if (rc != LITHE_OK) return rc;
+        rc = check_view(&idx_b[t], "idx_b");
+        if (rc != LITHE_OK) return rc;
+        if (idx_a[t].num_levels != idx_a[0].num_levels || idx_b[t].num_levels != idx_a[0].num_levels)
+            return fail_arg("every view must have the same num_levels");
+        const int64_t nb_a = 16LL * d_in / 64, nb_b = static_cast<int64_t>(d_out[t]) * 16 / 64;
+        if ((idx_a[t].format == LITHE_IDX_PACKED9 && idx_a[t].offset + idx_a[t].num_levels * nb_a > 0xffffffffLL) ||
+            (idx_b[t].format == LITHE_IDX_PACKED9 && idx_b[t].offset + idx_b[t].num_levels * nb_b > 0xffffffffLL))
+            return fail_unsupported("packed stream positions of one slot must fit in 32 bits");
+    }
+    if (batch == 0 || m == 0) return LITHE_OK;
+    if (!x || !ids) return fail_arg("x and ids must be non-NULL");
+    if (reinterpret_cast<uintptr_t>(x) % 16) return fail_arg("x must be 16-byte aligned");
+    for (int t = 0; t < n_targets; ++t) {
+        if (!h[t]) return fail_arg("h[%d] is NULL", t);
+        if (reinterpret_cast<uintptr_t>(h[t]) % 16 || reinterpret_cast<uintptr_t>(b_dec[t]) % 16)
+            return fail_arg("h[%d] and b_dec[%d] must be 16-byte aligned", t, t);
+    }
+    const int64_t n_mtiles = (static_cast<int64_t>(m) + kBM - 1) / kBM;
+    if (n_mtiles * batch > 0x7fffffffLL || static_cast<int64_t>(m) * batch > 0x7fffffffLL)
+        return fail_arg("batch * m exceeds 2^31");
+    const int64_t need = prep_multi_bytes(batch, d_in, n_targets);
+    if (!ws || reinterpret_cast<uintptr_t>(ws) % 16) return fail_arg("workspace must be non-NULL and 16-byte aligned");
+    if (ws_bytes < need)
+        return fail_arg("workspace holds %lld bytes, this call needs %lld", (long long)ws_bytes, (long long)need);
+
+    int device = 0, sms = 0;
+    rc = current_device_sms(&device, &sms);
+    if (rc != LITHE_OK) return rc;
+
+    SgmvParams p{};
+    p.ia = to_view(&idx_a[0]);
+    p.ib = to_view(&idx_b[0]);
+    p.ids = ids;
+    p.weights = weights;
+    p.err = err_flag;
+    p.n_slots = n_slots;
+    p.m = m;
+    p.d_in = d_in;
+    p.d_out = d_out[0];
+    p.n_mtiles = static_cast<int32_t>(n_mtiles);
+    p.n_xchunks = d_in / kChunk;
+    p.total_units = static_cast<int32_t>(n_mtiles * batch);
+    p.a_blocks_per_row = d_in / 64;
+    p.b_blocks = d_out[0] * 16 / 64;
+    p.scaling = scaling[0];
+    expand_lut(lut, idx_a[0].num_levels, p.lut);
+    p.n_targets = n_targets;
+    for (int t = 0; t < n_targets; ++t) {
+        p.ia_t[t] = to_view(&idx_a[t]);
+        p.ib_t[t] = to_view(&idx_b[t]);
+        p.d_out_t[t] = d_out[t];
+        p.b_blocks_t[t] = d_out[t] * 16 / 64;
+        p.n_ochunks_t[t] = (d_out[t] + kChunk - 1) / kChunk;
+        p.scaling_t[t] = scaling[t];
+        p.h_t[t] = static_cast<__nv_bfloat16*>(h[t]);
+        p.bdec_t[t] = static_cast<__nv_bfloat16*>(b_dec[t]);
+    }
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    {   // phase 1: the targets' A chunks into ws, and their b_dec
+        int64_t warps_needed = static_cast<int64_t>(batch) * p.n_xchunks * n_targets;
+        for (int t = 0; t < n_targets; ++t)
+            if (b_dec[t]) warps_needed += static_cast<int64_t>(batch) * p.n_ochunks_t[t];
+        int64_t blocks = (warps_needed + 7) / 8;
+        if (blocks > 2LL * sms) blocks = 2LL * sms;
+        prep_multi_decode_kernel<<<static_cast<unsigned>(blocks), 256, 0, s>>>(p, static_cast<uint8_t*>(ws), batch);
+        cudaError_t e = cudaGetLastError();
+        if (e != cudaSuccess) return fail_cuda(e, "prep_multi_decode_kernel launch");
+    }
+    // phase 2: the staged shrink, x read once for every target
+    CUtensorMap tmx;
+    rc = encode_bf16_chunked(&tmx, x, d_in, static_cast<uint64_t>(m) * batch, kBM, kStageChunks);
+    if (rc != LITHE_OK) return rc;
+    p.ws = static_cast<const uint8_t*>(ws);
+    p.n_chunks = p.n_xchunks;
+    p.n_ochunks = 0;
+    p.accumulate = 1;                 // unrouted samples skip all work (their h rows are zeroed)
+    p.h_out = p.h_t[0];
+    const int grid = static_cast<int>(p.total_units < sms ? p.total_units : sms);
+    switch (n_targets) {
+        case 1: return launch_multi_shrink<1>(tmx, p, grid, device, s);
+        case 2: return launch_multi_shrink<2>(tmx, p, grid, device, s);
+        case 3: return launch_multi_shrink<3>(tmx, p, grid, device, s);
+        default: return launch_multi_shrink<4>(tmx, p, grid, device, s);
+    }
+}
+
 }  // namespace lithe
 
 extern "C" int32_t lithe_sgmv_index(const void* x, void* out, int32_t accumulate, const lithe_index_view* idx_a,
@@ -1415,6 +1651,21 @@ extern "C" int64_t lithe_lora_prep_workspace_bytes(int32_t batch, int32_t m, int
     const int32_t rc = lithe::current_device_sms(&device, &sms);
     if (rc != LITHE_OK) return rc;
     return lithe::prep_split_bytes(lithe::prep_split_grid(batch, m, d_in, sms));
+}
+
+extern "C" int64_t lithe_lora_prep_multi_workspace_bytes(int32_t batch, int32_t d_in, int32_t n_targets) {
+    return lithe::prep_multi_bytes(batch, d_in, n_targets);
+}
+
+extern "C" int32_t lithe_lora_prep_multi(const void* x, int32_t n_targets, const lithe_index_view* idx_a,
+                                         const lithe_index_view* idx_b, const int32_t* d_out, int64_t n_slots,
+                                         const int32_t* ids, const float* weights, int32_t batch, int32_t m,
+                                         int32_t d_in, int32_t rank, const float* lut, const float* scaling,
+                                         void* const* h, void* const* b_dec, int32_t* err_flag, void* workspace,
+                                         int64_t workspace_bytes, void* stream) {
+    lithe::clear_error();
+    return lithe::prep_multi_impl(x, n_targets, idx_a, idx_b, d_out, n_slots, ids, weights, batch, m, d_in, rank, lut,
+                                  scaling, h, b_dec, err_flag, workspace, workspace_bytes, stream);
 }
 
 extern "C" int64_t lithe_sgmv_workspace_bytes(int32_t batch, int32_t d_in, int32_t d_out) {

@@ -7,13 +7,15 @@
 * ``layers``  nn.Module wrappers that route each sample of a batch to its own adapter.
 """
 from ._launch import device_errors, raise_device_errors
-from .layers import IndexLoRALinear, PackedLoRALinear, PerSampleLoRALinear, wrap_linears, wrap_packed
+from .layers import (IndexLoRALinear, PackedLoRALinear, PerSampleLoRALinear, SharedInputPrep, group_shared_inputs,
+                     wrap_linears, wrap_packed)
 from .packed import (PackedBank, PackedLayout, SlotLoader, decode_packed, flat_indices, pack_adapter,
                      pack_indices, split_decoded, unpack_indices)
 from .shared import packed_codebook_lora_delta_, shared_codebook_lora_delta, shared_codebook_lora_delta_
 
 __all__ = [
-    "IndexLoRALinear", "PackedLoRALinear", "PerSampleLoRALinear", "wrap_linears", "wrap_packed",
+    "IndexLoRALinear", "PackedLoRALinear", "PerSampleLoRALinear", "SharedInputPrep", "group_shared_inputs",
+    "wrap_linears", "wrap_packed",
     "PackedBank", "PackedLayout", "SlotLoader", "decode_packed", "flat_indices", "pack_adapter", "pack_indices",
     "split_decoded", "unpack_indices",
     "shared_codebook_lora_delta", "shared_codebook_lora_delta_", "packed_codebook_lora_delta_",

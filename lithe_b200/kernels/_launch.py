@@ -8,7 +8,7 @@ from __future__ import annotations
 
 import ctypes
 import threading
-from typing import Optional
+from typing import Optional, Sequence
 
 import numpy as np
 import torch
@@ -371,6 +371,51 @@ def lora_prep_(x: torch.Tensor, *, view_a: _lib.IndexView, view_b: _lib.IndexVie
         else:
             rc = _lib.lib().lithe_lora_prep(*common, stream_handle(x.device))
             _lib.check(rc, "lithe_lora_prep")
+
+
+def prep_multi_workspace_bytes(batch: int, d_in: int, n_targets: int) -> int:
+    return int(_lib.lib().lithe_lora_prep_multi_workspace_bytes(batch, d_in, n_targets))
+
+
+def lora_prep_multi_(x: torch.Tensor, *, views_a: Sequence[_lib.IndexView], views_b: Sequence[_lib.IndexView],
+                     d_outs: Sequence[int], n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor],
+                     lut: np.ndarray, scalings: Sequence[float], hs: Sequence[torch.Tensor],
+                     b_decs: Sequence[Optional[torch.Tensor]], err: Optional[torch.Tensor] = None,
+                     workspace: Optional[torch.Tensor] = None) -> None:
+    """lithe_lora_prep_multi: h and b_dec of up to 4 rank-16 linears that read the same x, with
+    x streamed once.  hs[t] (B*M, 16) and b_decs[t] (B, d_outs[t], 16) are bf16; a b_dec entry
+    may be None."""
+    _require_cuda(x, "x")
+    if x.dtype != torch.bfloat16 or x.dim() != 3 or not x.is_contiguous():
+        raise ValueError("x must be a contiguous (B, M, d_in) bfloat16 tensor")
+    n = len(views_a)
+    if not (1 <= n <= 4) or not (len(views_b) == len(d_outs) == len(scalings) == len(hs) == len(b_decs) == n):
+        raise ValueError("1 to 4 targets, with one view pair, d_out, scaling, h and b_dec each")
+    bsz, m, d_in = x.shape
+    for h, bd, d_out in zip(hs, b_decs, d_outs):
+        if h.dtype != torch.bfloat16 or h.numel() != bsz * m * 16 or not h.is_contiguous() or h.device != x.device:
+            raise ValueError("every h must be a contiguous (B*M, 16) bfloat16 tensor on x's device")
+        if bd is not None and (bd.dtype != torch.bfloat16 or bd.numel() != bsz * d_out * 16
+                               or not bd.is_contiguous() or bd.device != x.device):
+            raise ValueError("every b_dec must be a contiguous (B, d_out, 16) bfloat16 tensor on x's device")
+    if ids.dtype != torch.int32 or ids.numel() != bsz or ids.device != x.device or not ids.is_contiguous():
+        raise ValueError("ids must be a contiguous (B,) int32 tensor on x's device")
+    if err is None:
+        err = error_word(x.device)
+    if workspace is None:
+        workspace = torch.empty(max(prep_multi_workspace_bytes(bsz, d_in, n), 16), dtype=torch.uint8,
+                                device=x.device)
+    _require_cuda(workspace, "workspace")
+    va = (_lib.IndexView * n)(*views_a)
+    vb = (_lib.IndexView * n)(*views_b)
+    with device_ctx(x.device):
+        rc = _lib.lib().lithe_lora_prep_multi(
+            x.data_ptr(), n, va, vb, (ctypes.c_int32 * n)(*[int(d) for d in d_outs]), int(n_slots), ids.data_ptr(),
+            weights.data_ptr() if weights is not None else None, bsz, m, d_in, 16, lut_array(lut),
+            (ctypes.c_float * n)(*[float(v) for v in scalings]), (ctypes.c_void_p * n)(*[h.data_ptr() for h in hs]),
+            (ctypes.c_void_p * n)(*[bd.data_ptr() if bd is not None else None for bd in b_decs]), err.data_ptr(),
+            workspace.data_ptr(), workspace.numel(), stream_handle(x.device))
+    _lib.check(rc, "lithe_lora_prep_multi")
 
 
 def pack_raw_batch_(raw: torch.Tensor, segments: torch.Tensor, levels: int, bank: torch.Tensor,

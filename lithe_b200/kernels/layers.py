@@ -14,7 +14,8 @@ otherwise ``assign`` (B,) gives the slot of every sample, -1 for none.
 """
 from __future__ import annotations
 
-from typing import Callable, Dict, Iterable, Optional, Tuple
+import weakref
+from typing import Callable, Dict, Iterable, List, Optional, Tuple
 
 import torch
 from torch import nn
@@ -96,6 +97,109 @@ class IndexLoRALinear(nn.Module):
 FUSED_GEMM_MAX_K = 4096
 
 
+class _InputKey:
+    """Identifies one call's input, routing and weights by tensor identity and version, through
+    weak references: a key does not keep the activation it names alive."""
+
+    def __init__(self, x3, ids, w, scaling):
+        self._refs = (weakref.ref(x3), weakref.ref(ids), None if w is None else weakref.ref(w))
+        self._vals = (x3._version, ids._version, None if w is None else w._version, scaling)
+
+    def alive(self) -> bool:
+        """The input tensor still exists (an activation is freed once its forward is done)."""
+        return self._refs[0]() is not None
+
+    def matches(self, x3, ids, w, scaling) -> bool:
+        rx, ri, rw = self._refs
+        if rx() is not x3 or ri() is not ids or (rw is None) != (w is None) or (rw is not None and rw() is not w):
+            return False
+        return self._vals == (x3._version, ids._version, None if w is None else w._version, scaling)
+
+
+class SharedInputPrep:
+    """Fused-GEMM linears with their own adapter modules that read the same input tensor -- the
+    q, k and v projections of one attention block.  The first member to run on an input
+    computes every member's h and b_dec with one lithe_lora_prep_multi (the input read once
+    instead of once per linear) and hands the others theirs; results are bit-identical to
+    each member's own lithe_lora_prep.  A member called on another input while results for a
+    live input are pending, called again on an input it already took, on the cuBLAS path, or
+    under torch.compile (the hand-over keys on tensor identity, which a traced graph does not
+    have), computes its own.  Pending results for an input that has been freed are dropped.  Members must share one ``assign``
+    tensor (int32, on the device) for the hand-over to apply."""
+
+    def __init__(self, members: Iterable["PackedLoRALinear"]):
+        members = list(members)
+        if not 2 <= len(members) <= 4:
+            raise ValueError(f"a shared-input group has 2 to 4 members, got {len(members)}")
+        first = members[0]
+        for m in members:
+            if not isinstance(m, PackedLoRALinear) or m.rows is not None or m.rank != 16:
+                raise ValueError("group members are rank-16 PackedLoRALinear layers serving whole modules")
+            if m.bank is not first.bank or m.base.in_features != first.base.in_features:
+                raise ValueError("group members must share one bank and their in_features")
+        self.members = members
+        for m in members:
+            m.prep_group = self
+        self._key: Optional[_InputKey] = None
+        self._ready: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def prep(self, layer: "PackedLoRALinear", x3: torch.Tensor, ids: torch.Tensor,
+             w: Optional[torch.Tensor]) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
+        """(h, b_dec) of ``layer`` for this call, or None when the group does not apply."""
+        if self._key is not None:
+            if self._key.matches(x3, ids, w, None):
+                got = self._ready.pop(id(layer), None)
+                if not self._ready:
+                    self._key = None
+                # None: this member already took its result for this input and is called on it
+                # again; it prepares its own
+                return got
+            if self._key.alive():
+                return None         # results for another, live input are pending: prepare alone
+        members = [m for m in self.members
+                   if m.fused_gemm and m._gemm_ok(x3) and _slot_ids(m.assign, x3) is ids
+                   and ((w is None and m.weights is None) or (w is not None and m._weights(x3) is w))]
+        if layer not in members or len(members) < 2:
+            return None
+        words = layer.bank.words
+        outs = torch.ops.lithe_b200.lora_prep_multi(
+            x3, words, words, [v for m in members for v in m._va], [v for m in members for v in m._vb],
+            layer.bank.n_slots, ids, w, [m.base.out_features for m in members], layer._lut,
+            [m.scaling for m in members])
+        n = len(members)
+        self._ready = {id(m): (outs[i], outs[n + i]) for i, m in enumerate(members) if m is not layer}
+        self._key = _InputKey(x3, ids, w, None)
+        i = members.index(layer)
+        return outs[i], outs[n + i]
+
+
+# Sibling linears of a FLUX-shaped (diffusers-named) transformer that read one input tensor:
+# the image and the text stream's q / k / v of a double block, and a single block's q / k / v
+# together with its proj_mlp.
+_SHARED_INPUT_SETS = (("attn.to_q", ("attn.to_q", "attn.to_k", "attn.to_v", "proj_mlp")),
+                      ("attn.add_q_proj", ("attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj")))
+
+
+def group_shared_inputs(modules: Dict[str, nn.Module]) -> List[SharedInputPrep]:
+    """Group the wrapped linears of ``modules`` ({diffusers path: layer}) that read the same
+    input (see _SHARED_INPUT_SETS; a double block's proj_mlp does not exist, so its q / k / v
+    form the group) into SharedInputPrep objects.  Only whole-module PackedLoRALinear layers
+    of one bank join; Kohya split targets already share one h per fused module."""
+    groups = []
+    for path in modules:
+        for lead, names in _SHARED_INPUT_SETS:
+            if not path.endswith(lead):
+                continue
+            block = path[: -len(lead)]
+            members = [modules[block + n] for n in names if block + n in modules]
+            if (len(members) >= 2 and all(isinstance(m, PackedLoRALinear) and m.rows is None and m.rank == 16
+                                          and m.bank is members[0].bank
+                                          and m.base.in_features == members[0].base.in_features
+                                          and m.prep_group is None for m in members)):
+                groups.append(SharedInputPrep(members))
+    return groups
+
+
 class PackedLoRALinear(nn.Module):
     """y = W x + per-sample delta from module ``name`` of a shared packed bank.
 
@@ -136,6 +240,8 @@ class PackedLoRALinear(nn.Module):
         # the custom ops' arguments that do not change between calls
         self._va, self._vb = bank.view_params(name, self.rows)
         self._lut = bank.lut_list
+        # set by SharedInputPrep: siblings that read the same input share one prep launch
+        self.prep_group: Optional["SharedInputPrep"] = None
 
     def _gemm_ok(self, x3: torch.Tensor) -> bool:
         w = self.base.weight
@@ -166,20 +272,16 @@ class PackedLoRALinear(nn.Module):
         return self.weights.to(device=x3.device, dtype=torch.float32).contiguous()
 
     def _h_key(self, x3, ids, w):
-        """(tensors compared by identity, values compared by equality)."""
-        return (x3, ids, w), (x3._version, ids._version, None if w is None else w._version, self.scaling)
+        return _InputKey(x3, ids, w, self.scaling)
 
     def _shared_h(self, x3, ids, w) -> Optional[torch.Tensor]:
-        """The h a sibling split target computed for the same input, routing and scale, if any.
-        The entry holds the tensors themselves, so a hit needs the very same (unmodified) objects."""
+        """The h a sibling split target computed for the same input, routing and scale, if any
+        (the very same, unmodified tensor objects)."""
         entry = getattr(self.bank, "_shared_h", {}).get(self.name)
         if entry is None:
             return None
-        (objs, vals), h = entry
-        mine_objs, mine_vals = self._h_key(x3, ids, w)
-        if all(a is b for a, b in zip(objs, mine_objs)) and vals == mine_vals:
-            return h
-        return None
+        key, h = entry
+        return h if key.matches(x3, ids, w, self.scaling) else None
 
     def _store_h(self, x3, ids, w, h) -> None:
         if not hasattr(self.bank, "_shared_h"):
@@ -195,16 +297,25 @@ class PackedLoRALinear(nn.Module):
         # called with the same input, so h = x . A^T is computed once and reused by the others.  The
         # reuse keys on tensor identity, which a traced graph does not have: under torch.compile
         # every target computes its own h (the same values).
-        share = self.rows is not None and not torch.compiler.is_compiling()
-        h = self._shared_h(x3, ids, w) if share else None
-        fresh = h is None
-        words = self.bank.words
-        h_new, b_dec = torch.ops.lithe_b200.lora_prep(x3, words, words, self._va, self._vb, self.bank.n_slots, ids, w,
-                                                      d_out, self._lut, self.scaling, fresh)
-        if fresh:
-            h = h_new
-            if share:
-                self._store_h(x3, ids, w, h)
+        # Linears with their own A that read the same input (q, k, v of one attention) take
+        # their h and b_dec from one multi-target prep when grouped (SharedInputPrep).
+        compiling = torch.compiler.is_compiling()
+        got = None
+        if self.prep_group is not None and self.rows is None and not compiling:
+            got = self.prep_group.prep(self, x3, ids, w)
+        if got is not None:
+            h, b_dec = got
+        else:
+            share = self.rows is not None and not compiling
+            h = self._shared_h(x3, ids, w) if share else None
+            fresh = h is None
+            words = self.bank.words
+            h_new, b_dec = torch.ops.lithe_b200.lora_prep(x3, words, words, self._va, self._vb, self.bank.n_slots, ids,
+                                                          w, d_out, self._lut, self.scaling, fresh)
+            if fresh:
+                h = h_new
+                if share:
+                    self._store_h(x3, ids, w, h)
         out = torch.ops.lithe_b200.lora_gemm(x3.view(bsz * m, d_in), self.base.weight, self.base.bias, h, b_dec, m)
         return out.view(*x.shape[:-1], d_out)
 
@@ -306,7 +417,10 @@ def wrap_packed(model: nn.Module, bank: PackedBank, key_format: str = "diffusers
         full = r0 == 0 and r1 == lay.shapes_b[lay.index(name)][0]
         return PackedLoRALinear(lin, bank, name, rank, s, rows=None if full else (r0, r1), fused_gemm=fused_gemm)
 
-    return wrap_linears(model, want, factory)
+    wrapped = wrap_linears(model, want, factory)
+    if fused_gemm:
+        group_shared_inputs(wrapped)
+    return wrapped
 
 
 def pools_on(device, dtype=torch.float32):

@@ -1,0 +1,68 @@
+"""Shared-input prep groups (SharedInputPrep) on the fused-GEMM path.
+
+The q / k / v linears of an attention block read one input; grouped, the first of them to run
+computes all three h and b_dec with one lithe_lora_prep_multi.  The model's output must be
+bit-identical to the same model with every linear preparing its own (lithe_lora_prep), every
+group must hand all its results over (none left pending after the forward), and a member called
+on another input computes its own."""
+import pytest
+import torch
+
+from lithe_b200.flux_model import FluxConfig, FluxShapedTransformer, lora_targets
+from lithe_b200.kernels import PackedBank, PackedLayout, wrap_packed
+
+pytestmark = pytest.mark.gpu
+
+
+def _model(seed):
+    torch.manual_seed(seed)
+    cfg = FluxConfig.tiny()
+    model = FluxShapedTransformer(cfg).cuda().bfloat16().eval()
+    targets = lora_targets(model)
+    lay = PackedLayout.from_modules([{"name": n, "shape_a": [16, m.in_features], "shape_b": [m.out_features, 16]}
+                                     for n, m in targets])
+    bank = PackedBank(lay, 8, "cuda")
+    bank.fill_random(seed=seed + 1)
+    wrapped = wrap_packed(model, bank, scaling=20.0, fused_gemm=True)
+    ids = torch.tensor([2, 7], dtype=torch.int32, device="cuda")
+    for m in wrapped.values():
+        m.assign = ids
+    lat = torch.randn(2, 256, cfg.in_channels, device="cuda").bfloat16()
+    txt = torch.randn(2, 256, cfg.text_dim, device="cuda").bfloat16()
+    pooled = torch.randn(2, cfg.pooled_dim, device="cuda").bfloat16()
+    return model, wrapped, (lat, txt, pooled, torch.full((2,), 0.5, device="cuda"))
+
+
+def test_grouped_forward_equals_per_linear_prep():
+    model, wrapped, args = _model(5)
+    groups = {id(m.prep_group): m.prep_group for m in wrapped.values() if m.prep_group is not None}
+    assert len(groups) == 6
+    with torch.no_grad():
+        grouped = model(*args)
+        assert all(g._key is None and not g._ready for g in groups.values())      # every result handed over
+        for m in wrapped.values():
+            m.prep_group = None
+        alone = model(*args)
+    assert torch.equal(grouped, alone)
+
+
+def test_member_on_another_input_computes_its_own():
+    model, wrapped, args = _model(6)
+    q = wrapped["transformer_blocks.0.attn.to_q"]
+    k = wrapped["transformer_blocks.0.attn.to_k"]
+    x = torch.randn(2, 256, q.base.in_features, device="cuda").bfloat16()
+    x2 = x.clone()
+    g = q.prep_group
+    with torch.no_grad():
+        want_k = k(x2)
+        yq = q(x)                   # computes q, k, v for x
+        assert len(g._ready) == 2
+        got_k = k(x2)               # another tensor: not taken from the group (k prepares its own)
+        got_k_same = k(x)           # the same tensor: taken from the group
+        assert len(g._ready) == 1
+        again_k = k(x)              # called again on it: k prepares its own
+        for m in wrapped.values():
+            m.prep_group = None
+        want_q = q(x)
+    assert torch.equal(got_k, want_k) and torch.equal(got_k_same, want_k) and torch.equal(again_k, want_k)
+    assert torch.equal(yq, want_q)

@@ -341,3 +341,40 @@ def test_prep_split_choice():
     assert not prep_split_pays(14, 4096, 3072, 148)
     assert not prep_split_pays(14, 4608, 15360, 148) and not prep_split_pays(14, 512, 12288, 148)
     assert not prep_split_pays(4, 4096, 3072, 148) and not prep_split_pays(0, 4096, 3072, 148)
+
+
+def test_shared_input_groups_on_the_flux_names():
+    """wrap_packed(fused_gemm=True) groups the linears that read one input: per double block the
+    image and the text stream's q / k / v, per single block its q / k / v (its proj_mlp too when
+    it is a target).  Kohya split targets, other banks and other widths do not join."""
+    import pytest as _pytest
+
+    from lithe_b200.flux_model import FluxConfig, FluxShapedTransformer, lora_targets
+    from lithe_b200.kernels import PackedBank, PackedLayout, PackedLoRALinear, SharedInputPrep, wrap_packed
+    model = FluxShapedTransformer(FluxConfig.tiny())
+    targets = lora_targets(model)
+    lay = PackedLayout.from_modules([{"name": n, "shape_a": [16, m.in_features], "shape_b": [m.out_features, 16]}
+                                     for n, m in targets])
+    wrapped = wrap_packed(model, PackedBank(lay, 2, "cpu"), fused_gemm=True)
+    groups = {id(m.prep_group): m.prep_group for m in wrapped.values() if m.prep_group is not None}
+    names = {tuple(sorted(n for n, m in wrapped.items() if m.prep_group is g)) for g in groups.values()}
+    assert ("transformer_blocks.0.attn.to_k", "transformer_blocks.0.attn.to_q",
+            "transformer_blocks.0.attn.to_v") in names
+    assert ("transformer_blocks.1.attn.add_k_proj", "transformer_blocks.1.attn.add_q_proj",
+            "transformer_blocks.1.attn.add_v_proj") in names
+    assert ("single_transformer_blocks.0.attn.to_k", "single_transformer_blocks.0.attn.to_q",
+            "single_transformer_blocks.0.attn.to_v") in names
+    assert len(groups) == 6 and all(len(g.members) == 3 for g in groups.values())
+    assert wrapped["transformer_blocks.0.attn.to_out.0"].prep_group is None
+    # without the fused-GEMM path nothing is grouped
+    model2 = FluxShapedTransformer(FluxConfig.tiny())
+    assert all(m.prep_group is None for m in wrap_packed(model2, PackedBank(lay, 2, "cpu")).values())
+    # members must share a bank
+    other = PackedBank(lay, 2, "cpu")
+    q = wrapped["transformer_blocks.0.attn.to_q"]
+    lin = torch.nn.Linear(q.base.in_features, q.base.out_features)
+    stray = PackedLoRALinear(lin, other, "transformer_blocks.0.attn.to_q", 16, 1.0, fused_gemm=True)
+    with _pytest.raises(ValueError):
+        SharedInputPrep([PackedLoRALinear(lin, q.bank, "transformer_blocks.0.attn.to_q", 16, 1.0), stray])
+    with _pytest.raises(ValueError):
+        SharedInputPrep([stray])
