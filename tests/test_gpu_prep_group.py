@@ -50,19 +50,21 @@ def test_member_on_another_input_computes_its_own():
     model, wrapped, args = _model(6)
     q = wrapped["transformer_blocks.0.attn.to_q"]
     k = wrapped["transformer_blocks.0.attn.to_k"]
+    g = q.prep_group
     x = torch.randn(2, 256, q.base.in_features, device="cuda").bfloat16()
     x2 = x.clone()
-    g = q.prep_group
     with torch.no_grad():
-        want_k = k(x2)
-        yq = q(x)                   # computes q, k, v for x
-        assert len(g._ready) == 2
-        got_k = k(x2)               # another tensor: not taken from the group (k prepares its own)
-        got_k_same = k(x)           # the same tensor: taken from the group
-        assert len(g._ready) == 1
-        again_k = k(x)              # called again on it: k prepares its own
-        for m in wrapped.values():
+        for m in g.members:
             m.prep_group = None
-        want_q = q(x)
-    assert torch.equal(got_k, want_k) and torch.equal(got_k_same, want_k) and torch.equal(again_k, want_k)
+        want_q, want_k = q(x), k(x)            # each linear preparing its own
+        for m in g.members:
+            m.prep_group = g
+        yq = q(x)                   # prepares q, k and v for x
+        assert len(g._ready) == 2
+        got_k2 = k(x2)              # another input while x's results are pending: k prepares its own
+        assert len(g._ready) == 2
+        got_k = k(x)                # taken from the group
+        assert len(g._ready) == 1
+        again_k = k(x)              # called again on the same input: k prepares its own
     assert torch.equal(yq, want_q)
+    assert torch.equal(got_k, want_k) and torch.equal(got_k2, want_k) and torch.equal(again_k, want_k)
