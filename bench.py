@@ -148,8 +148,10 @@ class ClockSampler:
         sm = [num(r[0]) for r in rows if num(r[0]) is not None]
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         reasons = sorted({n for r in rows for n, v in zip(names, r[4:8]) if v.lower() == "active"})
+        pw = [num(r[2]) for r in rows if num(r[2]) is not None]
         return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": num(rows[0][1]),
-                "power_w_max": max((num(r[2]) or 0.0) for r in rows), "reasons": reasons, "samples": len(rows)}
+                "power_w_max": max(pw) if pw else None, "power_w_median": statistics.median(pw) if pw else None,
+                "reasons": reasons, "samples": len(rows)}
 
 
 def measured_peaks():
@@ -1211,6 +1213,94 @@ def run_lora_gemm(args):
         dist.destroy_process_group()
 
 
+def run_gemm_sustained(args):
+    """The base GEMM of the fused path under the sustained power cap: cuBLAS
+    (torch.nn.functional.linear), lithe_lora_gemm without LoRA, and lithe_lora_gemm with the
+    fused rank-16 expand, each back to back for --seconds at 57344 x 3072 x 3072 (the img_sq
+    linears of a 1024^2 B=14 forward), in ABBA order, with nvidia-smi sampled every 100 ms
+    during every pass: TFLOP/s, median SM clock, TFLOP/s per GHz and TFLOP per joule (at the
+    median power draw)."""
+    import torch.nn.functional as F
+    from lithe_b200.kernels import _launch as _lk
+
+    world, rank, local = dist_env()
+    metric = "sustained TFLOP/s of lithe_lora_gemm with the fused expand, 57344 x 3072 x 3072, power-capped"
+    if args.impl == "reference":
+        if rank == 0:
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no fused base-GEMM path"}))
+        return
+    init_dist(world, local)
+    dev = torch.device("cuda", local)
+    rows, n, k, rps = 57344, 3072, 3072, 4096
+    g = torch.Generator(device=dev)
+    g.manual_seed(21 + rank)
+    x = torch.randn(rows, k, device=dev, generator=g).bfloat16()
+    w = (torch.randn(n, k, device=dev, generator=g) * 0.02).bfloat16()
+    b = torch.randn(n, device=dev, generator=g).bfloat16()
+    h = torch.randn(rows, 16, device=dev, generator=g).bfloat16()
+    bd = (torch.randn(rows // rps, n, 16, device=dev, generator=g) * 0.1).bfloat16()
+    out = torch.empty(rows, n, device=dev, dtype=torch.bfloat16)
+    fs = {"cublas": lambda: F.linear(x, w, b), "lithe_plain": lambda: _lk.lora_gemm_(x, w, b, out),
+          "lithe_fused": lambda: _lk.lora_gemm_(x, w, b, out, h=h, b_dec=bd, rows_per_sample=rps)}
+    flops = {"cublas": 2.0 * rows * n * k, "lithe_plain": 2.0 * rows * n * k,
+             "lithe_fused": 2.0 * rows * n * (k + 16)}
+    order = ["cublas", "lithe_plain", "lithe_fused", "lithe_fused", "lithe_plain", "cublas"]
+    passes = {name: [] for name in fs}
+    with torch.no_grad():
+        for name in order:
+            f = fs[name]
+            for _ in range(max(3, args.warmup)):
+                f()
+            torch.cuda.synchronize(dev)
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            with ClockSampler(local) as cs:
+                e0.record()
+                iters, t_end = 0, time.time() + args.seconds
+                while time.time() < t_end:
+                    for _ in range(10):
+                        f()
+                    iters += 10
+                e1.record()
+                torch.cuda.synchronize(dev)
+            secs = e0.elapsed_time(e1) / 1000.0
+            clk = cs.summary()
+            tf = iters * flops[name] / secs / 1e12
+            rec = {"iters": iters, "seconds": round(secs, 3), "tflops": round(tf, 1), "clocks": clk}
+            if clk.get("sm_mhz"):
+                rec["tflops_per_ghz"] = round(tf / (clk["sm_mhz"] / 1000.0), 1)
+            if clk.get("power_w_median"):
+                rec["tflop_per_joule"] = round(tf / clk["power_w_median"], 3)
+            passes[name].append(rec)
+    summary = {name: {"tflops": round(statistics.mean(p["tflops"] for p in ps), 1),
+                      "sm_mhz": [p["clocks"].get("sm_mhz") for p in ps],
+                      "tflops_per_ghz": [p.get("tflops_per_ghz") for p in ps],
+                      "tflop_per_joule": [p.get("tflop_per_joule") for p in ps]} for name, ps in passes.items()}
+    value = summary["lithe_fused"]["tflops"]
+    peaks = {}
+    try:
+        peaks = json.loads((ROOT / "MEASURED_PEAKS.json").read_text())
+    except (OSError, ValueError):
+        pass
+    peak = peaks.get("bf16_tflops_sustained", 1400.0)
+    if rank == 0:
+        print(json.dumps({
+            "metric": metric, "value": value, "unit": "TFLOP/s", "n_gpus": world, "steps": len(order),
+            "warmup": args.warmup, "ms_per_step": None, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16 (fp32 accumulate)", "data": "synthetic N(0,1) bf16 operands",
+            "config": {"workload": args.workload, "rows": rows, "n": n, "k": k, "rows_per_sample": rps,
+                       "seconds_per_pass": args.seconds, "order": order},
+            "roofline": {"bound": "tensor", "achieved": value, "peak": peak, "unit": "TFLOP/s", "frac": value / peak,
+                         "peak_source": "bf16_tflops_sustained (cuBLAS 8192^3 back to back for 4 s) of " +
+                                        ("measured" if "bf16_tflops_sustained" in peaks else "fallback"),
+                         "traffic": None},
+            "summary": summary, "passes": passes, "cpu_baseline": None, "e2e": None,
+            "gpu_launches": sum(p["iters"] for name in ("lithe_plain", "lithe_fused") for p in passes[name]),
+            "device_errors": _lk.device_errors(dev)}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+        dist.destroy_process_group()
+
+
 def wrap_linears_any(model, names, table):
     """Point model.<name> at table[name] (swaps between plain, packed and dense wrappers)."""
     for n in names:
@@ -1227,9 +1317,12 @@ def main():
     ap.add_argument("--impl", choices=["lithe", "reference"], default="lithe")
     ap.add_argument("--workload", choices=["flux_sweep_b14", "decode_flux342", "decode_kohya304", "denoise_512",
                                            "denoise_256_b96", "denoise_1024", "denoise_512_kohya",
-                                           "denoise_1024_kohya", "hotswap_kohya304", "lora_gemm_flux"],
+                                           "denoise_1024_kohya", "hotswap_kohya304", "lora_gemm_flux",
+                                           "gemm_sustained"],
                     default="flux_sweep_b14", help="flux_sweep_b14: fused decode+SGMV (default); decode_*: "
                     "standalone packed decode of 14 resident adapters per launch")
+    ap.add_argument("--seconds", type=float, default=3.0,
+                    help="gemm_sustained: seconds of back-to-back calls per pass")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
                     help="CPU-baseline sample length of the decode and hot-swap workloads (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
@@ -1264,6 +1357,8 @@ def main():
         run_denoise(args)
     elif args.workload == "hotswap_kohya304":
         run_hotswap(args)
+    elif args.workload == "gemm_sustained":
+        run_gemm_sustained(args)
     elif args.workload == "lora_gemm_flux":
         run_lora_gemm(args)
     elif args.impl == "reference":
