@@ -161,7 +161,7 @@ class SharedInputPrep:
                    and ((w is None and m.weights is None) or (w is not None and m._weights(x3) is w))]
         if layer not in members or len(members) < 2:
             return None
-        words = layer.bank.words
+        words = [layer.bank.words] * len(members)
         outs = torch.ops.lithe_b200.lora_prep_multi(
             x3, words, words, [v for m in members for v in m._va], [v for m in members for v in m._vb],
             layer.bank.n_slots, ids, w, [m.base.out_features for m in members], layer._lut,
@@ -180,23 +180,32 @@ _SHARED_INPUT_SETS = (("attn.to_q", ("attn.to_q", "attn.to_k", "attn.to_v", "pro
                       ("attn.add_q_proj", ("attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj")))
 
 
+def shared_input_sets(paths: Iterable[str]) -> List[List[str]]:
+    """The groups of ``paths`` (diffusers names of a FLUX-shaped transformer) that read one input
+    tensor, per _SHARED_INPUT_SETS, each with at least two members."""
+    have = set(paths)
+    sets = []
+    for path in sorted(have):
+        for lead, names in _SHARED_INPUT_SETS:
+            if path.endswith(lead):
+                block = path[: -len(lead)]
+                members = [block + n for n in names if block + n in have]
+                if len(members) >= 2:
+                    sets.append(members)
+    return sets
+
+
 def group_shared_inputs(modules: Dict[str, nn.Module]) -> List[SharedInputPrep]:
     """Group the wrapped linears of ``modules`` ({diffusers path: layer}) that read the same
     input (see _SHARED_INPUT_SETS; a double block's proj_mlp does not exist, so its q / k / v
     form the group) into SharedInputPrep objects.  Only whole-module PackedLoRALinear layers
     of one bank join; Kohya split targets already share one h per fused module."""
     groups = []
-    for path in modules:
-        for lead, names in _SHARED_INPUT_SETS:
-            if not path.endswith(lead):
-                continue
-            block = path[: -len(lead)]
-            members = [modules[block + n] for n in names if block + n in modules]
-            if (len(members) >= 2 and all(isinstance(m, PackedLoRALinear) and m.rows is None and m.rank == 16
-                                          and m.bank is members[0].bank
-                                          and m.base.in_features == members[0].base.in_features
-                                          and m.prep_group is None for m in members)):
-                groups.append(SharedInputPrep(members))
+    for names in shared_input_sets(modules):
+        members = [modules[n] for n in names]
+        if all(isinstance(m, PackedLoRALinear) and m.rows is None and m.rank == 16 and m.bank is members[0].bank
+               and m.base.in_features == members[0].base.in_features and m.prep_group is None for m in members):
+            groups.append(SharedInputPrep(members))
     return groups
 
 

@@ -17,8 +17,9 @@ ABI as a flat list of 2 * levels * 10 floats.
   lora_prep(x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, d_out, lut, scaling,
             compute_h) -> (h, b_dec)                     lithe_lora_prep (h is (0, 16) when
                                                          compute_h is False)
-  lora_prep_multi(x, bank_a, bank_b, views_a, views_b, n_slots, ids, weights, d_outs, lut,
-                  scalings) -> [h...] + [b_dec...]      lithe_lora_prep_multi (linears sharing x)
+  lora_prep_multi(x, banks_a, banks_b, views_a, views_b, n_slots, ids, weights, d_outs, lut,
+                  scalings) -> [h...] + [b_dec...]      lithe_lora_prep_multi (linears sharing x;
+                                                         one bank tensor pair per target)
   lora_gemm(x, weight, bias, h, b_dec, rows_per_sample) -> out       lithe_lora_gemm
   decode_packed(words, n_blocks, levels, sides, lut, fp32) -> out    lithe_decode_packed
 """
@@ -81,24 +82,25 @@ def _lora_prep_fake(x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, d_
 
 
 @torch.library.custom_op(f"{_NS}::lora_prep_multi", mutates_args=(), device_types="cuda")
-def lora_prep_multi(x: torch.Tensor, bank_a: torch.Tensor, bank_b: torch.Tensor, views_a: List[int],
+def lora_prep_multi(x: torch.Tensor, banks_a: List[torch.Tensor], banks_b: List[torch.Tensor], views_a: List[int],
                     views_b: List[int], n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor],
                     d_outs: List[int], lut: List[float], scalings: List[float]) -> List[torch.Tensor]:
-    """lithe_lora_prep_multi for len(d_outs) linears reading x: views_a / views_b hold their
-    index views back to back (five integers each); returns [h_0 .. h_n-1, b_dec_0 .. b_dec_n-1]."""
+    """lithe_lora_prep_multi for len(d_outs) linears reading x: target t's index views are
+    banks_a[t] / banks_b[t] with the five integers views_a[5t:5t+5] / views_b[5t:5t+5];
+    returns [h_0 .. h_n-1, b_dec_0 .. b_dec_n-1]."""
     bsz, m, _ = x.shape
     n = len(d_outs)
     hs = [torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device) for _ in range(n)]
     bds = [torch.empty(bsz, d, 16, dtype=torch.bfloat16, device=x.device) for d in d_outs]
-    _launch.lora_prep_multi_(x, views_a=[_view(bank_a, views_a[5 * t:5 * t + 5]) for t in range(n)],
-                             views_b=[_view(bank_b, views_b[5 * t:5 * t + 5]) for t in range(n)], d_outs=d_outs,
+    _launch.lora_prep_multi_(x, views_a=[_view(banks_a[t], views_a[5 * t:5 * t + 5]) for t in range(n)],
+                             views_b=[_view(banks_b[t], views_b[5 * t:5 * t + 5]) for t in range(n)], d_outs=d_outs,
                              n_slots=n_slots, ids=ids, weights=weights, lut=_launch.lut_from_list(lut),
                              scalings=scalings, hs=hs, b_decs=bds)
     return hs + bds
 
 
 @lora_prep_multi.register_fake
-def _lora_prep_multi_fake(x, bank_a, bank_b, views_a, views_b, n_slots, ids, weights, d_outs, lut, scalings):
+def _lora_prep_multi_fake(x, banks_a, banks_b, views_a, views_b, n_slots, ids, weights, d_outs, lut, scalings):
     bsz, m, _ = x.shape
     return ([x.new_empty(bsz * m, 16, dtype=torch.bfloat16) for _ in d_outs] +
             [x.new_empty(bsz, d, 16, dtype=torch.bfloat16) for d in d_outs])

@@ -23,7 +23,7 @@ from . import codebook as cb
 from . import quant
 from .fileio import LitheAdapter
 from .kernels import _launch, ops
-from .kernels.layers import FUSED_GEMM_MAX_K, _inference_only
+from .kernels.layers import FUSED_GEMM_MAX_K, _inference_only, _InputKey, shared_input_sets
 
 Route = Sequence[Tuple[int, float]]
 
@@ -120,6 +120,8 @@ class MultiAdapterLinear(nn.Module):
         self.scales: List[float] = []
         self.lut = cb.kernel_lut(pool_a, pool_b)      # computed once from the (host) pools
         self._lut = [float(v) for v in self.lut.reshape(-1)]
+        # set by _RoutePrepGroup: siblings that read the same input share one prep launch
+        self.prep_group: Optional["_RoutePrepGroup"] = None
 
     def add_adapter(self, idx_a: np.ndarray, idx_b: np.ndarray, scale: float) -> None:
         dev = self.idx_a.device
@@ -142,9 +144,15 @@ class MultiAdapterLinear(nn.Module):
                             w: torch.Tensor) -> torch.Tensor:
         bsz, m, d_in = xs.shape
         d_out = self.base.out_features
-        va, vb = self._view_params()
-        h, b_dec = torch.ops.lithe_b200.lora_prep(xs, self.idx_a, self.idx_b, va, vb, self.idx_a.shape[0], slot_ids, w,
-                                                  d_out, self._lut, 1.0, True)
+        got = None
+        if self.prep_group is not None and not torch.compiler.is_compiling():
+            got = self.prep_group.prep(self, x, xs, slot_ids, w)
+        if got is not None:
+            h, b_dec = got
+        else:
+            va, vb = self._view_params()
+            h, b_dec = torch.ops.lithe_b200.lora_prep(xs, self.idx_a, self.idx_b, va, vb, self.idx_a.shape[0],
+                                                      slot_ids, w, d_out, self._lut, 1.0, True)
         out = torch.ops.lithe_b200.lora_gemm(xs.view(bsz * m, d_in), self.base.weight, self.base.bias, h, b_dec, m)
         return out.view(*x.shape[:-1], d_out)
 
@@ -180,6 +188,50 @@ class MultiAdapterLinear(nn.Module):
         return out
 
 
+class _RoutePrepGroup:
+    """MultiAdapterLinear siblings that read one input (the q, k and v projections of an
+    attention block) on the fused-GEMM path: the first called on an input runs one
+    lithe_lora_prep_multi for all of them -- the input read once -- and hands the others their
+    h and b_dec.  The rules of kernels.SharedInputPrep, keyed on the layer's input tensor and
+    the router's slot-id / weight column."""
+
+    def __init__(self, members: List["MultiAdapterLinear"]):
+        if not 2 <= len(members) <= 4:
+            raise ValueError(f"a shared-input group has 2 to 4 members, got {len(members)}")
+        self.members = list(members)
+        for m in self.members:
+            m.prep_group = self
+        self._key: Optional[_InputKey] = None
+        self._ready: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
+
+    def prep(self, layer: "MultiAdapterLinear", x: torch.Tensor, xs: torch.Tensor, ids: torch.Tensor,
+             w: torch.Tensor) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
+        if self._key is not None:
+            if self._key.matches(x, ids, w, None):
+                got = self._ready.pop(id(layer), None)
+                if not self._ready:
+                    self._key = None
+                return got
+            if self._key.alive():
+                return None
+        members = [m for m in self.members
+                   if m.fused_gemm and m.router is layer.router and m.scales == layer.scales and m._lut == layer._lut
+                   and m.idx_a.shape[0] == layer.idx_a.shape[0] and m.base.in_features == layer.base.in_features
+                   and m._gemm_ok(xs)]
+        if layer not in members or len(members) < 2:
+            return None
+        views = [m._view_params() for m in members]
+        outs = torch.ops.lithe_b200.lora_prep_multi(
+            xs, [m.idx_a for m in members], [m.idx_b for m in members], [v for va, _ in views for v in va],
+            [v for _, vb in views for v in vb], layer.idx_a.shape[0], ids, w, [m.base.out_features for m in members],
+            layer._lut, [1.0] * len(members))
+        n = len(members)
+        self._ready = {id(m): (outs[i], outs[n + i]) for i, m in enumerate(members) if m is not layer}
+        self._key = _InputKey(x, ids, w, None)
+        i = members.index(layer)
+        return outs[i], outs[n + i]
+
+
 def _shared_module_names(adapters: List[LitheAdapter]) -> List[str]:
     """Module names of the first adapter, after checking that every adapter covers the same
     set of modules (in any order) with the same rank."""
@@ -212,6 +264,7 @@ def attach_adapters(model: nn.Module, adapters: List[LitheAdapter], router: Opti
     scales = [float(ad.alpha) / ad.rank for ad in adapters]
     prefix = "transformer."
     layers: Dict[str, MultiAdapterLinear] = {}
+    by_path: Dict[str, MultiAdapterLinear] = {}
     for name in names:
         path = name[len(prefix):] if name.startswith(prefix) else name
         base = _modtree.linear_at(model, path)
@@ -220,6 +273,11 @@ def attach_adapters(model: nn.Module, adapters: List[LitheAdapter], router: Opti
         for ad, scale in zip(adapters, scales):
             layer.add_adapter(ad.indices[name]["A"], ad.indices[name]["B"], scale)
         layers[name] = _modtree.swap(model, path, layer)
+        by_path[path] = layer
+    if fused_gemm:
+        # q / k / v of each attention block read one input: one multi-target prep per triple
+        for group in shared_input_sets(by_path):
+            _RoutePrepGroup([by_path[p] for p in group])
     return router, layers
 
 

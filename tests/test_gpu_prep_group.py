@@ -68,3 +68,32 @@ def test_member_on_another_input_computes_its_own():
         again_k = k(x)              # called again on the same input: k prepares its own
     assert torch.equal(yq, want_q)
     assert torch.equal(got_k, want_k) and torch.equal(got_k2, want_k) and torch.equal(again_k, want_k)
+
+
+def test_attach_adapters_groups_qkv_on_the_fused_path():
+    """serve.attach_adapters(fused_gemm=True) groups the q / k / v MultiAdapterLinear layers of
+    each attention block; the routed forward is bit-identical to every layer preparing its own."""
+    from lithe_b200 import serve
+    from tests.helpers import random_adapter
+
+    torch.manual_seed(9)
+    cfg = FluxConfig.tiny()
+    model = FluxShapedTransformer(cfg).cuda().bfloat16().eval()
+    targets = lora_targets(model)
+    ads = [random_adapter([(n, m.in_features, m.out_features) for n, m in targets], rank=16, seed=30 + s)
+           for s in range(3)]
+    router, layers = serve.attach_adapters(model, ads, fused_gemm=True)
+    groups = {id(m.prep_group): m.prep_group for m in layers.values() if m.prep_group is not None}
+    assert len(groups) == 6 and all(len(g.members) == 3 for g in groups.values())
+    router.set([[(2, 1.0)], [(0, 0.5)]])
+    lat = torch.randn(2, 256, cfg.in_channels, device="cuda").bfloat16()
+    txt = torch.randn(2, 256, cfg.text_dim, device="cuda").bfloat16()
+    pooled = torch.randn(2, cfg.pooled_dim, device="cuda").bfloat16()
+    args = (lat, txt, pooled, torch.full((2,), 0.5, device="cuda"))
+    with torch.no_grad():
+        grouped = model(*args)
+        assert all(g._key is None and not g._ready for g in groups.values())
+        for m in layers.values():
+            m.prep_group = None
+        alone = model(*args)
+    assert torch.equal(grouped, alone)
