@@ -116,6 +116,19 @@ class _InputKey:
         return self._vals == (x3._version, ids._version, None if w is None else w._version, scaling)
 
 
+class _RouteKey:
+    """Identifies the routing a decoded B factor was made for: the slot-id tensor (identity and
+    version, through a weak reference) and the caller's tuple of what else it depends on (the
+    index bank's contents key, the group's members)."""
+
+    def __init__(self, ids, extra):
+        self._ref = weakref.ref(ids)
+        self._vals = (ids._version, extra)
+
+    def matches(self, ids, extra) -> bool:
+        return self._ref() is ids and self._vals == (ids._version, extra)
+
+
 class SharedInputPrep:
     """Fused-GEMM linears with their own adapter modules that read the same input tensor -- the
     q, k and v projections of one attention block.  The first member to run on an input
@@ -142,6 +155,9 @@ class SharedInputPrep:
             m.prep_group = self
         self._key: Optional[_InputKey] = None
         self._ready: Dict[int, Tuple[torch.Tensor, torch.Tensor]] = {}
+        # the members' decoded B factors for the last routing (reused while it is unchanged)
+        self._bdec_key: Optional[_RouteKey] = None
+        self._bdecs: List[torch.Tensor] = []
 
     def prep(self, layer: "PackedLoRALinear", x3: torch.Tensor, ids: torch.Tensor,
              w: Optional[torch.Tensor]) -> Optional[Tuple[torch.Tensor, torch.Tensor]]:
@@ -162,15 +178,21 @@ class SharedInputPrep:
         if layer not in members or len(members) < 2:
             return None
         words = [layer.bank.words] * len(members)
+        extra = (layer.bank.contents_key(), tuple(id(m) for m in members))
+        cached = self._bdec_key is not None and self._bdec_key.matches(ids, extra)
         outs = torch.ops.lithe_b200.lora_prep_multi(
             x3, words, words, [v for m in members for v in m._va], [v for m in members for v in m._vb],
             layer.bank.n_slots, ids, w, [m.base.out_features for m in members], layer._lut,
-            [m.scaling for m in members])
+            [m.scaling for m in members], not cached)
         n = len(members)
-        self._ready = {id(m): (outs[i], outs[n + i]) for i, m in enumerate(members) if m is not layer}
+        if not cached:
+            self._bdecs = outs[n:]
+            self._bdec_key = _RouteKey(ids, extra)
+        bds = self._bdecs
+        self._ready = {id(m): (outs[i], bds[i]) for i, m in enumerate(members) if m is not layer}
         self._key = _InputKey(x3, ids, w, None)
         i = members.index(layer)
-        return outs[i], outs[n + i]
+        return outs[i], bds[i]
 
 
 # Sibling linears of a FLUX-shaped (diffusers-named) transformer that read one input tensor:
@@ -251,6 +273,8 @@ class PackedLoRALinear(nn.Module):
         self._lut = bank.lut_list
         # set by SharedInputPrep: siblings that read the same input share one prep launch
         self.prep_group: Optional["SharedInputPrep"] = None
+        # (routing key, b_dec): the decoded B factor of the last routing on the fused-GEMM path
+        self._bdec_cache: Optional[Tuple[_RouteKey, torch.Tensor]] = None
 
     def _gemm_ok(self, x3: torch.Tensor) -> bool:
         w = self.base.weight
@@ -319,8 +343,20 @@ class PackedLoRALinear(nn.Module):
             h = self._shared_h(x3, ids, w) if share else None
             fresh = h is None
             words = self.bank.words
-            h_new, b_dec = torch.ops.lithe_b200.lora_prep(x3, words, words, self._va, self._vb, self.bank.n_slots, ids,
-                                                          w, d_out, self._lut, self.scaling, fresh)
+            # B factor of this routing: decoded once and kept while the routing and the bank's
+            # contents are unchanged (a denoise loop's steps); traced graphs decode every call
+            b_dec = None
+            bank_key = self.bank.contents_key()
+            if not compiling and self._bdec_cache is not None and self._bdec_cache[0].matches(ids, bank_key):
+                b_dec = self._bdec_cache[1]
+            if b_dec is None:
+                h_new, b_dec = torch.ops.lithe_b200.lora_prep(x3, words, words, self._va, self._vb, self.bank.n_slots,
+                                                              ids, w, d_out, self._lut, self.scaling, fresh)
+                if not compiling:
+                    self._bdec_cache = (_RouteKey(ids, bank_key), b_dec)
+            elif fresh:
+                h_new = torch.ops.lithe_b200.lora_prep_h(x3, words, words, self._va, self._vb, self.bank.n_slots, ids,
+                                                         w, d_out, self._lut, self.scaling)
             if fresh:
                 h = h_new
                 if share:

@@ -17,8 +17,11 @@ ABI as a flat list of 2 * levels * 10 floats.
   lora_prep(x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, d_out, lut, scaling,
             compute_h) -> (h, b_dec)                     lithe_lora_prep (h is (0, 16) when
                                                          compute_h is False)
+  lora_prep_h(x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, d_out, lut,
+              scaling) -> h                              lithe_lora_prep with b_dec NULL (h only)
   lora_prep_multi(x, banks_a, banks_b, views_a, views_b, n_slots, ids, weights, d_outs, lut,
-                  scalings) -> [h...] + [b_dec...]      lithe_lora_prep_multi (linears sharing x;
+                  scalings, compute_bdec) -> [h...] + [b_dec...]
+                                                         lithe_lora_prep_multi (linears sharing x;
                                                          one bank tensor pair per target)
   lora_gemm(x, weight, bias, h, b_dec, rows_per_sample) -> out       lithe_lora_gemm
   decode_packed(words, n_blocks, levels, sides, lut, fp32) -> out    lithe_decode_packed
@@ -81,29 +84,51 @@ def _lora_prep_fake(x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, d_
     return h, x.new_empty(bsz, d_out, 16, dtype=torch.bfloat16)
 
 
+@torch.library.custom_op(f"{_NS}::lora_prep_h", mutates_args=(), device_types="cuda")
+def lora_prep_h(x: torch.Tensor, bank_a: torch.Tensor, bank_b: torch.Tensor, view_a: List[int], view_b: List[int],
+                n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor], d_out: int, lut: List[float],
+                scaling: float) -> torch.Tensor:
+    """The h of lithe_lora_prep alone (b_dec NULL): for a layer whose decoded B factor for this
+    routing is already at hand."""
+    bsz, m, _ = x.shape
+    h = torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device)
+    _launch.lora_prep_(x, view_a=_view(bank_a, view_a), view_b=_view(bank_b, view_b), n_slots=n_slots, ids=ids,
+                       weights=weights, d_out=d_out, lut=_launch.lut_from_list(lut), scaling=scaling, h=h, b_dec=None)
+    return h
+
+
+@lora_prep_h.register_fake
+def _lora_prep_h_fake(x, bank_a, bank_b, view_a, view_b, n_slots, ids, weights, d_out, lut, scaling):
+    bsz, m, _ = x.shape
+    return x.new_empty(bsz * m, 16, dtype=torch.bfloat16)
+
+
 @torch.library.custom_op(f"{_NS}::lora_prep_multi", mutates_args=(), device_types="cuda")
 def lora_prep_multi(x: torch.Tensor, banks_a: List[torch.Tensor], banks_b: List[torch.Tensor], views_a: List[int],
                     views_b: List[int], n_slots: int, ids: torch.Tensor, weights: Optional[torch.Tensor],
-                    d_outs: List[int], lut: List[float], scalings: List[float]) -> List[torch.Tensor]:
+                    d_outs: List[int], lut: List[float], scalings: List[float],
+                    compute_bdec: bool) -> List[torch.Tensor]:
     """lithe_lora_prep_multi for len(d_outs) linears reading x: target t's index views are
     banks_a[t] / banks_b[t] with the five integers views_a[5t:5t+5] / views_b[5t:5t+5];
-    returns [h_0 .. h_n-1, b_dec_0 .. b_dec_n-1]."""
+    returns [h_0 .. h_n-1, b_dec_0 .. b_dec_n-1] (each b_dec (0, d_out, 16) when compute_bdec is
+    False)."""
     bsz, m, _ = x.shape
     n = len(d_outs)
     hs = [torch.empty(bsz * m, 16, dtype=torch.bfloat16, device=x.device) for _ in range(n)]
-    bds = [torch.empty(bsz, d, 16, dtype=torch.bfloat16, device=x.device) for d in d_outs]
+    bds = [torch.empty(bsz if compute_bdec else 0, d, 16, dtype=torch.bfloat16, device=x.device) for d in d_outs]
     _launch.lora_prep_multi_(x, views_a=[_view(banks_a[t], views_a[5 * t:5 * t + 5]) for t in range(n)],
                              views_b=[_view(banks_b[t], views_b[5 * t:5 * t + 5]) for t in range(n)], d_outs=d_outs,
                              n_slots=n_slots, ids=ids, weights=weights, lut=_launch.lut_from_list(lut),
-                             scalings=scalings, hs=hs, b_decs=bds)
+                             scalings=scalings, hs=hs, b_decs=bds if compute_bdec else [None] * n)
     return hs + bds
 
 
 @lora_prep_multi.register_fake
-def _lora_prep_multi_fake(x, banks_a, banks_b, views_a, views_b, n_slots, ids, weights, d_outs, lut, scalings):
+def _lora_prep_multi_fake(x, banks_a, banks_b, views_a, views_b, n_slots, ids, weights, d_outs, lut, scalings,
+                          compute_bdec):
     bsz, m, _ = x.shape
     return ([x.new_empty(bsz * m, 16, dtype=torch.bfloat16) for _ in d_outs] +
-            [x.new_empty(bsz, d, 16, dtype=torch.bfloat16) for d in d_outs])
+            [x.new_empty(bsz if compute_bdec else 0, d, 16, dtype=torch.bfloat16) for d in d_outs])
 
 
 @torch.library.custom_op(f"{_NS}::lora_gemm", mutates_args=(), device_types="cuda")

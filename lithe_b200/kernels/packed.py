@@ -221,6 +221,7 @@ class PackedBank:
         self.device = torch.device(device)
         self.slot_stride = layout.num_words + (layout.num_words & 1)
         self.words = torch.zeros((n_slots, self.slot_stride), dtype=torch.int64, device=self.device)
+        self._kernel_writes = 0          # slot writes by the pack kernels (not seen by words._version)
         pa, pb = pools if pools is not None else cb.twin_pools()
         self.pool_a, self.pool_b = pa, pb
         self.lut = _lut(pa, pb, layout.num_levels)
@@ -230,6 +231,12 @@ class PackedBank:
     @property
     def n_slots(self) -> int:
         return int(self.words.shape[0])
+
+    def contents_key(self) -> Tuple[int, int]:
+        """Changes whenever a slot is written: by a torch op on ``words`` (its version counter)
+        or by the pack kernels (load_raw, load_raw_batch).  Layers key their cached decoded
+        B factors on it."""
+        return (self.words._version, self._kernel_writes)
 
     @property
     def slot_bytes(self) -> int:
@@ -278,6 +285,7 @@ class PackedBank:
             raise ValueError(f"payload has {raw.numel()} indices, the layout needs {self.layout.num_indices}")
         _launch.pack_raw_(raw, self.layout.segments_on(self.device), self.layout.num_levels,
                           self.words[slot, : self.layout.num_words], err)
+        self._kernel_writes += 1
 
     def load_raw_batch(self, slot_ids, raw: torch.Tensor, err: Optional[torch.Tensor] = None) -> None:
         """Pack n raw payloads already on the device ((n, num_indices) int16 rows, the stream
@@ -287,6 +295,7 @@ class PackedBank:
             raise ValueError(f"raw must be ({ids.numel()}, {self.layout.num_indices}) for these slots")
         _launch.pack_raw_batch_(raw, self.layout.segments_on(self.device), self.layout.num_levels, self.words, ids,
                                 self.layout.num_words, err)
+        self._kernel_writes += 1
 
     def fill_random(self, seed: int, slots: Optional[slice] = None) -> None:
         """Seeded uniform 9-bit indices in every slot: int64 random_() draws uniform words in

@@ -23,7 +23,7 @@ from . import codebook as cb
 from . import quant
 from .fileio import LitheAdapter
 from .kernels import _launch, ops
-from .kernels.layers import FUSED_GEMM_MAX_K, _inference_only, _InputKey, shared_input_sets
+from .kernels.layers import FUSED_GEMM_MAX_K, _inference_only, _InputKey, _RouteKey, shared_input_sets
 
 Route = Sequence[Tuple[int, float]]
 
@@ -122,6 +122,9 @@ class MultiAdapterLinear(nn.Module):
         self._lut = [float(v) for v in self.lut.reshape(-1)]
         # set by _RoutePrepGroup: siblings that read the same input share one prep launch
         self.prep_group: Optional["_RoutePrepGroup"] = None
+        # (routing key, b_dec): the decoded B factor of the last routing on the fused-GEMM path
+        self._bdec_cache: Optional[Tuple[_RouteKey, torch.Tensor]] = None
+        self._n_added = 0               # adapters added (part of that key)
 
     def add_adapter(self, idx_a: np.ndarray, idx_b: np.ndarray, scale: float) -> None:
         dev = self.idx_a.device
@@ -132,6 +135,7 @@ class MultiAdapterLinear(nn.Module):
         self.idx_a = torch.cat([self.idx_a, ia]).contiguous()
         self.idx_b = torch.cat([self.idx_b, ib]).contiguous()
         self.scales.append(float(scale))
+        self._n_added += 1
 
     def _gemm_ok(self, x3: torch.Tensor) -> bool:
         w, b = self.base.weight, self.base.bias
@@ -151,8 +155,19 @@ class MultiAdapterLinear(nn.Module):
             h, b_dec = got
         else:
             va, vb = self._view_params()
-            h, b_dec = torch.ops.lithe_b200.lora_prep(xs, self.idx_a, self.idx_b, va, vb, self.idx_a.shape[0],
-                                                      slot_ids, w, d_out, self._lut, 1.0, True)
+            # the B factors of this route column, decoded once while it and the banks are unchanged
+            bank_key = (self._n_added, self.idx_a._version, self.idx_b._version)
+            compiling = torch.compiler.is_compiling()
+            cache = self._bdec_cache
+            if not compiling and cache is not None and cache[0].matches(slot_ids, bank_key):
+                b_dec = cache[1]
+                h = torch.ops.lithe_b200.lora_prep_h(xs, self.idx_a, self.idx_b, va, vb, self.idx_a.shape[0], slot_ids,
+                                                     w, d_out, self._lut, 1.0)
+            else:
+                h, b_dec = torch.ops.lithe_b200.lora_prep(xs, self.idx_a, self.idx_b, va, vb, self.idx_a.shape[0],
+                                                          slot_ids, w, d_out, self._lut, 1.0, True)
+                if not compiling:
+                    self._bdec_cache = (_RouteKey(slot_ids, bank_key), b_dec)
         out = torch.ops.lithe_b200.lora_gemm(xs.view(bsz * m, d_in), self.base.weight, self.base.bias, h, b_dec, m)
         return out.view(*x.shape[:-1], d_out)
 
@@ -224,7 +239,7 @@ class _RoutePrepGroup:
         outs = torch.ops.lithe_b200.lora_prep_multi(
             xs, [m.idx_a for m in members], [m.idx_b for m in members], [v for va, _ in views for v in va],
             [v for _, vb in views for v in vb], layer.idx_a.shape[0], ids, w, [m.base.out_features for m in members],
-            layer._lut, [1.0] * len(members))
+            layer._lut, [1.0] * len(members), True)
         n = len(members)
         self._ready = {id(m): (outs[i], outs[n + i]) for i, m in enumerate(members) if m is not layer}
         self._key = _InputKey(x, ids, w, None)

@@ -97,3 +97,44 @@ def test_attach_adapters_groups_qkv_on_the_fused_path():
             m.prep_group = None
         alone = model(*args)
     assert torch.equal(grouped, alone)
+
+
+def test_decoded_b_factors_are_reused_while_routing_and_bank_are_unchanged():
+    """The fused-GEMM path decodes a layer's (or a group's) B factors once per routing: later
+    calls with the same slot-id tensor and unchanged bank take the cached b_dec and give the
+    same output bit for bit; a new routing, an in-place change of the slot ids, or a write to
+    the bank (torch op or pack kernel) decodes again."""
+    model, wrapped, args = _model(11)
+    q = wrapped["transformer_blocks.0.attn.to_q"]
+    o = wrapped["transformer_blocks.0.attn.to_out.0"]          # not in a group
+    g = q.prep_group
+    bank = q.bank
+    with torch.no_grad():
+        first = model(*args)
+        bd_solo, bd_group = o._bdec_cache[1], list(g._bdecs)
+        second = model(*args)
+        assert o._bdec_cache[1] is bd_solo and all(a is b for a, b in zip(g._bdecs, bd_group))
+        assert torch.equal(first, second)
+        # a new routing (another tensor) decodes again
+        ids2 = torch.tensor([7, 2], dtype=torch.int32, device="cuda")
+        for m in wrapped.values():
+            m.assign = ids2
+        routed2 = model(*args)
+        assert o._bdec_cache[1] is not bd_solo and not torch.equal(routed2, first)
+        # an in-place change of the slot ids decodes again
+        ids2.copy_(torch.tensor([2, 7], dtype=torch.int32))
+        back = model(*args)
+        assert torch.equal(back, first)
+        # a write to the bank through the pack kernel decodes again: slot 7 gets slot 2's payload
+        keep = o._bdec_cache[1]
+        raw = torch.randint(0, 512, (bank.layout.num_indices,), dtype=torch.int16, device="cuda")
+        bank.load_raw(7, raw)
+        after = model(*args)
+        assert o._bdec_cache[1] is not keep and not torch.equal(after, first)
+        # against a forward with nothing cached
+        for m in wrapped.values():
+            m._bdec_cache = None
+            if m.prep_group is not None:
+                m.prep_group._bdec_key = None
+        fresh = model(*args)
+    assert torch.equal(after, fresh)
