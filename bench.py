@@ -162,13 +162,37 @@ def measured_peaks():
     return FALLBACK_HBM_GBS, "fallback"
 
 
+def _code_only(text: str) -> str:
+    """C/C++ source without its comments, whitespace runs collapsed (string and character
+    literals kept as they are)."""
+    out, i, n = [], 0, len(text)
+    while i < n:
+        if text.startswith("//", i):
+            j = text.find("\n", i)
+            i = n if j < 0 else j
+        elif text.startswith("/*", i):
+            j = text.find("*/", i + 2)
+            i = n if j < 0 else j + 2
+            out.append(" ")
+        elif text[i] in "\"'":
+            q, j = text[i], i + 1
+            while j < n and text[j] != q:
+                j += 2 if text[j] == "\\" else 1
+            out.append(text[i:j + 1])
+            i = j + 1
+        else:
+            out.append(text[i])
+            i += 1
+    return " ".join("".join(out).split())
+
+
 def kernel_source_digest() -> str:
-    """SHA-256 of the sources the fused SGMV kernel is built from (the recorded DRAM traffic is
-    valid only for the kernel it was captured on)."""
+    """SHA-256 of the code (comments and whitespace aside) the fused SGMV kernel is built from:
+    the recorded DRAM traffic is valid only for the kernel it was captured on."""
     import hashlib
     h = hashlib.sha256()
     for name in ("sgmv_index.cu", "device_common.cuh", "host_common.cu"):
-        h.update((ROOT / "lithe_b200" / "csrc" / name).read_bytes())
+        h.update(_code_only((ROOT / "lithe_b200" / "csrc" / name).read_text()).encode())
     return h.hexdigest()
 
 

@@ -37,6 +37,16 @@
 // columns repeated 4 times, so delta = h . B^T is 2 mma.m16n8k16 (n = 16 logical
 // columns, k = 16 ranks) and each thread adds its 2 results to 8 output values per row.
 // The stage is released as soon as the tile is in registers; the stores need no proxy fence.
+//
+// Shrink-only forms (the prep of lithe_lora_gemm's fused expand; SgmvParams::h_out set):
+//   lithe_lora_prep      x tiles only, h = bf16(w . s . x . A^T) stored after the shrink.
+//   lithe_lora_prep_ws   the same with the CTAs taking equal runs of the (unit, x stage)
+//                        sequence (SgmvParams::split): a unit may be shared by neighbouring
+//                        CTAs, each storing its fp32 partial h in a workspace that the B-decode
+//                        launch after it adds up in CTA order (split_combine).
+//   lithe_lora_prep_multi  kT (<= 4) linears reading the same x, staged form: their decoded A
+//                        chunks come from a workspace (prep_multi_decode_kernel) next to each
+//                        x tile, and the consumers accumulate kT h's from one read of x.
 #include <mutex>
 
 #include "device_common.cuh"
