@@ -378,3 +378,14 @@ def test_shared_input_groups_on_the_flux_names():
         SharedInputPrep([PackedLoRALinear(lin, q.bank, "transformer_blocks.0.attn.to_q", 16, 1.0), stray])
     with _pytest.raises(ValueError):
         SharedInputPrep([stray])
+
+
+def test_traffic_digest_ignores_comments_only():
+    """The recorded DRAM traffic is keyed on the kernel's code: comments and whitespace do not
+    change the digest, code does; string and character literals are kept verbatim."""
+    import bench
+    a = 'int f(int x) {  // note\n  return x + 1; /* block */ }\nconst char* s = "a//b/*c*/";\n'
+    b = 'int f(int x) {\n\n    return x + 1;   }\nconst char* s = "a//b/*c*/";  // other\n'
+    c = 'int f(int x) { return x + 2; }\nconst char* s = "a//b/*c*/";\n'
+    assert bench._code_only(a) == bench._code_only(b) != bench._code_only(c)
+    assert '"a//b/*c*/"' in bench._code_only(a)
