@@ -137,8 +137,10 @@ class SharedInputPrep:
     each member's own lithe_lora_prep.  A member called on another input while results for a
     live input are pending, called again on an input it already took, on the cuBLAS path, or
     under torch.compile (the hand-over keys on tensor identity, which a traced graph does not
-    have), computes its own.  Pending results for an input that has been freed are dropped.  Members must share one ``assign``
-    tensor (int32, on the device) for the hand-over to apply."""
+    have), computes its own.  Pending results for an input that has been freed are dropped.
+    Members must share one ``assign`` tensor (int32, on the device) for the hand-over to
+    apply.  The members' decoded B factors are kept for the last routing (see
+    PackedLoRALinear's B-factor cache)."""
 
     def __init__(self, members: Iterable["PackedLoRALinear"]):
         members = list(members)

@@ -96,7 +96,14 @@ def test_attach_adapters_groups_qkv_on_the_fused_path():
         for m in layers.values():
             m.prep_group = None
         alone = model(*args)
-    assert torch.equal(grouped, alone)
+        again = model(*args)                         # the B factors from each layer's cache
+        router.set([[(1, 1.0)], [(0, 0.5)]])
+        rerouted = model(*args)
+        for m in layers.values():
+            m._bdec_cache = None
+        rerouted_fresh = model(*args)
+    assert torch.equal(grouped, alone) and torch.equal(again, alone)
+    assert not torch.equal(rerouted, alone) and torch.equal(rerouted, rerouted_fresh)
 
 
 def test_decoded_b_factors_are_reused_while_routing_and_bank_are_unchanged():
