@@ -637,6 +637,216 @@ def run_decode(args):
         dist.destroy_process_group()
 
 
+# --------------------------------------------------------------------------------------- the reference's GPU kernels
+REF_INSTALL = ROOT / "baseline" / "_ref"
+
+
+def reference_package():
+    """The unmodified reference package (``lithe``) from its offline pip install in
+    baseline/_ref, with its Triton kernels usable.  Raises ImportError with the reason when it
+    cannot be used, so that the workload prints an ``unavailable`` line instead."""
+    if not (REF_INSTALL / "lithe" / "__init__.py").exists():
+        raise ImportError("no reference install in baseline/_ref")
+    if str(REF_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REF_INSTALL))
+    import lithe
+    import lithe.codebook
+    import lithe.kernels.packed
+    import lithe.kernels.sgmv
+    import lithe.kernels.shared
+    from lithe.kernels import _triton
+    if Path(lithe.__file__).resolve().parent != (REF_INSTALL / "lithe").resolve():
+        raise ImportError(f"'lithe' resolved to {lithe.__file__}, not the install in baseline/_ref")
+    if not _triton.HAS_TRITON:
+        raise ImportError("triton is not importable, so the reference would run its torch fallback")
+    return lithe
+
+
+def _event_ms(fn, steps: int, warmup: int, stream) -> float:
+    """Mean CUDA-event time of ``fn`` over ``steps`` calls after ``warmup`` untimed ones."""
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
+    for e0, e1 in evs:
+        e0.record(stream)
+        fn()
+        e1.record(stream)
+    torch.cuda.synchronize()
+    return statistics.mean(e0.elapsed_time(e1) for e0, e1 in evs)
+
+
+def _fp32_delta(x, idx_a, idx_b, pa, pb, assign, d_out):
+    """fp32 truth of the per-sample delta: A_j and B_j decoded in fp32 through the fp32 pools
+    (levels summed in order 0, 1, 2, lithe/quant.py:74-92), then (x_b A_j^T) B_j^T in fp32."""
+    d_in = x.shape[2]
+    res = torch.empty((x.shape[0], x.shape[1], d_out), dtype=torch.float32, device=x.device)
+    for b in range(x.shape[0]):
+        j = int(assign[b])
+        a = pa[0][idx_a[j, 0].long()]
+        bm = pb[0][idx_b[j, 0].long()]
+        for lv in range(1, pa.shape[0]):
+            a = a + pa[lv][idx_a[j, lv].long()]
+            bm = bm + pb[lv][idx_b[j, lv].long()]
+        res[b] = (x[b].float() @ a.reshape(RANK, d_in).T) @ bm.reshape(d_out, RANK).T
+    return res
+
+
+def _delta_error(d: torch.Tensor, truth: torch.Tensor) -> dict:
+    diff = d.float() - truth
+    return {"max_abs_rel": float(diff.abs().max() / truth.abs().max()), "rel_fro": float(diff.norm() / truth.norm())}
+
+
+def run_ref_gpu(args):
+    """The reference's own Triton kernels beside ours on the same B200, same inputs.
+
+    SGMV, per FLUX shape of config 2 (B=14, M=4608, r=16, 14 distinct slots of a 10,000-slot
+    bank): the reference's LoRA path of ``IndexLoRALinear.forward`` (lithe/kernels/layers.py:
+    119-131) is ``shared_codebook_lora_delta`` (two Triton launches, lithe/kernels/shared.py:
+    197-263) and then ``out + delta``; ours is one ``lithe_sgmv_index`` launch accumulating into
+    ``out`` in place.  Both get the same int32 index banks (n_slots, L, n_blocks), the same bf16
+    pools, x and routing; both deltas are checked against an fp32 truth decoded on the device.
+    Also timed: the reference's dense decoded-factor SGMV ``per_sample_lora_delta``
+    (lithe/kernels/sgmv.py:112-160) + the add, given the batch's bf16 factors.
+
+    Decode, per adapter layout (342-module FLUX, Kohya-304): the reference's Triton
+    ``decode_packed`` (lithe/kernels/packed.py:205-222) and ours, one adapter per call on the
+    same packed words (the stream layouts are identical), outputs compared bit for bit.
+    """
+    world, rank, local = dist_env()
+    if world > 1:
+        raise SystemExit("ref_gpu_flux runs on one GPU")
+    try:
+        ref = reference_package()
+    except ImportError as e:
+        print(json.dumps({"workload": args.workload, "unavailable": str(e)}), flush=True)
+        return
+    from lithe_b200 import codebook as cb
+    from lithe_b200 import device_errors
+    from lithe_b200.kernels import PackedBank, PackedLayout
+    from lithe_b200.kernels import _launch, ops
+    from lithe_b200.kernels.packed import decode_packed as ours_decode_packed
+    from lithe_b200.kernels.shared import _lut_list
+
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    stream = torch.cuda.current_stream(dev)
+    steps, warmup = args.steps, args.warmup
+    pa32, pb32 = (p.to(dev) for p in ref.codebook.twin_pools())
+    pa16, pb16 = pa32.to(torch.bfloat16), pb32.to(torch.bfloat16)       # pools in the activation dtype, as
+    lut = _lut_list(pa16, pb16, torch.bfloat16)                          # IndexLoRALinear holds them
+    slots = torch.randperm(BANK_SLOTS, generator=torch.Generator().manual_seed(100))[:BATCH]
+    assign = slots.to(torch.int32).to(dev)
+    peak, peak_kind = measured_peaks()
+    shapes = []
+    for si, (d_in, d_out) in enumerate(SHAPES):
+        g = torch.Generator(device=dev)
+        g.manual_seed(500 + si)
+        idx_a = torch.randint(0, 512, (BANK_SLOTS, LEVELS, RANK * d_in // 64), generator=g, device=dev,
+                              dtype=torch.int32)
+        idx_b = torch.randint(0, 512, (BANK_SLOTS, LEVELS, d_out * RANK // 64), generator=g, device=dev,
+                              dtype=torch.int32)
+        x = torch.randn(BATCH, TOKENS, d_in, generator=g, device=dev, dtype=torch.bfloat16)
+        base = torch.randn(BATCH, TOKENS, d_out, generator=g, device=dev, dtype=torch.bfloat16) * 0.05
+        # parity of both deltas against the fp32 truth
+        d_ref = ref.kernels.shared.shared_codebook_lora_delta(x, idx_a, pa16, idx_b, pb16, assign, RANK, d_out, 1.0,
+                                                              out_dtype=torch.bfloat16)
+        d_ours = torch.zeros_like(base)
+        va = ops.view_params(_launch.level_major_view(idx_a))
+        vb = ops.view_params(_launch.level_major_view(idx_b))
+        torch.ops.lithe_b200.sgmv_index_(d_ours, x, idx_a, idx_b, va, vb, BANK_SLOTS, assign, None, RANK, lut, 1.0,
+                                         True)
+        truth = _fp32_delta(x, idx_a, idx_b, pa32, pb32, assign.cpu(), d_out)
+        parity = {"ours_vs_fp32": _delta_error(d_ours, truth), "reference_vs_fp32": _delta_error(d_ref, truth),
+                  "ours_vs_reference": _delta_error(d_ours, d_ref.float())}
+        del truth, d_ref, d_ours
+        out = base.clone()
+
+        def ref_call():
+            base + ref.kernels.shared.shared_codebook_lora_delta(x, idx_a, pa16, idx_b, pb16, assign, RANK, d_out,
+                                                                 1.0, out_dtype=torch.bfloat16)
+
+        def ours_call():
+            torch.ops.lithe_b200.sgmv_index_(out, x, idx_a, idx_b, va, vb, BANK_SLOTS, assign, None, RANK, lut, 1.0,
+                                             True)
+
+        # the reference's dense comparator: the batch's decoded bf16 factors resident, Triton SGMV + add
+        sa = torch.stack([(sum(pa32[lv][idx_a[int(j), lv].long()] for lv in range(LEVELS))).reshape(RANK, d_in)
+                          for j in slots]).to(torch.bfloat16)
+        sb = torch.stack([(sum(pb32[lv][idx_b[int(j), lv].long()] for lv in range(LEVELS))).reshape(d_out, RANK)
+                          for j in slots]).to(torch.bfloat16)
+        scal = torch.ones(BATCH, device=dev, dtype=torch.float32)
+
+        def ref_dense_call():
+            base + ref.kernels.sgmv.per_sample_lora_delta(x, sa, sb, scal)
+
+        t_ref = _event_ms(ref_call, steps, warmup, stream)
+        t_ours = _event_ms(ours_call, steps, warmup, stream)
+        t_dense = _event_ms(ref_dense_call, steps, warmup, stream)
+        nbytes = algorithmic_bytes(d_in, d_out)
+        shapes.append({"shape": f"{d_in}x{d_out}", "reference_ms": t_ref, "ours_ms": t_ours,
+                       "reference_dense_ms": t_dense, "speedup": t_ref / t_ours,
+                       "reference_gbs": nbytes / t_ref / 1e6, "ours_gbs": nbytes / t_ours / 1e6,
+                       "ours_frac_of_peak": nbytes / t_ours / 1e6 / peak, "parity": parity})
+        del idx_a, idx_b, x, base, out, sa, sb
+        torch.cuda.empty_cache()
+
+    decode = []
+    for kind in ("flux342", "kohya304"):
+        mods = decode_modules(kind)
+        lay = PackedLayout.from_modules(mods)
+        bank = PackedBank(lay, DECODE_PER_LAUNCH, dev)
+        bank.fill_random(seed=4321)
+        ref_lay = ref.kernels.packed.PackedLayout(
+            names=list(lay.names), shapes_a=list(lay.shapes_a), shapes_b=list(lay.shapes_b), a_off=list(lay.a_off),
+            b_off=list(lay.b_off), sides=lay.sides.clone(), num_levels=lay.num_levels, block_size=lay.block_size,
+            scaling=lay.scaling)
+        words = [bank.words[s, : lay.num_words] for s in range(DECODE_PER_LAUNCH)]
+        equal = all(torch.equal(ref.kernels.packed.decode_packed(w.view(torch.uint64), ref_lay, pa32, pb32),
+                                ours_decode_packed(w, lay, pa32.cpu(), pb32.cpu())) for w in words)
+        k = [0]
+
+        def ref_dec():
+            ref.kernels.packed.decode_packed(words[k[0] % DECODE_PER_LAUNCH].view(torch.uint64), ref_lay, pa32, pb32)
+            k[0] += 1
+
+        # ours through the same one-adapter API, its LUT, sides and output prepared once (as a
+        # layer holds them); and the batched form, 14 adapters per launch
+        sides = lay.sides_on(dev)
+        one = torch.empty((lay.total_blocks, lay.block_size), dtype=torch.bfloat16, device=dev)
+
+        def ours_dec():
+            _launch.decode_packed_(words[k[0] % DECODE_PER_LAUNCH], lay.total_blocks, lay.num_levels, sides, bank.lut,
+                                   one)
+            k[0] += 1
+
+        ids14 = torch.arange(DECODE_PER_LAUNCH, dtype=torch.int32, device=dev)
+        out14 = torch.empty((DECODE_PER_LAUNCH, lay.total_blocks, lay.block_size), dtype=torch.bfloat16, device=dev)
+        t_ref = _event_ms(ref_dec, steps, warmup, stream)
+        t_ours = _event_ms(ours_dec, steps, warmup, stream)
+        t_batch = _event_ms(lambda: bank.decode(ids14, out=out14), steps, warmup, stream) / DECODE_PER_LAUNCH
+        mb = lay.total_blocks * 128 / 1e6
+        decode.append({"layout": kind, "decoded_mb_per_adapter": mb, "reference_ms_per_adapter": t_ref,
+                       "ours_ms_per_adapter": t_ours, "ours_batched_ms_per_adapter": t_batch,
+                       "speedup": t_ref / t_ours, "reference_gbs": mb / t_ref, "ours_gbs": mb / t_ours,
+                       "ours_batched_gbs": mb / t_batch, "bit_exact": bool(equal)})
+        del bank, words, one, out14
+        torch.cuda.empty_cache()
+    tok = len(SHAPES) * BATCH * TOKENS
+    ref_ms, ours_ms = sum(s["reference_ms"] for s in shapes), sum(s["ours_ms"] for s in shapes)
+    print(json.dumps({
+        "workload": args.workload, "metric": "SGMV tokens/s at B=14 FLUX shapes: reference Triton vs lithe_b200",
+        "unit": "tokens/s", "reference_value": tok / ref_ms * 1e3, "value": tok / ours_ms * 1e3,
+        "speedup": ref_ms / ours_ms, "steps": steps, "warmup": warmup, "dtype": "bf16",
+        "data": "synthetic: seeded uniform 9-bit indices (int32 banks), x ~ N(0,1)",
+        "config": {"batch": BATCH, "tokens": TOKENS, "rank": RANK, "bank_slots": BANK_SLOTS,
+                   "reference": f"lithe {getattr(ref, '__version__', '1.0.0')} from baseline/_ref, unmodified",
+                   "triton": __import__("triton").__version__, "peak_gbs": peak, "peak_source": peak_kind,
+                   "l2": "inputs larger than L2 (>= 396 MB of x per call), no flush",
+                   "tolerance": "max-abs-rel 2e-2 of the fp32 delta"},
+        "per_shape": shapes, "decode": decode, "device_errors": device_errors(dev)}), flush=True)
+
+
 # --------------------------------------------------------------------------------------- denoise workloads
 
 
@@ -1342,9 +1552,10 @@ def main():
     ap.add_argument("--workload", choices=["flux_sweep_b14", "decode_flux342", "decode_kohya304", "denoise_512",
                                            "denoise_256_b96", "denoise_1024", "denoise_512_kohya",
                                            "denoise_1024_kohya", "hotswap_kohya304", "lora_gemm_flux",
-                                           "gemm_sustained"],
+                                           "gemm_sustained", "ref_gpu_flux"],
                     default="flux_sweep_b14", help="flux_sweep_b14: fused decode+SGMV (default); decode_*: "
-                    "standalone packed decode of 14 resident adapters per launch")
+                    "standalone packed decode of 14 resident adapters per launch; ref_gpu_flux: the reference's "
+                    "Triton kernels (from baseline/_ref) beside ours on the same inputs")
     ap.add_argument("--seconds", type=float, default=3.0,
                     help="gemm_sustained: seconds of back-to-back calls per pass")
     ap.add_argument("--cpu-seconds", type=float, default=15.0,
@@ -1385,6 +1596,8 @@ def main():
         run_gemm_sustained(args)
     elif args.workload == "lora_gemm_flux":
         run_lora_gemm(args)
+    elif args.workload == "ref_gpu_flux":
+        run_ref_gpu(args)
     elif args.impl == "reference":
         run_reference(args)
     else:
