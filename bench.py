@@ -780,14 +780,16 @@ def run_ref_gpu(args):
         def ref_dense_call():
             base + ref.kernels.sgmv.per_sample_lora_delta(x, sa, sb, scal)
 
-        t_ref = _event_ms(ref_call, steps, warmup, stream)
-        t_ours = _event_ms(ours_call, steps, warmup, stream)
-        t_dense = _event_ms(ref_dense_call, steps, warmup, stream)
+        with ClockSampler(local) as clocks:
+            t_ref = _event_ms(ref_call, steps, warmup, stream)
+            t_ours = _event_ms(ours_call, steps, warmup, stream)
+            t_dense = _event_ms(ref_dense_call, steps, warmup, stream)
         nbytes = algorithmic_bytes(d_in, d_out)
         shapes.append({"shape": f"{d_in}x{d_out}", "reference_ms": t_ref, "ours_ms": t_ours,
                        "reference_dense_ms": t_dense, "speedup": t_ref / t_ours,
                        "reference_gbs": nbytes / t_ref / 1e6, "ours_gbs": nbytes / t_ours / 1e6,
-                       "ours_frac_of_peak": nbytes / t_ours / 1e6 / peak, "parity": parity})
+                       "ours_frac_of_peak": nbytes / t_ours / 1e6 / peak, "parity": parity,
+                       "clocks": clocks.summary()})
         del idx_a, idx_b, x, base, out, sa, sb
         torch.cuda.empty_cache()
 
@@ -822,14 +824,15 @@ def run_ref_gpu(args):
 
         ids14 = torch.arange(DECODE_PER_LAUNCH, dtype=torch.int32, device=dev)
         out14 = torch.empty((DECODE_PER_LAUNCH, lay.total_blocks, lay.block_size), dtype=torch.bfloat16, device=dev)
-        t_ref = _event_ms(ref_dec, steps, warmup, stream)
-        t_ours = _event_ms(ours_dec, steps, warmup, stream)
-        t_batch = _event_ms(lambda: bank.decode(ids14, out=out14), steps, warmup, stream) / DECODE_PER_LAUNCH
+        with ClockSampler(local) as clocks:
+            t_ref = _event_ms(ref_dec, steps, warmup, stream)
+            t_ours = _event_ms(ours_dec, steps, warmup, stream)
+            t_batch = _event_ms(lambda: bank.decode(ids14, out=out14), steps, warmup, stream) / DECODE_PER_LAUNCH
         mb = lay.total_blocks * 128 / 1e6
         decode.append({"layout": kind, "decoded_mb_per_adapter": mb, "reference_ms_per_adapter": t_ref,
                        "ours_ms_per_adapter": t_ours, "ours_batched_ms_per_adapter": t_batch,
                        "speedup": t_ref / t_ours, "reference_gbs": mb / t_ref, "ours_gbs": mb / t_ours,
-                       "ours_batched_gbs": mb / t_batch, "bit_exact": bool(equal)})
+                       "ours_batched_gbs": mb / t_batch, "bit_exact": bool(equal), "clocks": clocks.summary()})
         del bank, words, one, out14
         torch.cuda.empty_cache()
     tok = len(SHAPES) * BATCH * TOKENS
