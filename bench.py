@@ -651,6 +651,7 @@ def reference_package():
         sys.path.insert(0, str(REF_INSTALL))
     import lithe
     import lithe.codebook
+    import lithe.kernels.layers
     import lithe.kernels.packed
     import lithe.kernels.sgmv
     import lithe.kernels.shared
@@ -695,6 +696,26 @@ def _fp32_delta(x, idx_a, idx_b, pa, pb, assign, d_out):
 def _delta_error(d: torch.Tensor, truth: torch.Tensor) -> dict:
     diff = d.float() - truth
     return {"max_abs_rel": float(diff.abs().max() / truth.abs().max()), "rel_fro": float(diff.norm() / truth.norm())}
+
+
+def int32_index_banks(bank, name: str, slot_ids) -> tuple:
+    """Module ``name``'s indices of the given slots of a packed bank as the reference's
+    IndexLoRALinear holds them: (n, L, n_blocks_A) and (n, L, n_blocks_B) int32, unpacked on
+    the bank's device from the (block, level)-major stream (A blocks, then B blocks)."""
+    lay = bank.layout
+    i = lay.index(name)
+    levels = lay.num_levels
+    n_a = lay.b_off[i] - lay.a_off[i]
+    n_b = lay.shapes_b[i][0] * lay.shapes_b[i][1] // lay.block_size
+    start, stop = levels * lay.a_off[i], levels * (lay.b_off[i] + n_b)
+    w0, w1 = start // 7, -(-stop // 7)
+    ids = torch.as_tensor(slot_ids, dtype=torch.long).to(bank.words.device)
+    words = bank.words[ids][:, w0:w1]
+    shifts = torch.arange(7, device=words.device, dtype=torch.int64) * 9
+    flat = ((words[:, :, None] >> shifts) & 511).reshape(ids.numel(), -1)[:, start - 7 * w0: stop - 7 * w0]
+    a = flat[:, : levels * n_a].reshape(-1, n_a, levels).transpose(1, 2)
+    b = flat[:, levels * n_a:].reshape(-1, n_b, levels).transpose(1, 2)
+    return a.to(torch.int32).contiguous(), b.to(torch.int32).contiguous()
 
 
 def run_ref_gpu(args):
@@ -859,10 +880,11 @@ class _DenoiseSetup:
     10,000-slot bank (``PackedLoRALinear``, cuBLAS + the fused decode/SGMV kernel, or with
     ``fused_gemm`` lithe_lora_prep + the expand inside lithe_lora_gemm); a dense resident-LoRA
     comparator (the batch's decoded bf16 factors resident in HBM, cuBLAS bmm + in-place baddbmm);
-    and a diagnostic with the base linears on lithe_lora_gemm without LoRA.  Samples [lo, hi) of
-    the batch run on this rank; the bank and the base weights are identical on every rank."""
+    and a diagnostic with the base linears on lithe_lora_gemm without LoRA.  Given the reference
+    package, also the reference's own GPU path (``reference_triton``).  Samples [lo, hi) of the
+    batch run on this rank; the bank and the base weights are identical on every rank."""
 
-    def __init__(self, dev, img_tok, txt_tok, batch, key_format, lo, hi, slot_seed, input_seed):
+    def __init__(self, dev, img_tok, txt_tok, batch, key_format, lo, hi, slot_seed, input_seed, reference=None):
         from lithe_b200 import kohya
         from lithe_b200.flux_model import FluxShapedTransformer, lora_targets
         from lithe_b200.kernels import (PackedBank, PackedLayout, PackedLoRALinear, PerSampleLoRALinear,
@@ -940,6 +962,38 @@ class _DenoiseSetup:
         self.packed = packed
         self.tables = {"base": bases, "plain_gemm": plain, "lithe": packed, "lithe_fused": packed,
                        "lithe_fused_all": packed, "dense": dense}
+        self.reference_check = None
+        if reference is not None:
+            # the reference's own GPU path: its IndexLoRALinear (cuBLAS base + the Triton
+            # shared_codebook_lora_delta + out + delta) on every target, holding the batch's slots
+            # as int32 banks unpacked from the same packed bank (its kernel reads only the routed
+            # slots, so the bank's size does not enter its time), pools in bf16
+            if split is not None:
+                raise SystemExit("the reference_triton variant serves the diffusers-342 layout only")
+            pa16, pb16 = (p.to(device=dev, dtype=torch.bfloat16) for p in reference.codebook.twin_pools())
+            local_ids = torch.arange(self.nb, dtype=torch.int32, device=dev)
+            ref_layers = {}
+            for n in self.names:
+                ia, ib = int32_index_banks(bank, n, slots)
+                lyr = reference.kernels.layers.IndexLoRALinear(bases[n], ia, ib, pa16, pb16, RANK, 1.0)
+                lyr.assign = local_ids
+                ref_layers[n] = lyr
+            self.tables["reference_triton"] = ref_layers
+            # the two paths on one linear of each shape, same input: their deltas must agree
+            self.reference_check = {}
+            seen = set()
+            with torch.no_grad():
+                for n in self.names:
+                    shape = (bases[n].in_features, bases[n].out_features)
+                    if shape in seen:
+                        continue
+                    seen.add(shape)
+                    x = torch.randn(self.nb, 256, shape[0], generator=g, device=dev, dtype=torch.bfloat16)
+                    packed[n].fused_gemm = False
+                    y0 = bases[n](x).float()
+                    d_ours, d_ref = packed[n](x).float() - y0, ref_layers[n](x).float() - y0
+                    self.reference_check[f"{shape[0]}x{shape[1]}"] = float((d_ours - d_ref).abs().max()
+                                                                          / d_ref.abs().max())
 
     def install(self, kind):
         from lithe_b200.kernels.layers import FUSED_GEMM_MAX_K
@@ -1025,12 +1079,16 @@ DENOISE = {  # workload -> (image tokens, text tokens, batch, steps, adapter key
 }
 
 
+DENOISE_VARIANTS = ("base", "plain_gemm", "lithe", "lithe_fused", "lithe_fused_all", "dense")
+
+
 def run_denoise(args):
     """The denoise workloads with all six variants (base, plain tcgen05 GEMM without LoRA, LITHE
     cuBLAS + decode/SGMV, LITHE fused GEMM with the default in_features policy, fused GEMM on
     every eligible linear, dense resident LoRA), ABBA order.  Targets: the 342 diffusers
     linears, or the 494 linears a Kohya-304 adapter covers (its fused q/k/v modules served in
-    place)."""
+    place).  ``--variants`` times a subset; its ``reference_triton`` variant adds the
+    reference's own GPU path (its IndexLoRALinear from baseline/_ref) on the 342 layout."""
     from lithe_b200.shard import shard_bounds
     img_tok, txt_tok, batch, steps, key_format = DENOISE[args.workload]
     world, rank, local = dist_env()
@@ -1040,14 +1098,51 @@ def run_denoise(args):
                               "FLUX.1-dev weights, absent on this box; its CPU path is timed per linear by the "
                               "flux_sweep_b14 workload"}), flush=True)
         return
+    kinds = tuple(args.variants.split(",")) if args.variants else DENOISE_VARIANTS
+    unknown = [k for k in kinds if k not in DENOISE_VARIANTS + ("reference_triton",)]
+    if unknown or "base" not in kinds:
+        raise SystemExit(f"--variants: unknown {unknown}" if unknown else "--variants must include base")
+    reference = None
+    if "reference_triton" in kinds:
+        try:
+            reference = reference_package()
+        except ImportError as e:
+            if rank == 0:
+                print(json.dumps({"workload": args.workload, "unavailable": f"reference_triton: {e}"}), flush=True)
+            return
     init_dist(world, local)
     dev = torch.device("cuda", local)
     strong = args.scaling == "strong"
     lo, hi = shard_bounds(batch, world, rank) if strong else (0, batch)
     setup = _DenoiseSetup(dev, img_tok, txt_tok, batch, key_format, lo, hi,
-                          slot_seed=300 if strong else 300 + rank, input_seed=7 + (0 if strong else rank))
-    kinds = ("base", "plain_gemm", "lithe", "lithe_fused", "lithe_fused_all", "dense")
+                          slot_seed=300 if strong else 300 + rank, input_seed=7 + (0 if strong else rank),
+                          reference=reference)
     mean, runs, clock_log = setup.time_abba(kinds, steps, world, local, dev)
+    if kinds != DENOISE_VARIANTS:
+        if rank == 0:
+            t_base = mean["base"]
+            print(json.dumps({
+                "metric": f"{steps}-step denoise wall time", "unit": "s", "n_gpus": world, "steps": steps,
+                "higher_is_better": False, "variants_s": mean,
+                "lora_overhead_s": {k: v - t_base for k, v in mean.items() if k != "base"},
+                "overhead_ratio_vs_dense": ({k: (v - t_base) / max(1e-9, mean["dense"] - t_base)
+                                             for k, v in mean.items() if k not in ("base", "dense")}
+                                            if "dense" in mean else None),
+                "reference_triton_path": "the reference's IndexLoRALinear (lithe/kernels/layers.py:97-131) from "
+                                         "baseline/_ref: cuBLAS base + Triton shared_codebook_lora_delta + out + delta"
+                                         if reference is not None else None,
+                "reference_delta_check_max_abs_rel": setup.reference_check,
+                "dtype": "bf16", "data": "synthetic: random-init FLUX.1-dev-shaped transformer, seeded uniform 9-bit "
+                "packed adapters",
+                "config": {"workload": args.workload, "image_tokens": img_tok, "text_tokens": txt_tok,
+                           "batch": batch, "rank_batch": setup.nb, "lora_linears": len(setup.names),
+                           "bank_slots": BANK_SLOTS, "adapter_format": key_format},
+                "passes_s": runs, "order": "ABBA: " + " ".join(kinds + tuple(reversed(kinds))),
+                "clocks": clock_log}), flush=True)
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        return
     t_base, t_lithe, t_dense = mean["base"], mean["lithe"], mean["dense"]
     t_fused = mean["lithe_fused"]
     if rank == 0:
@@ -1571,6 +1666,9 @@ def main():
     ap.add_argument("--scaling", choices=["strong", "weak"], default="strong",
                     help="N > 1: strong (default) splits the fixed B=14 batch by sample across the ranks; weak gives "
                          "every rank its own B=14 batch (the default line also reports weak scaling as a secondary key)")
+    ap.add_argument("--variants", default="", help="denoise_*: comma list of variants to time (default: "
+                    + ",".join(DENOISE_VARIANTS) + "); reference_triton adds the reference's own GPU path "
+                    "(its IndexLoRALinear from baseline/_ref)")
     ap.add_argument("--no-denoise", action="store_true",
                     help="leave out the 28-step 1024^2 denoise record of the default line")
     ap.add_argument("--shapes", default="", help="comma list of d_inxd_out to run (default: all four), "
