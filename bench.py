@@ -427,6 +427,16 @@ def run_lithe(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = cpu_reference_passes(args.steps, warmup=args.warmup)
+    # the reference's own GPU kernels on this device and the same inputs (one GPU only)
+    reference_gpu = None
+    if world == 1 and not args.no_reference_gpu:
+        try:
+            reference_gpu = reference_gpu_comparison(reference_package(), dev, args.steps, args.warmup)
+        except ImportError as e:
+            reference_gpu = {"unavailable": str(e)}
+        except Exception as e:  # a comparator failure (e.g. a Triton JIT error) must not cost the headline line
+            reference_gpu = {"error": f"{type(e).__name__}: {e}"}
+        torch.cuda.empty_cache()
 
     peak, peak_kind = measured_peaks()
     alg = [algorithmic_bytes(a, b, batch=nb, distinct=nb) for a, b in SHAPES]
@@ -484,6 +494,7 @@ def run_lithe(args):
             "gpu_launches": launches,
             "per_shape": shapes_out,
             "weak_scaling": weak,
+            "reference_gpu": reference_gpu,
             "denoise": denoise,
             "device_errors": errors,
         }
@@ -718,7 +729,7 @@ def int32_index_banks(bank, name: str, slot_ids) -> tuple:
     return a.to(torch.int32).contiguous(), b.to(torch.int32).contiguous()
 
 
-def run_ref_gpu(args):
+def reference_gpu_comparison(ref, dev, steps: int, warmup: int) -> dict:
     """The reference's own Triton kernels beside ours on the same B200, same inputs.
 
     SGMV, per FLUX shape of config 2 (B=14, M=4608, r=16, 14 distinct slots of a 10,000-slot
@@ -734,25 +745,14 @@ def run_ref_gpu(args):
     ``decode_packed`` (lithe/kernels/packed.py:205-222) and ours, one adapter per call on the
     same packed words (the stream layouts are identical), outputs compared bit for bit.
     """
-    world, rank, local = dist_env()
-    if world > 1:
-        raise SystemExit("ref_gpu_flux runs on one GPU")
-    try:
-        ref = reference_package()
-    except ImportError as e:
-        print(json.dumps({"workload": args.workload, "unavailable": str(e)}), flush=True)
-        return
-    from lithe_b200 import codebook as cb
     from lithe_b200 import device_errors
     from lithe_b200.kernels import PackedBank, PackedLayout
     from lithe_b200.kernels import _launch, ops
     from lithe_b200.kernels.packed import decode_packed as ours_decode_packed
     from lithe_b200.kernels.shared import _lut_list
 
-    torch.cuda.set_device(local)
-    dev = torch.device("cuda", local)
+    local = dev.index if dev.index is not None else torch.cuda.current_device()
     stream = torch.cuda.current_stream(dev)
-    steps, warmup = args.steps, args.warmup
     pa32, pb32 = (p.to(dev) for p in ref.codebook.twin_pools())
     pa16, pb16 = pa32.to(torch.bfloat16), pb32.to(torch.bfloat16)       # pools in the activation dtype, as
     lut = _lut_list(pa16, pb16, torch.bfloat16)                          # IndexLoRALinear holds them
@@ -858,17 +858,32 @@ def run_ref_gpu(args):
         torch.cuda.empty_cache()
     tok = len(SHAPES) * BATCH * TOKENS
     ref_ms, ours_ms = sum(s["reference_ms"] for s in shapes), sum(s["ours_ms"] for s in shapes)
-    print(json.dumps({
-        "workload": args.workload, "metric": "SGMV tokens/s at B=14 FLUX shapes: reference Triton vs lithe_b200",
-        "unit": "tokens/s", "reference_value": tok / ref_ms * 1e3, "value": tok / ours_ms * 1e3,
-        "speedup": ref_ms / ours_ms, "steps": steps, "warmup": warmup, "dtype": "bf16",
-        "data": "synthetic: seeded uniform 9-bit indices (int32 banks), x ~ N(0,1)",
-        "config": {"batch": BATCH, "tokens": TOKENS, "rank": RANK, "bank_slots": BANK_SLOTS,
-                   "reference": f"lithe {getattr(ref, '__version__', '1.0.0')} from baseline/_ref, unmodified",
-                   "triton": __import__("triton").__version__, "peak_gbs": peak, "peak_source": peak_kind,
-                   "l2": "inputs larger than L2 (>= 396 MB of x per call), no flush",
-                   "tolerance": "max-abs-rel 2e-2 of the fp32 delta"},
-        "per_shape": shapes, "decode": decode, "device_errors": device_errors(dev)}), flush=True)
+    return {"metric": "SGMV tokens/s at B=14 FLUX shapes: reference Triton vs lithe_b200 on the same inputs",
+            "unit": "tokens/s", "reference_value": tok / ref_ms * 1e3, "value": tok / ours_ms * 1e3,
+            "speedup": ref_ms / ours_ms, "steps": steps, "warmup": warmup, "dtype": "bf16",
+            "data": "synthetic: seeded uniform 9-bit indices (int32 banks), x ~ N(0,1)",
+            "config": {"batch": BATCH, "tokens": TOKENS, "rank": RANK, "bank_slots": BANK_SLOTS,
+                       "reference": f"lithe {getattr(ref, '__version__', '1.0.0')} from baseline/_ref, unmodified",
+                       "triton": __import__("triton").__version__, "peak_gbs": peak, "peak_source": peak_kind,
+                       "l2": "inputs larger than L2 (>= 396 MB of x per call), no flush",
+                       "tolerance": "max-abs-rel 2e-2 of the fp32 delta",
+                       "ours": "lithe_sgmv_index on the same int32 banks (the headline reads the packed bank)"},
+            "per_shape": shapes, "decode": decode, "device_errors": device_errors(dev)}
+
+
+def run_ref_gpu(args):
+    """``--workload ref_gpu_flux``: the comparison above as one JSON line (one GPU)."""
+    world, _, local = dist_env()
+    if world > 1:
+        raise SystemExit("ref_gpu_flux runs on one GPU")
+    try:
+        ref = reference_package()
+    except ImportError as e:
+        print(json.dumps({"workload": args.workload, "unavailable": str(e)}), flush=True)
+        return
+    torch.cuda.set_device(local)
+    rec = reference_gpu_comparison(ref, torch.device("cuda", local), args.steps, args.warmup)
+    print(json.dumps({"workload": args.workload, **rec}), flush=True)
 
 
 # --------------------------------------------------------------------------------------- denoise workloads
@@ -1660,6 +1675,8 @@ def main():
                     help="CPU-baseline sample length of the decode and hot-swap workloads (rank 0, N=1)")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-e2e", action="store_true", help="skip the host-buffer end-to-end leg")
+    ap.add_argument("--no-reference-gpu", action="store_true",
+                    help="leave out the reference's Triton kernels timed beside ours in the default line (N=1)")
     ap.add_argument("--mode", choices=["staged", "fused"], default=None,
                     help="form of the fused op: fused (decode inside the SGMV kernel per 64-token tile, default) "
                          "or staged (decode once per call into a workspace)")
