@@ -994,7 +994,10 @@ class _DenoiseSetup:
                 lyr.assign = local_ids
                 ref_layers[n] = lyr
             self.tables["reference_triton"] = ref_layers
-            # the two paths on one linear of each shape, same input: their deltas must agree
+            # the two kernels on one linear of each shape, same input, each delta on its own (a
+            # difference of two bf16 base + delta sums would measure the rounding of the base):
+            # max |ours - reference| / max |reference|
+            from lithe_b200.kernels import packed_codebook_lora_delta_
             self.reference_check = {}
             seen = set()
             with torch.no_grad():
@@ -1004,10 +1007,13 @@ class _DenoiseSetup:
                         continue
                     seen.add(shape)
                     x = torch.randn(self.nb, 256, shape[0], generator=g, device=dev, dtype=torch.bfloat16)
-                    packed[n].fused_gemm = False
-                    y0 = bases[n](x).float()
-                    d_ours, d_ref = packed[n](x).float() - y0, ref_layers[n](x).float() - y0
-                    self.reference_check[f"{shape[0]}x{shape[1]}"] = float((d_ours - d_ref).abs().max()
+                    lyr = ref_layers[n]
+                    d_ref = reference.kernels.shared.shared_codebook_lora_delta(
+                        x, lyr.idx_a, lyr.pool_a, lyr.idx_b, lyr.pool_b, lyr.assign, RANK, shape[1], 1.0,
+                        out_dtype=torch.bfloat16).float()
+                    d_ours = torch.zeros(self.nb, 256, shape[1], device=dev, dtype=torch.bfloat16)
+                    packed_codebook_lora_delta_(d_ours, x, bank, n, ids, scaling=1.0)
+                    self.reference_check[f"{shape[0]}x{shape[1]}"] = float((d_ours.float() - d_ref).abs().max()
                                                                           / d_ref.abs().max())
 
     def install(self, kind):

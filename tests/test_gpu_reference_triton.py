@@ -7,13 +7,15 @@ when it is absent) runs its Triton ``shared_codebook_lora_delta`` (lithe/kernels
 - SGMV: both deltas within max-abs-rel 2e-2 and relative Frobenius error 1e-2 of the fp32
   truth (the tolerance of the other SGMV tests) and of each other, ragged token counts, int32
   index banks, pools in the activation dtype as the reference's IndexLoRALinear holds them;
-- decode: our bf16 output equal bit for bit to the reference kernel's on the same packed words.
+- decode: our bf16 output equal bit for bit to the reference kernel's on the same packed words;
+- the reference's kernel on int32 banks unpacked from our packed bank (the form the denoise
+  bench's ``reference_triton`` variant serves) against our kernel on the packed bank itself.
 """
 import pytest
 import torch
 
 import bench
-from lithe_b200.kernels import PackedBank, PackedLayout, shared_codebook_lora_delta
+from lithe_b200.kernels import PackedBank, PackedLayout, packed_codebook_lora_delta_, shared_codebook_lora_delta
 from lithe_b200.kernels.packed import decode_packed
 from tests.helpers import max_abs_rel, rel_fro
 
@@ -72,3 +74,30 @@ def test_decode_bit_exact_against_reference_triton(kind):
         want = ref.kernels.packed.decode_packed(words.view(torch.uint64), ref_lay, pa32.to(dev), pb32.to(dev))
         got = decode_packed(words, lay, pa32, pb32)
         assert torch.equal(got, want)
+
+
+@pytest.mark.gpu
+def test_reference_on_unpacked_banks_matches_packed_bank():
+    ref = _reference()
+    dev = torch.device("cuda")
+    shapes = {"q": (3072, 3072), "ff": (3072, 12288), "down": (12288, 3072)}
+    lay = PackedLayout.from_modules([{"name": n, "shape_a": [16, a], "shape_b": [b, 16]} for n, (a, b) in shapes.items()])
+    bank = PackedBank(lay, 40, dev)
+    bank.fill_random(seed=5)
+    slots = [31, 2, 17]
+    ids = torch.tensor(slots, dtype=torch.int32, device=dev)
+    local = torch.arange(len(slots), dtype=torch.int32, device=dev)
+    pa16, pb16 = (p.to(device=dev, dtype=torch.bfloat16) for p in ref.codebook.twin_pools())
+    g = torch.Generator(device=dev)
+    g.manual_seed(9)
+    for name, (d_in, d_out) in shapes.items():
+        ia, ib = bench.int32_index_banks(bank, name, slots)
+        assert ia.shape == (3, 3, 16 * d_in // 64) and ib.shape == (3, 3, d_out * 16 // 64)
+        x = torch.randn(3, 200, d_in, generator=g, device=dev, dtype=torch.bfloat16)
+        d_ref = ref.kernels.shared.shared_codebook_lora_delta(x, ia, pa16, ib, pb16, local, 16, d_out, 1.0,
+                                                              out_dtype=torch.bfloat16)
+        d_ours = torch.zeros(3, 200, d_out, device=dev, dtype=torch.bfloat16)
+        packed_codebook_lora_delta_(d_ours, x, bank, name, ids, scaling=1.0)
+        torch.cuda.synchronize()
+        assert max_abs_rel(d_ours.float(), d_ref.float()) <= MAX_ABS_REL
+        assert rel_fro(d_ours.float(), d_ref.float()) < REL_FRO
