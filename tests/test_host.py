@@ -389,3 +389,20 @@ def test_traffic_digest_ignores_comments_only():
     c = 'int f(int x) { return x + 2; }\nconst char* s = "a//b/*c*/";\n'
     assert bench._code_only(a) == bench._code_only(b) != bench._code_only(c)
     assert '"a//b/*c*/"' in bench._code_only(a)
+
+
+def test_int32_index_banks_unpack_the_packed_stream():
+    """The bench's reference_triton variant feeds the reference's IndexLoRALinear int32 banks
+    unpacked from the packed slots: they must be each adapter's own (L, n_blocks) indices."""
+    import bench
+    mods = [("a", 3072, 3072), ("b", 3072, 12288), ("c", 12288, 3072), ("odd", 96, 40), ("e", 15360, 3072)]
+    ads = [random_adapter(mods, rank=16, seed=s) for s in range(3)]
+    bank = packed.PackedBank.from_adapters(ads, "cpu")
+    order = [2, 0, 1]
+    for name, d_in, d_out in mods:
+        a, b = bench.int32_index_banks(bank, name, order)
+        assert a.dtype == torch.int32 and a.shape == (3, 3, quant.num_blocks((16, d_in)))
+        assert b.shape == (3, 3, quant.num_blocks((d_out, 16)))
+        for k, s in enumerate(order):
+            assert np.array_equal(a[k].numpy(), ads[s].indices[name]["A"].astype(np.int32))
+            assert np.array_equal(b[k].numpy(), ads[s].indices[name]["B"].astype(np.int32))
