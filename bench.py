@@ -13,9 +13,11 @@ Metric: tokens/s = (4 linears x B x M tokens x N ranks) / max-over-ranks step ti
 is weak scaling: every rank runs its own B=14 batch against its own replica of the bank; the
 only collectives are the timing barrier and the max over ranks.
 
-``--impl reference`` times the reference's CPU path (the oracle's restatement of
-lithe/serve.py MultiAdapterLinear in torch CPU ops, all host threads) on a bounded sample of
-the same workload and prints the same JSON line with "impl": "reference".
+``--impl reference`` times the reference's CPU path (the unmodified reference's
+lithe/serve.py MultiAdapterLinear from its install in baseline/_ref, else the oracle's
+restatement of it, torch CPU ops, all host threads) on a bounded sample of the same workload
+and prints the same JSON line with "impl": "reference".  At N=1 the default line also times the
+reference's Triton kernels on the same GPU and inputs (``reference_gpu``).
 """
 from __future__ import annotations
 
@@ -212,17 +214,37 @@ def traffic_per_launch():
 
 
 # --------------------------------------------------------------------------------------- CPU arm
+class _GivenOutput(torch.nn.Module):
+    """Stands in for the base linear of a wrapped layer: returns the base output it was given,
+    so the timed forward is the LoRA path alone (as the GPU arm, which adds into a given base
+    output)."""
+
+    def __init__(self, out: torch.Tensor, d_in: int):
+        super().__init__()
+        self.in_features, self.out_features = d_in, out.shape[-1]
+        self.weight = torch.nn.Parameter(torch.empty(0), requires_grad=False)
+        self.out = out
+
+    def forward(self, x):
+        return self.out
+
+
 def cpu_reference_passes(n_passes: int, warmup: int = 2, seed: int = 0) -> dict:
-    """The reference's CPU path on the host cores: the oracle port of serve.py's routed forward
-    (decode of the sample's adapter in fp32, bmm, bmm, out + delta) over one full sample of the
-    workload -- 1 sample x 4608 tokens, fp32 -- of each of the four shapes per pass.  Every pass
-    is timed on its own; the rate is tokens / median pass time, with the fastest and slowest
-    pass as the spread.  Both bench arms call this with the same pass counts, so the reference
-    arm's value and the GPU arm's cpu_baseline measure the same thing."""
-    from oracle import codebook_ref, sgmv_ref
+    """The reference's CPU path on the host cores: serve.py's routed forward (decode of the
+    sample's adapter in fp32, bmm, bmm, out + delta, lithe/serve.py:75-97) over one full sample
+    of the workload -- 1 sample x 4608 tokens, fp32 -- of each of the four shapes per pass.  It
+    runs the unmodified reference's ``MultiAdapterLinear`` from its install in baseline/_ref
+    (kind "reference"), its base linear replaced by the given base output; where that install
+    is absent, the oracle's restatement of the same forward (kind "port").  Every pass is timed
+    on its own; the rate is tokens / median pass time, with the fastest and slowest pass as the
+    spread.  Both bench arms call this with the same pass counts, so the reference arm's value
+    and the GPU arm's cpu_baseline measure the same thing."""
     threads = os.cpu_count() or 1
     torch.set_num_threads(threads)
-    pa, pb = codebook_ref.twin_pools()
+    try:
+        ref = reference_package(require_triton=False)
+    except ImportError:
+        ref = None
     rng = np.random.default_rng(seed)
     cases = []
     gen = torch.Generator().manual_seed(seed)
@@ -232,27 +254,46 @@ def cpu_reference_passes(n_passes: int, warmup: int = 2, seed: int = 0) -> dict:
         x = torch.randn(1, CPU_SAMPLE_TOKENS, d_in, generator=gen)
         base = torch.randn(1, CPU_SAMPLE_TOKENS, d_out, generator=gen)
         cases.append((x, base, bank_a, bank_b, d_out))
-    ids, w = sgmv_ref.routes_to_tables([[(0, 1.0)]])
-
-    def one_pass():
+    if ref is not None:
+        kind, path = "reference", "lithe.serve.MultiAdapterLinear (unmodified, baseline/_ref)"
+        pool_a, pool_b = ref.codebook.twin_pools()
+        router = ref.serve.Router()
+        router.set([[(0, 1.0)]])
+        layers = []
         for x, base, ba, bb, d_out in cases:
-            sgmv_ref.serve_forward(base, x, ba, bb, [1.0], ids, w, RANK, d_out, pa, pb)
+            lyr = ref.serve.MultiAdapterLinear(_GivenOutput(base, x.shape[-1]), router, RANK, pool_a, pool_b)
+            lyr.add_adapter(ba[0], bb[0], 1.0)
+            layers.append((lyr, x))
 
-    for _ in range(max(1, warmup)):
-        one_pass()
-    times = []
-    for _ in range(max(1, n_passes)):
-        t0 = time.perf_counter()
-        one_pass()
-        times.append(time.perf_counter() - t0)
+        def one_pass():
+            for lyr, x in layers:
+                lyr(x)
+    else:
+        from oracle import codebook_ref, sgmv_ref
+        kind, path = "port", "oracle port of lithe/serve.py MultiAdapterLinear forward"
+        pa, pb = codebook_ref.twin_pools()
+        ids, w = sgmv_ref.routes_to_tables([[(0, 1.0)]])
+
+        def one_pass():
+            for x, base, ba, bb, d_out in cases:
+                sgmv_ref.serve_forward(base, x, ba, bb, [1.0], ids, w, RANK, d_out, pa, pb)
+
+    with torch.no_grad():
+        for _ in range(max(1, warmup)):
+            one_pass()
+        times = []
+        for _ in range(max(1, n_passes)):
+            t0 = time.perf_counter()
+            one_pass()
+            times.append(time.perf_counter() - t0)
     tokens = len(SHAPES) * CPU_SAMPLE_TOKENS
     med = statistics.median(times)
-    return {"value": tokens / med, "unit": "tokens/s", "cores": threads, "kind": "port",
+    return {"value": tokens / med, "unit": "tokens/s", "cores": threads, "kind": kind,
             "spread": {"min": tokens / max(times), "median": tokens / med, "max": tokens / min(times)},
             "passes": len(times), "pass_ms_median": 1000.0 * med,
-            "sample": f"oracle port of lithe/serve.py MultiAdapterLinear forward, fp32, {threads} host threads: "
-                      f"1 sample x {CPU_SAMPLE_TOKENS} tokens of each of the 4 shapes per pass, {len(times)} passes "
-                      f"timed one by one after {max(1, warmup)} warm-up passes, rate = tokens / median pass"}
+            "sample": f"{path}, fp32, {threads} host threads: 1 sample x {CPU_SAMPLE_TOKENS} tokens of each of the "
+                      f"4 shapes per pass (base output given), {len(times)} passes timed one by one after "
+                      f"{max(1, warmup)} warm-up passes, rate = tokens / median pass"}
 
 
 def run_reference(args):
@@ -267,7 +308,7 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded uniform 9-bit indices, x ~ N(0,1)",
         "config": {"workload": "flux_sweep_b14", "shapes": SHAPES, "batch": BATCH, "tokens_per_sample": TOKENS,
-                   "rank": RANK, "path": "oracle port of lithe/serve.py MultiAdapterLinear (torch CPU)",
+                   "rank": RANK, "path": cpu["sample"].split(",")[0] + " (torch CPU)",
                    "step": "one pass: 1 sample x 4608 tokens of each of the 4 shapes"},
         "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
@@ -652,16 +693,18 @@ def run_decode(args):
 REF_INSTALL = ROOT / "baseline" / "_ref"
 
 
-def reference_package():
+def reference_package(require_triton: bool = True):
     """The unmodified reference package (``lithe``) from its offline pip install in
-    baseline/_ref, with its Triton kernels usable.  Raises ImportError with the reason when it
-    cannot be used, so that the workload prints an ``unavailable`` line instead."""
+    baseline/_ref (with its Triton kernels usable, unless ``require_triton`` is False).  Raises
+    ImportError with the reason when it cannot be used, so that the caller reports it as
+    unavailable or falls back."""
     if not (REF_INSTALL / "lithe" / "__init__.py").exists():
         raise ImportError("no reference install in baseline/_ref")
     if str(REF_INSTALL) not in sys.path:
         sys.path.insert(0, str(REF_INSTALL))
     import lithe
     import lithe.codebook
+    import lithe.serve
     import lithe.kernels.layers
     import lithe.kernels.packed
     import lithe.kernels.sgmv
@@ -669,7 +712,7 @@ def reference_package():
     from lithe.kernels import _triton
     if Path(lithe.__file__).resolve().parent != (REF_INSTALL / "lithe").resolve():
         raise ImportError(f"'lithe' resolved to {lithe.__file__}, not the install in baseline/_ref")
-    if not _triton.HAS_TRITON:
+    if require_triton and not _triton.HAS_TRITON:
         raise ImportError("triton is not importable, so the reference would run its torch fallback")
     return lithe
 
