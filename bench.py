@@ -288,7 +288,7 @@ def cpu_reference_passes(n_passes: int, warmup: int = 2, seed: int = 0) -> dict:
             times.append(time.perf_counter() - t0)
     tokens = len(SHAPES) * CPU_SAMPLE_TOKENS
     med = statistics.median(times)
-    return {"value": tokens / med, "unit": "tokens/s", "cores": threads, "kind": kind,
+    return {"value": tokens / med, "unit": "tokens/s", "cores": threads, "kind": kind, "path": path,
             "spread": {"min": tokens / max(times), "median": tokens / med, "max": tokens / min(times)},
             "passes": len(times), "pass_ms_median": 1000.0 * med,
             "sample": f"{path}, fp32, {threads} host threads: 1 sample x {CPU_SAMPLE_TOKENS} tokens of each of the "
@@ -308,7 +308,7 @@ def run_reference(args):
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic: seeded uniform 9-bit indices, x ~ N(0,1)",
         "config": {"workload": "flux_sweep_b14", "shapes": SHAPES, "batch": BATCH, "tokens_per_sample": TOKENS,
-                   "rank": RANK, "path": cpu["sample"].split(",")[0] + " (torch CPU)",
+                   "rank": RANK, "path": cpu["path"] + ", torch CPU",
                    "step": "one pass: 1 sample x 4608 tokens of each of the 4 shapes"},
         "cpu_baseline": cpu,
         "e2e": {"value": value, "unit": "tokens/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
