@@ -282,6 +282,28 @@ def test_attach_adapters_checks_on_cpu():
         serve.attach_adapters(model_for(ads[0].modules), [ads[0], other])
 
 
+def test_attach_accepts_different_module_order():
+    """Adapters may list the same modules in different orders (tests/test_serve.py:65-76 of the
+    reference); every layer then holds each adapter's indices of its own module."""
+    from torch import nn
+    mods = [{"name": n, "shape_a": [4, 128], "shape_b": [64, 4]} for n in ("fc", "gc")]
+    rng = np.random.default_rng(1)
+
+    def idx():
+        return {"A": rng.integers(0, 512, (3, 8)).astype(np.uint16), "B": rng.integers(0, 512, (3, 4)).astype(np.uint16)}
+
+    a = fileio.LitheAdapter(modules=mods, indices={"fc": idx(), "gc": idx()}, rank=4, alpha=8.0)
+    b = fileio.LitheAdapter(modules=mods[::-1], indices={"fc": idx(), "gc": idx()}, rank=4, alpha=8.0)
+    model = nn.Module()
+    model.fc, model.gc = nn.Linear(128, 64), nn.Linear(128, 64)
+    _, layers = serve.attach_adapters(model, [a, b])
+    assert set(layers) == {"fc", "gc"}
+    for name, layer in layers.items():
+        for row, ad in enumerate((a, b)):
+            assert np.array_equal(layer.idx_a[row].numpy(), ad.indices[name]["A"].astype(np.int16))
+            assert np.array_equal(layer.idx_b[row].numpy(), ad.indices[name]["B"].astype(np.int16))
+
+
 def test_flux_rope_tables():
     """The FLUX-shaped model's rotary embedding: text tokens unrotated, rotations keep norms,
     the fused form equals the pairwise rotation, and a query-key product depends only on the
