@@ -82,6 +82,17 @@ class LitheAdapter:
         return b"".join(chunks)
 
 
+def pack_stream(raw: bytes) -> bytes:
+    """One part of a .lithe file (the JSON header or the index payload) as it is stored:
+    LZMA with preset 9 | EXTREME (lithe/fileio.py:61-62)."""
+    return lzma.compress(raw, preset=LZMA_PRESET)
+
+
+def unpack_stream(blob: bytes) -> bytes:
+    """The bytes ``pack_stream`` stored (lithe/fileio.py:65-66); lzma.LZMAError if corrupt."""
+    return lzma.decompress(blob)
+
+
 def _header(ad: LitheAdapter, raw: bytes) -> Dict[str, Any]:
     return {
         "format": "lithe",
@@ -112,8 +123,8 @@ def save_lithe(path, ad: LitheAdapter) -> int:
     if ad.n_bits > 16:
         raise ValueError("uint16 streams need n_bits <= 16")
     raw = ad.raw_stream()
-    head = lzma.compress(json.dumps(_header(ad, raw), separators=(",", ":")).encode("utf-8"), preset=LZMA_PRESET)
-    body = lzma.compress(raw, preset=LZMA_PRESET)
+    head = pack_stream(json.dumps(_header(ad, raw), separators=(",", ":")).encode("utf-8"))
+    body = pack_stream(raw)
     path = Path(path)
     path.parent.mkdir(parents=True, exist_ok=True)
     path.write_bytes(MAGIC + struct.pack("<I", len(head)) + head + body)
@@ -129,7 +140,7 @@ def _split_file(path):
     if start + n > len(data):
         raise ValueError(f"{path}: truncated header")
     try:
-        header = json.loads(lzma.decompress(data[start:start + n]).decode("utf-8"))
+        header = json.loads(unpack_stream(data[start:start + n]).decode("utf-8"))
     except (lzma.LZMAError, UnicodeDecodeError, json.JSONDecodeError) as e:
         raise ValueError(f"{path}: corrupt header ({e})") from e
     return header, data[start + n:]
@@ -147,7 +158,7 @@ def read_payload(path, verify: bool = True) -> Tuple[Dict[str, Any], bytes]:
     """
     header, body = _split_file(path)
     try:
-        raw = lzma.decompress(body)
+        raw = unpack_stream(body)
     except lzma.LZMAError as e:
         raise ValueError(f"{path}: corrupt index stream ({e})") from e
     cbh = header["codebook"]

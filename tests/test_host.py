@@ -136,6 +136,20 @@ def test_lithe_file_roundtrip_and_corruption(tmp_path):
     assert hdr["num_indices"] == ad.num_indices
 
 
+def test_stream_codec_and_file_body(tmp_path):
+    """pack_stream / unpack_stream round trip, and a saved file's body is pack_stream of the
+    raw payload (tests/test_fileio.py:25-28,45-50 of the reference)."""
+    raw = np.random.default_rng(3).integers(0, 512, 5000).astype("<u2").tobytes()
+    assert fileio.unpack_stream(fileio.pack_stream(raw)) == raw
+    ad = random_adapter(SMALL, rank=8, seed=4)
+    path = tmp_path / "a.lithe"
+    fileio.save_lithe(path, ad)
+    blob = path.read_bytes()
+    n = int.from_bytes(blob[8:12], "little")
+    assert blob[12 + n:] == fileio.pack_stream(ad.raw_stream())
+    assert fileio.read_payload(path)[1] == ad.raw_stream()
+
+
 def test_router_and_parse_route():
     r = serve.Router()
     r.set([[(0, 1.0)], [(2, 1.0)], [], [(1, 0.6), (2, 0.4)]])
