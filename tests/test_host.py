@@ -442,3 +442,29 @@ def test_int32_index_banks_unpack_the_packed_stream():
         for k, s in enumerate(order):
             assert np.array_equal(a[k].numpy(), ads[s].indices[name]["A"].astype(np.int32))
             assert np.array_equal(b[k].numpy(), ads[s].indices[name]["B"].astype(np.int32))
+
+
+def test_reference_install_missing_is_reported_and_cpu_arm_falls_back(tmp_path, monkeypatch):
+    """Without the reference's install the GPU comparators report why (ImportError, printed as
+    an unavailable line) and the CPU arm times the oracle port instead (kind "port")."""
+    import bench
+    monkeypatch.setattr(bench, "REF_INSTALL", tmp_path / "absent")
+    monkeypatch.setattr(bench, "SHAPES", [(128, 192)])
+    monkeypatch.setattr(bench, "CPU_SAMPLE_TOKENS", 64)
+    with pytest.raises(ImportError, match="baseline/_ref"):
+        bench.reference_package()
+    rec = bench.cpu_reference_passes(2, warmup=1)
+    assert rec["kind"] == "port" and rec["passes"] == 2 and rec["value"] > 0
+    assert rec["spread"]["min"] <= rec["spread"]["median"] <= rec["spread"]["max"]
+
+
+def test_cpu_arm_runs_the_reference_when_installed(monkeypatch):
+    import bench
+    try:
+        bench.reference_package(require_triton=False)
+    except ImportError as e:
+        pytest.skip(f"reference install absent: {e}")
+    monkeypatch.setattr(bench, "SHAPES", [(128, 192)])
+    monkeypatch.setattr(bench, "CPU_SAMPLE_TOKENS", 64)
+    rec = bench.cpu_reference_passes(2, warmup=1)
+    assert rec["kind"] == "reference" and "MultiAdapterLinear" in rec["path"]
