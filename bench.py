@@ -213,6 +213,34 @@ def traffic_per_launch():
     return rec.get("dram_bytes_per_launch"), note
 
 
+# --------------------------------------------------------------------------------------- the reference install
+REF_INSTALL = ROOT / "baseline" / "_ref"
+
+
+def reference_package(require_triton: bool = True):
+    """The unmodified reference package (``lithe``) from its offline pip install in
+    baseline/_ref (with its Triton kernels usable, unless ``require_triton`` is False).  Raises
+    ImportError with the reason when it cannot be used, so that the caller reports it as
+    unavailable or falls back."""
+    if not (REF_INSTALL / "lithe" / "__init__.py").exists():
+        raise ImportError("no reference install in baseline/_ref")
+    if str(REF_INSTALL) not in sys.path:
+        sys.path.insert(0, str(REF_INSTALL))
+    import lithe
+    import lithe.codebook
+    import lithe.serve
+    import lithe.kernels.layers
+    import lithe.kernels.packed
+    import lithe.kernels.sgmv
+    import lithe.kernels.shared
+    from lithe.kernels import _triton
+    if Path(lithe.__file__).resolve().parent != (REF_INSTALL / "lithe").resolve():
+        raise ImportError(f"'lithe' resolved to {lithe.__file__}, not the install in baseline/_ref")
+    if require_triton and not _triton.HAS_TRITON:
+        raise ImportError("triton is not importable, so the reference would run its torch fallback")
+    return lithe
+
+
 # --------------------------------------------------------------------------------------- CPU arm
 class _GivenOutput(torch.nn.Module):
     """Stands in for the base linear of a wrapped layer: returns the base output it was given,
@@ -690,33 +718,6 @@ def run_decode(args):
 
 
 # --------------------------------------------------------------------------------------- the reference's GPU kernels
-REF_INSTALL = ROOT / "baseline" / "_ref"
-
-
-def reference_package(require_triton: bool = True):
-    """The unmodified reference package (``lithe``) from its offline pip install in
-    baseline/_ref (with its Triton kernels usable, unless ``require_triton`` is False).  Raises
-    ImportError with the reason when it cannot be used, so that the caller reports it as
-    unavailable or falls back."""
-    if not (REF_INSTALL / "lithe" / "__init__.py").exists():
-        raise ImportError("no reference install in baseline/_ref")
-    if str(REF_INSTALL) not in sys.path:
-        sys.path.insert(0, str(REF_INSTALL))
-    import lithe
-    import lithe.codebook
-    import lithe.serve
-    import lithe.kernels.layers
-    import lithe.kernels.packed
-    import lithe.kernels.sgmv
-    import lithe.kernels.shared
-    from lithe.kernels import _triton
-    if Path(lithe.__file__).resolve().parent != (REF_INSTALL / "lithe").resolve():
-        raise ImportError(f"'lithe' resolved to {lithe.__file__}, not the install in baseline/_ref")
-    if require_triton and not _triton.HAS_TRITON:
-        raise ImportError("triton is not importable, so the reference would run its torch fallback")
-    return lithe
-
-
 def _event_ms(fn, steps: int, warmup: int, stream) -> float:
     """Mean CUDA-event time of ``fn`` over ``steps`` calls after ``warmup`` untimed ones."""
     for _ in range(warmup):
